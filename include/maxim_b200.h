@@ -1,0 +1,240 @@
+/*
+ * maxim_b200.h - the C ABI of the B200-native MAXIM forward pass.
+ *
+ * Two groups of entry points live here:
+ *
+ *   1. The GPU executor (mx_driver_ready, mx_gpu_*). This is the drop-in
+ *      boundary: it replaces the reference's `exec_gpu::Gpu`
+ *      (src/exec_gpu.rs:48-357) and the device glue under it (src/cuda.rs).
+ *      A caller hands it a plan as a flat POD op table (mx_plan) plus host
+ *      weight blobs in the plan's own layouts, and gets the same methods the
+ *      Rust type has: new / run / begin / step_op / read_buf / read_into /
+ *      read_arena / timeline / stats. Nothing here takes or returns a torch or
+ *      CUDA type; device memory is owned by the handle.
+ *
+ *   2. The host contract (mx_weights_*, mx_plan_*, mx_image_*, mx_param_spec),
+ *      a C++ restatement of the reference's Rust host: safetensors weights with
+ *      the checkpoint-derived config (src/weights.rs, src/config.rs), the plan
+ *      builder and live-range arena packer (src/model.rs), and the PNG / pad /
+ *      crop pipeline (src/image.rs). A caller that already has a Plan (the Rust
+ *      crate itself) only needs group 1.
+ *
+ * Conventions (src/lib.rs:29-56 is the reference's error type):
+ *   - every function returns an int status: MX_OK (0) or a negative MX_E_*;
+ *   - on failure the thread-local message is available from mx_last_error();
+ *   - sizes are in elements of float (fp32) unless the name says bytes;
+ *   - buffer ids, op indices and weight ids are the plan's own indices.
+ */
+#ifndef MAXIM_B200_H
+#define MAXIM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status codes */
+enum {
+  MX_OK = 0,
+  MX_E_INVALID = -1,    /* bad argument, bad shape, unsupported plan */
+  MX_E_IO = -2,         /* file / PNG / safetensors problem */
+  MX_E_NO_DEVICE = -3,  /* the CUDA driver or device is unavailable */
+  MX_E_OOM = -4,        /* the pass does not fit in device memory */
+  MX_E_CUDA = -5,       /* a CUDA call failed */
+  MX_E_DEVICE = -6,     /* a kernel reported an error through its status word */
+};
+
+/* Copy the calling thread's last error message into buf (always NUL
+ * terminated). Returns the full message length. */
+size_t mx_last_error(char* buf, size_t len);
+
+/* ----------------------------------------------------------- the plan (POD)
+ * The op kinds of `model::Op` (src/model.rs:66-112), in the enum's order. */
+enum {
+  MX_OP_COPY = 0,
+  MX_OP_ADD = 1,
+  MX_OP_MUL = 2,
+  MX_OP_GATE_APPLY = 3,
+  MX_OP_GELU = 4,
+  MX_OP_LRELU = 5,
+  MX_OP_SIGMOID = 6,
+  MX_OP_CHAN_LN = 7,
+  MX_OP_CHAN_MEAN = 8,
+  MX_OP_CHAN_SCALE = 9,
+  MX_OP_CONV1X1 = 10,
+  MX_OP_CONV3X3 = 11,
+  MX_OP_CONV4X4S2 = 12,
+  MX_OP_CONVT2X2 = 13,
+  MX_OP_GATE_MM = 14,
+  MX_OP_BLOCK_PERM = 15,
+  MX_OP_RESIZE = 16,
+  MX_OP_DOWN_S = 17,
+  MX_OP_KINDS = 18
+};
+
+/* One op. Unused fields are -1 (ids) or 0 (sizes). Field meaning per kind
+ * follows `model::Op` (src/model.rs:66-112):
+ *   Copy/Add/Mul/GateApply/Gelu/Lrelu/Sigmoid: dst, src (a / u), src2 (b / v), n, slope
+ *   ChanLn: dst, src, scale, bias, c, hw
+ *   ChanMean: dst, src, c, hw          ChanScale: dst, src, src2 (= s), c, hw
+ *   Conv1x1/Conv3x3: dst, src, w, wt, bias, c_in, c_out, h, wd
+ *   Conv4x4s2: ... + pad_top, pad_left, oh, ow     ConvT2x2: dst, src, w, bias, c_in, c_out, h, wd
+ *   GateMm: dst, src, w, bias, c, outer, inner, mode
+ *   BlockPerm: dst, src, c, h, wd, gh, gw, fh, fw, swap, forward
+ *   Resize: dst, src, tmp, c, hin, win, hout, wout
+ *   DownS: dst, src, c, h, wd, stride, off, oh, ow                                  */
+typedef struct mx_op {
+  int32_t kind;
+  int32_t dst, src, src2, tmp;
+  int32_t w, wt, bias, scale;
+  int64_t n;
+  int32_t c, c_in, c_out, h, wd, oh, ow, pad_top, pad_left;
+  int32_t outer, inner, mode;
+  int32_t gh, gw, fh, fw, swap, forward;
+  int32_t stride, off;
+  int32_t hin, win, hout, wout;
+  int64_t hw;
+  float slope;
+} mx_op;
+
+/* A buffer's [c][h][w] shape (`model::BufShape`, src/model.rs:37-62). */
+typedef struct mx_buf {
+  int64_t c, h, w;
+} mx_buf;
+
+/* The plan as a read-only POD view (`model::Plan`, src/model.rs:1237-1272).
+ * `offs` are element offsets into the arena, views already resolved;
+ * `alias_parent[i]` is -1 for a buffer that owns its storage, else the buffer
+ * it is a channel range of, at element delta `alias_delta[i]`. */
+typedef struct mx_plan {
+  int32_t n_bufs;
+  const mx_buf* bufs;
+  const int64_t* offs;
+  const int32_t* alias_parent;
+  const int64_t* alias_delta;
+  int32_t n_ops;
+  const mx_op* ops;
+  int32_t n_weights;
+  const float* const* weights; /* host blobs in the plan's layouts */
+  const int64_t* weight_lens;
+  int64_t arena_len;
+  int32_t input, output;
+  mx_buf shape; /* the padded input shape the plan was built for */
+} mx_plan;
+
+/* ================================================== 1. the GPU executor ==== */
+
+typedef struct mx_gpu mx_gpu;
+
+/* `exec_gpu::driver_ready` (src/exec_gpu.rs:81-83): bring the driver up. */
+int mx_driver_ready(void);
+/* Number of visible CUDA devices (0 when the driver is unavailable). */
+int mx_device_count(int* count);
+
+/* `Gpu::new` (src/exec_gpu.rs:96-157): size the pass, refuse it with the
+ * numbers if arena + weights exceed free device memory, then make ONE arena
+ * allocation and upload every weight in the kernels' layouts (resident, not
+ * lazy). The plan is copied; the caller may free its view afterwards. */
+int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out);
+void mx_gpu_free(mx_gpu* g);
+
+/* `Gpu::run` (src/exec_gpu.rs:196-229): input [3][H][W] host floats in,
+ * output [3][H][W] host floats out (the plan's output buffer), synchronous. */
+int mx_gpu_run(mx_gpu* g, const float* input, float* output);
+
+/* The same pass split into its parts, for callers that keep the input and
+ * output on the device or overlap copies with other work: upload the input,
+ * enqueue the whole op stream (one CUDA graph launch), download the output.
+ * All three are asynchronous on the handle's stream; mx_gpu_sync waits. */
+int mx_gpu_upload_input(mx_gpu* g, const float* input);
+int mx_gpu_enqueue(mx_gpu* g);
+int mx_gpu_download_output(mx_gpu* g, float* output);
+int mx_gpu_sync(mx_gpu* g);
+
+/* `Gpu::begin` / `step_op` / `read_buf` / `read_into` / `read_arena`
+ * (src/exec_gpu.rs:329-357): the op-by-op walk behind `--verify-gpu`.
+ * read_buf returns buffer `id` in the plan's [c][h][w] layout (converted from
+ * the executor's internal layout). step_op runs op `i` alone, unfused. */
+int mx_gpu_begin(mx_gpu* g, const float* input);
+int mx_gpu_step_op(mx_gpu* g, int32_t i);
+int mx_gpu_read_buf(mx_gpu* g, int32_t id, float* out, int64_t len);
+int mx_gpu_read_arena(mx_gpu* g, float* out, int64_t len);
+
+/* `Gpu::set_timeline` / `timeline` (src/exec_gpu.rs:180-265): with the
+ * timeline on, mx_gpu_run records an event around every launch group and
+ * per_op_ms[i] receives op i's device time (0 for ops fused into another). */
+int mx_gpu_set_timeline(mx_gpu* g, int on);
+int mx_gpu_timeline(mx_gpu* g, float* per_op_ms, int32_t n_ops, float* total_ms);
+
+/* `device_name` / `arena_bytes` / `weight_bytes` / `pool_bytes` /
+ * `ops_launched` (src/exec_gpu.rs:160-190). `kernels` is the number of kernel
+ * launches one pass enqueues. */
+typedef struct mx_gpu_stats {
+  char device_name[128];
+  int64_t arena_bytes;
+  int64_t weight_bytes;
+  int64_t pool_bytes;
+  int64_t ops;
+  int64_t kernels;
+} mx_gpu_stats;
+int mx_gpu_get_stats(mx_gpu* g, mx_gpu_stats* s);
+
+/* ================================================= 2. the host contract ==== */
+
+typedef struct mx_weights mx_weights;
+typedef struct mx_plan_handle mx_plan_handle;
+
+/* `Weights::open` + `Config::of_checkpoint` (src/weights.rs:37-41,
+ * src/config.rs:71-100): the variant is derived from the file. */
+int mx_weights_open(const char* path, mx_weights** out);
+void mx_weights_free(mx_weights* w);
+/* The variant name ("S-3", ...) the checkpoint was derived as. */
+int mx_weights_variant(const mx_weights* w, char* buf, size_t len);
+
+/* The parameter inventory a checkpoint of `variant` must hold, in the
+ * builder's request order: one "name\tshape\n" line per tensor, shape as
+ * comma-separated dims. `*needed` receives the full byte length. */
+int mx_param_spec(const char* variant, char* buf, size_t len, size_t* needed);
+
+/* `Builder::new(..)[.without_dumps()].build(h, w)` (src/model.rs:743-891):
+ * h and w are the PADDED dimensions. With dumps != 0 the named activations
+ * (`Plan::dumps`) are kept live to the end of the run, as `--dump` needs. */
+int mx_plan_build(const mx_weights* w, int32_t h, int32_t wd, int dumps, mx_plan_handle** out);
+/* The same plan for a named variant with no checkpoint: every weight blob is
+ * empty. For shape, op-count and arena queries (the reference's arena and
+ * packing tests need a checkpoint only for its shapes). */
+int mx_plan_build_variant(const char* variant, int32_t h, int32_t wd, int dumps, mx_plan_handle** out);
+void mx_plan_free(mx_plan_handle* p);
+const mx_plan* mx_plan_view(const mx_plan_handle* p);
+/* Named activations: count, and the i-th name / buffer id. */
+int32_t mx_plan_dump_count(const mx_plan_handle* p);
+int mx_plan_dump(const mx_plan_handle* p, int32_t i, char* name, size_t len, int32_t* id);
+/* A buffer's human-readable label (`Plan::labels`). */
+int mx_plan_label(const mx_plan_handle* p, int32_t id, char* buf, size_t len);
+
+/* An image, [c][h][w] floats in 0..1 (`image::Image`, src/image.rs:9-30).
+ * Memory is owned by the library; free with mx_image_free. */
+typedef struct mx_image {
+  int32_t c, h, w;
+  float* data;
+} mx_image;
+void mx_image_free(mx_image* img);
+/* `image::read_png` / `write_png` (src/image.rs:33-104): 8-bit PNG, gray /
+ * gray+alpha / RGB / RGBA read as RGB; written RGB with round-half-up. */
+int mx_png_read(const char* path, mx_image* out);
+int mx_png_read_mem(const uint8_t* bytes, size_t n, mx_image* out);
+int mx_png_write(const char* path, const mx_image* img);
+/* `image::preprocess(img, factor)` (src/image.rs:171-207): even reflect, then
+ * centred reflect to a multiple of `factor`; returns the even shape too.
+ * Refuses an image too small to reflect, with the reference's reasoning. */
+int mx_preprocess(const mx_image* img, int32_t factor, mx_image* padded, int32_t* even_h, int32_t* even_w);
+/* `image::crop_out` (src/image.rs:233-246). */
+int mx_crop_out(const mx_image* pred, int32_t orig_h, int32_t orig_w, int32_t even_h, int32_t even_w,
+                mx_image* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MAXIM_B200_H */

@@ -1,0 +1,376 @@
+"""ctypes binding of libmaxim_b200.so (declared in include/maxim_b200.h).
+
+The library is the product: the GPU executor behind the reference's
+`exec_gpu::Gpu` interface (src/exec_gpu.rs:48-357) and the C++ restatement of
+the reference's host contract (weights, config, plan builder, image pipeline).
+This module only marshals arguments; it performs no computation of its own.
+Loading fails loudly when the library has not been built.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmaxim_b200.so")
+
+MX_OK = 0
+OP_NAMES = ["copy", "add", "mul", "gate_apply", "gelu", "lrelu", "sigmoid", "chan_ln", "chan_mean", "chan_scale",
+            "conv1x1", "conv3x3", "conv4x4s2", "convt2x2", "gate_mm", "block_perm", "resize", "down_s"]
+
+
+class mx_op(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("dst", ctypes.c_int32), ("src", ctypes.c_int32),
+                ("src2", ctypes.c_int32), ("tmp", ctypes.c_int32), ("w", ctypes.c_int32), ("wt", ctypes.c_int32),
+                ("bias", ctypes.c_int32), ("scale", ctypes.c_int32), ("n", ctypes.c_int64),
+                ("c", ctypes.c_int32), ("c_in", ctypes.c_int32), ("c_out", ctypes.c_int32), ("h", ctypes.c_int32),
+                ("wd", ctypes.c_int32), ("oh", ctypes.c_int32), ("ow", ctypes.c_int32),
+                ("pad_top", ctypes.c_int32), ("pad_left", ctypes.c_int32), ("outer", ctypes.c_int32),
+                ("inner", ctypes.c_int32), ("mode", ctypes.c_int32), ("gh", ctypes.c_int32), ("gw", ctypes.c_int32),
+                ("fh", ctypes.c_int32), ("fw", ctypes.c_int32), ("swap", ctypes.c_int32),
+                ("forward", ctypes.c_int32), ("stride", ctypes.c_int32), ("off", ctypes.c_int32),
+                ("hin", ctypes.c_int32), ("win", ctypes.c_int32), ("hout", ctypes.c_int32),
+                ("wout", ctypes.c_int32), ("hw", ctypes.c_int64), ("slope", ctypes.c_float)]
+
+
+class mx_buf(ctypes.Structure):
+    _fields_ = [("c", ctypes.c_int64), ("h", ctypes.c_int64), ("w", ctypes.c_int64)]
+
+
+class mx_plan(ctypes.Structure):
+    _fields_ = [("n_bufs", ctypes.c_int32), ("bufs", ctypes.POINTER(mx_buf)), ("offs", ctypes.POINTER(ctypes.c_int64)),
+                ("alias_parent", ctypes.POINTER(ctypes.c_int32)), ("alias_delta", ctypes.POINTER(ctypes.c_int64)),
+                ("n_ops", ctypes.c_int32), ("ops", ctypes.POINTER(mx_op)), ("n_weights", ctypes.c_int32),
+                ("weights", ctypes.POINTER(ctypes.POINTER(ctypes.c_float))),
+                ("weight_lens", ctypes.POINTER(ctypes.c_int64)), ("arena_len", ctypes.c_int64),
+                ("input", ctypes.c_int32), ("output", ctypes.c_int32), ("shape", mx_buf)]
+
+
+class mx_gpu_stats(ctypes.Structure):
+    _fields_ = [("device_name", ctypes.c_char * 128), ("arena_bytes", ctypes.c_int64),
+                ("weight_bytes", ctypes.c_int64), ("pool_bytes", ctypes.c_int64), ("ops", ctypes.c_int64),
+                ("kernels", ctypes.c_int64)]
+
+
+class mx_image(ctypes.Structure):
+    _fields_ = [("c", ctypes.c_int32), ("h", ctypes.c_int32), ("w", ctypes.c_int32),
+                ("data", ctypes.POINTER(ctypes.c_float))]
+
+
+class MaximError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(msg)
+        self.code = code
+
+
+_lib = None
+
+_SIGS = {
+    "mx_last_error": (ctypes.c_size_t, [ctypes.c_char_p, ctypes.c_size_t]),
+    "mx_driver_ready": (ctypes.c_int, []),
+    "mx_device_count": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "mx_gpu_new": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(mx_plan), ctypes.POINTER(ctypes.c_void_p)]),
+    "mx_gpu_free": (None, [ctypes.c_void_p]),
+    "mx_gpu_run": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "mx_gpu_upload_input": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "mx_gpu_enqueue": (ctypes.c_int, [ctypes.c_void_p]),
+    "mx_gpu_download_output": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "mx_gpu_sync": (ctypes.c_int, [ctypes.c_void_p]),
+    "mx_gpu_begin": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "mx_gpu_step_op": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32]),
+    "mx_gpu_read_buf": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64]),
+    "mx_gpu_read_arena": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64]),
+    "mx_gpu_set_timeline": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "mx_gpu_timeline": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                       ctypes.POINTER(ctypes.c_float)]),
+    "mx_gpu_get_stats": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(mx_gpu_stats)]),
+    "mx_weights_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "mx_weights_free": (None, [ctypes.c_void_p]),
+    "mx_weights_variant": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]),
+    "mx_param_spec": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t,
+                                     ctypes.POINTER(ctypes.c_size_t)]),
+    "mx_plan_build": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int,
+                                     ctypes.POINTER(ctypes.c_void_p)]),
+    "mx_plan_build_variant": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int,
+                                             ctypes.POINTER(ctypes.c_void_p)]),
+    "mx_plan_free": (None, [ctypes.c_void_p]),
+    "mx_plan_view": (ctypes.POINTER(mx_plan), [ctypes.c_void_p]),
+    "mx_plan_dump_count": (ctypes.c_int32, [ctypes.c_void_p]),
+    "mx_plan_dump": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_char_p, ctypes.c_size_t,
+                                    ctypes.POINTER(ctypes.c_int32)]),
+    "mx_plan_label": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_char_p, ctypes.c_size_t]),
+    "mx_image_free": (None, [ctypes.POINTER(mx_image)]),
+    "mx_png_read": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(mx_image)]),
+    "mx_png_read_mem": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(mx_image)]),
+    "mx_png_write": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(mx_image)]),
+    "mx_preprocess": (ctypes.c_int, [ctypes.POINTER(mx_image), ctypes.c_int32, ctypes.POINTER(mx_image),
+                                     ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]),
+    "mx_crop_out": (ctypes.c_int, [ctypes.POINTER(mx_image), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                   ctypes.c_int32, ctypes.POINTER(mx_image)]),
+}
+
+
+def lib():
+    """The loaded library. Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError("%s is missing: run `python maxim-rs_b200/build.py` (or __graft_entry__.build())"
+                               % LIB_PATH)
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def exported_symbols():
+    """The ABI's entry point names (what include/maxim_b200.h declares)."""
+    return sorted(_SIGS)
+
+
+def last_error():
+    buf = ctypes.create_string_buffer(4096)
+    lib().mx_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(rc, what=""):
+    if rc != MX_OK:
+        raise MaximError(rc, (what + ": " if what else "") + last_error())
+
+
+def _ptr(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+class Weights:
+    """`Weights::open` (src/weights.rs:37-41): a converted checkpoint, variant derived from the file."""
+
+    def __init__(self, path):
+        self._h = ctypes.c_void_p()
+        check(lib().mx_weights_open(os.fsencode(path), ctypes.byref(self._h)), path)
+        buf = ctypes.create_string_buffer(16)
+        check(lib().mx_weights_variant(self._h, buf, 16))
+        self.variant = buf.value.decode()
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().mx_weights_free(self._h)
+            self._h = None
+
+
+def param_spec(variant):
+    """[(name, shape)] a checkpoint of `variant` holds, in the builder's request order."""
+    need = ctypes.c_size_t()
+    check(lib().mx_param_spec(variant.encode(), None, 0, ctypes.byref(need)))
+    buf = ctypes.create_string_buffer(need.value)
+    check(lib().mx_param_spec(variant.encode(), buf, need.value, None))
+    out = []
+    for line in buf.value.decode().splitlines():
+        name, shape = line.split("\t")
+        out.append((name, tuple(int(x) for x in shape.split(","))))
+    return out
+
+
+class Plan:
+    """`model::Plan` (src/model.rs:1237-1272) for one padded input shape."""
+
+    def __init__(self, weights=None, h=0, w=0, dumps=False, variant=None):
+        self._h = ctypes.c_void_p()
+        self._weights = weights
+        if weights is not None:
+            check(lib().mx_plan_build(weights._h, h, w, int(dumps), ctypes.byref(self._h)), "plan")
+        else:
+            check(lib().mx_plan_build_variant(variant.encode(), h, w, int(dumps), ctypes.byref(self._h)), "plan")
+        self.view = lib().mx_plan_view(self._h)
+        v = self.view.contents
+        self.n_ops, self.n_bufs, self.n_weights = v.n_ops, v.n_bufs, v.n_weights
+        self.arena_len, self.input, self.output = v.arena_len, v.input, v.output
+        self.shape = (v.shape.c, v.shape.h, v.shape.w)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().mx_plan_free(self._h)
+            self._h = None
+
+    @property
+    def arena_bytes(self):
+        return self.arena_len * 4
+
+    def buf(self, i):
+        b = self.view.contents.bufs[i]
+        return (b.c, b.h, b.w)
+
+    def off(self, i):
+        return self.view.contents.offs[i]
+
+    def alias(self, i):
+        v = self.view.contents
+        p = v.alias_parent[i]
+        return None if p < 0 else (p, v.alias_delta[i])
+
+    def op(self, i):
+        return self.view.contents.ops[i]
+
+    def ops(self):
+        v = self.view.contents
+        return [v.ops[i] for i in range(v.n_ops)]
+
+    def label(self, i):
+        buf = ctypes.create_string_buffer(128)
+        check(lib().mx_plan_label(self._h, i, buf, 128))
+        return buf.value.decode()
+
+    def dumps(self):
+        out = []
+        for i in range(lib().mx_plan_dump_count(self._h)):
+            buf = ctypes.create_string_buffer(256)
+            bid = ctypes.c_int32()
+            check(lib().mx_plan_dump(self._h, i, buf, 256, ctypes.byref(bid)))
+            out.append((buf.value.decode(), bid.value))
+        return out
+
+    def weight_bytes(self):
+        v = self.view.contents
+        return sum(v.weight_lens[i] for i in range(v.n_weights)) * 4
+
+    def weight(self, i):
+        v = self.view.contents
+        n = v.weight_lens[i]
+        return np.ctypeslib.as_array(v.weights[i], shape=(n,)).copy() if n else np.zeros(0, np.float32)
+
+
+def driver_ready():
+    """`exec_gpu::driver_ready` (src/exec_gpu.rs:81-83)."""
+    check(lib().mx_driver_ready(), "cuda")
+
+
+def device_count():
+    n = ctypes.c_int()
+    rc = lib().mx_device_count(ctypes.byref(n))
+    return n.value if rc == MX_OK else 0
+
+
+class Gpu:
+    """`exec_gpu::Gpu` (src/exec_gpu.rs:48-357) on one device, over the C ABI."""
+
+    def __init__(self, plan, device=0):
+        self.plan = plan
+        self._h = ctypes.c_void_p()
+        check(lib().mx_gpu_new(device, plan.view, ctypes.byref(self._h)), "gpu")
+        c, h, w = plan.buf(plan.input)
+        self.in_len = c * h * w
+        c, h, w = plan.buf(plan.output)
+        self.out_shape = (c, h, w)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().mx_gpu_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def run(self, image, out=None):
+        x = np.ascontiguousarray(image, dtype=np.float32).reshape(-1)
+        if x.size != self.in_len:
+            raise ValueError("input has %d values, the plan's input buffer %d" % (x.size, self.in_len))
+        if out is None:
+            out = np.empty(self.out_shape, np.float32)
+        check(lib().mx_gpu_run(self._h, _ptr(x), _ptr(out)), "run")
+        return out
+
+    def upload_input(self, image):
+        x = np.ascontiguousarray(image, dtype=np.float32).reshape(-1)
+        check(lib().mx_gpu_upload_input(self._h, _ptr(x)), "upload")
+
+    def enqueue(self):
+        check(lib().mx_gpu_enqueue(self._h), "enqueue")
+
+    def download_output(self, out):
+        check(lib().mx_gpu_download_output(self._h, _ptr(out)), "download")
+
+    def sync(self):
+        check(lib().mx_gpu_sync(self._h), "sync")
+
+    def begin(self, image):
+        x = np.ascontiguousarray(image, dtype=np.float32).reshape(-1)
+        check(lib().mx_gpu_begin(self._h, _ptr(x)), "begin")
+
+    def step_op(self, i):
+        check(lib().mx_gpu_step_op(self._h, i), "step_op %d" % i)
+
+    def read_buf(self, i):
+        c, h, w = self.plan.buf(i)
+        out = np.empty((c, h, w), np.float32)
+        check(lib().mx_gpu_read_buf(self._h, i, _ptr(out), out.size), "read_buf")
+        return out
+
+    def read_arena(self):
+        out = np.empty(self.plan.arena_len, np.float32)
+        check(lib().mx_gpu_read_arena(self._h, _ptr(out), out.size), "read_arena")
+        return out
+
+    def set_timeline(self, on):
+        check(lib().mx_gpu_set_timeline(self._h, int(on)))
+
+    def timeline(self):
+        per = np.zeros(self.plan.n_ops, np.float32)
+        tot = ctypes.c_float()
+        check(lib().mx_gpu_timeline(self._h, _ptr(per), self.plan.n_ops, ctypes.byref(tot)), "timeline")
+        return per, tot.value
+
+    def stats(self):
+        s = mx_gpu_stats()
+        check(lib().mx_gpu_get_stats(self._h, ctypes.byref(s)))
+        return {"device_name": s.device_name.decode(), "arena_bytes": s.arena_bytes,
+                "weight_bytes": s.weight_bytes, "pool_bytes": s.pool_bytes, "ops": s.ops, "kernels": s.kernels}
+
+
+def _image_to_np(img):
+    a = np.ctypeslib.as_array(img.data, shape=(img.c, img.h, img.w)).copy()
+    lib().mx_image_free(ctypes.byref(img))
+    return a
+
+
+def _np_to_image(a):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    img = mx_image(a.shape[0], a.shape[1], a.shape[2], a.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    return img, a
+
+
+def png_read(path):
+    img = mx_image()
+    check(lib().mx_png_read(os.fsencode(path), ctypes.byref(img)), str(path))
+    return _image_to_np(img)
+
+
+def png_read_bytes(data):
+    img = mx_image()
+    check(lib().mx_png_read_mem(data, len(data), ctypes.byref(img)), "png")
+    return _image_to_np(img)
+
+
+def png_write(path, a):
+    img, keep = _np_to_image(a)
+    check(lib().mx_png_write(os.fsencode(path), ctypes.byref(img)), str(path))
+
+
+def preprocess(a, factor=64):
+    """`image::preprocess` (src/image.rs:171-207) -> (padded, (even_h, even_w))."""
+    img, keep = _np_to_image(a)
+    out = mx_image()
+    eh, ew = ctypes.c_int32(), ctypes.c_int32()
+    check(lib().mx_preprocess(ctypes.byref(img), factor, ctypes.byref(out), ctypes.byref(eh), ctypes.byref(ew)),
+          "preprocess")
+    return _image_to_np(out), (eh.value, ew.value)
+
+
+def crop_out(a, orig_h, orig_w, even_h, even_w):
+    img, keep = _np_to_image(a)
+    out = mx_image()
+    check(lib().mx_crop_out(ctypes.byref(img), orig_h, orig_w, even_h, even_w, ctypes.byref(out)), "crop")
+    return _image_to_np(out)

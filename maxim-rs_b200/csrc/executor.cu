@@ -1,0 +1,689 @@
+// The GPU executor: the B200 replacement for the reference's `exec_gpu::Gpu`
+// (src/exec_gpu.rs:48-357) behind the C ABI in include/maxim_b200.h.
+//
+// What differs from the reference, by design:
+//   * Activations live in ONE device arena at the plan's own packed offsets
+//     (the plan's liveness is the contract), but each storage-owning buffer is
+//     laid out NHWC - pixel-major, channels contiguous - instead of NCHW. A
+//     channel view of a wider buffer becomes a strided view (same pixel
+//     stride as its parent), so the model's splits and concatenations still
+//     cost nothing. Host images stay NCHW; the boundary transposes on device.
+//   * Every weight is converted to its kernel's layout and uploaded once, at
+//     construction (resident, not lazy per op).
+//   * The whole op stream - input transpose, every op, output transpose - is
+//     captured once into a CUDA graph and replayed per image: one launch per
+//     pass instead of one host dispatch per op.
+// The per-op walk (begin / step_op / read_buf) stays available for the
+// op-by-op verification and runs each op eagerly, unfused.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.h"
+#include "gpu_common.cuh"
+#include "kernels_simt.cuh"
+#include "maxim_b200.h"
+
+namespace mx {
+
+const char* describe_kind(int k);
+
+namespace {
+
+constexpr float kLnEps = 1e-6f;  // src/model.rs:35
+constexpr int TPB = 256;
+
+// Tap table of one resize axis, built exactly as the reference's `ResizeTaps`
+// (src/exec_cpu.rs:1224-1282) so the device kernels apply the same weights.
+struct HostTaps {
+  std::vector<int> j0, w0, cnt;
+  std::vector<float> w, wsum;
+};
+HostTaps make_taps(int n_in, int n_out, int max_taps) {
+  HostTaps t;
+  float inv = float(n_in) / float(n_out);
+  float kscale = inv > 1.0f ? inv : 1.0f;
+  for (int o = 0; o < n_out; ++o) {
+    float sample = (float(o) + 0.5f) * inv - 0.5f;
+    long a = long(std::ceil(sample - kscale));
+    long b = long(std::floor(sample + kscale));
+    if (a < 0) a = 0;
+    if (b > n_in - 1) b = n_in - 1;
+    int first = int(t.w.size());
+    float s = 0.0f;
+    for (long j = a; j <= b; ++j) {
+      float d = std::fabs(sample - float(j)) / kscale;
+      if (d < 1.0f) {
+        float wv = 1.0f - d;
+        t.w.push_back(wv);
+        s += wv;
+      }
+    }
+    t.j0.push_back(int(a));
+    t.w0.push_back(first);
+    t.wsum.push_back(s);
+  }
+  for (int o = 0; o < n_out; ++o) {
+    int end = o + 1 < n_out ? t.w0[o + 1] : int(t.w.size());
+    t.cnt.push_back(std::min(end - t.w0[o], max_taps));
+  }
+  return t;
+}
+
+// A bump allocator over one device allocation: weights and tables, each
+// 256-byte aligned.
+struct DevicePool {
+  std::vector<char> host;
+  char* dev = nullptr;
+  size_t size() const { return host.size(); }
+  size_t put(const void* data, size_t bytes) {
+    size_t off = (host.size() + 255) & ~size_t(255);
+    host.resize(off + bytes);
+    if (bytes) memcpy(&host[off], data, bytes);
+    return off;
+  }
+  template <class T>
+  size_t put(const std::vector<T>& v) {
+    return put(v.data(), v.size() * sizeof(T));
+  }
+};
+
+struct Step {
+  int op;       // plan op index, -1 for the boundary transposes
+  int kernels;  // launches it makes
+  std::function<void(cudaStream_t)> run;
+};
+
+}  // namespace
+}  // namespace mx
+
+struct mx_gpu {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::vector<mx_buf> bufs;
+  std::vector<int64_t> offs;
+  std::vector<int32_t> alias_parent;
+  std::vector<mx_op> ops;
+  int32_t input = -1, output = -1;
+  int64_t arena_len = 0;
+  mx_buf shape{};
+  float* arena = nullptr;
+  float* io_in = nullptr;   // NCHW staging of the input image
+  float* io_out = nullptr;  // NCHW staging of the output image
+  mx::DevicePool pool;
+  int64_t weight_bytes = 0;
+  std::vector<mx::Step> steps;  // full pass: [in-transpose, ops..., out-transpose]
+  std::vector<int> step_of_op;  // op index -> step index
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t graph_exec = nullptr;
+  bool timeline_on = false;
+  std::vector<float> timeline_ms;
+  float timeline_total = 0.0f;
+  int64_t kernels = 0;
+  std::string name;
+};
+
+namespace mx {
+namespace {
+
+struct DevicePin {
+  explicit DevicePin(int dev) { MX_CUDA(cudaSetDevice(dev)); }
+};
+
+int32_t root_of(const mx_gpu& g, int32_t id) {
+  while (g.alias_parent[size_t(id)] >= 0) id = g.alias_parent[size_t(id)];
+  return id;
+}
+
+View view_of(const mx_gpu& g, int32_t id) {
+  int32_t base = root_of(g, id);
+  const mx_buf& b = g.bufs[size_t(id)];
+  int64_t hw = b.h * b.w;
+  int64_t ch0 = hw ? (g.offs[size_t(id)] - g.offs[size_t(base)]) / hw : 0;
+  View v;
+  v.ptr = g.arena + g.offs[size_t(base)] + ch0;
+  v.stride = g.bufs[size_t(base)].c;
+  v.c = b.c;
+  v.npix = hw;
+  return v;
+}
+
+bool aligned4(const View& v) {
+  return (reinterpret_cast<uintptr_t>(v.ptr) % 16 == 0) && v.stride % 4 == 0 && v.c % 4 == 0;
+}
+
+template <int KIND>
+void launch_ew(cudaStream_t s, View d, View a, View b, float slope) {
+  int64_t npix = d.npix;
+  if (aligned4(d) && aligned4(a) && (b.ptr == nullptr || aligned4(b))) {
+    int c4 = int(d.c / 4);
+    ew_kernel4<KIND><<<blocks_for(npix * c4, TPB), TPB, 0, s>>>(npix, c4, a.ptr, a.stride, b.ptr, b.stride, d.ptr,
+                                                                  d.stride, slope);
+  } else {
+    ew_kernel1<KIND><<<blocks_for(npix * d.c, TPB), TPB, 0, s>>>(npix, int(d.c), a.ptr, a.stride, b.ptr, b.stride,
+                                                                   d.ptr, d.stride, slope);
+  }
+}
+
+template <int BM, int BN, class P>
+void launch_gemm(cudaStream_t s, const P& p, int batch) {
+  dim3 grid(unsigned((p.M + BM - 1) / BM), unsigned((p.N + BN - 1) / BN), unsigned(batch));
+  simt_gemm_kernel<BM, BN, 4, 4, P><<<grid, (BM / 4) * (BN / 4), 0, s>>>(p);
+}
+
+void check_launch() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw Error(std::string("kernel launch: ") + cudaGetErrorString(e), MX_E_CUDA);
+}
+
+// Build the step for one op. Weight layouts are converted here and recorded
+// in the pool; pointers are resolved after the pool is uploaded, so each
+// step captures the pool offset and reads the base at run time.
+void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
+  const mx_op o = plan.ops[oi];
+  auto W = [&](int32_t id) -> std::vector<float> {
+    if (id < 0) return {};
+    return std::vector<float>(plan.weights[id], plan.weights[id] + plan.weight_lens[id]);
+  };
+  auto put = [&](const std::vector<float>& v) -> int64_t {
+    if (v.empty()) return -1;
+    g.weight_bytes += int64_t(v.size() * 4);
+    return int64_t(g.pool.put(v));
+  };
+  mx_gpu* G = &g;
+  auto P = [G](int64_t off) -> const float* {
+    return off < 0 ? nullptr : reinterpret_cast<const float*>(G->pool.dev + off);
+  };
+  Step st{oi, 1, nullptr};
+  const int32_t dst = o.dst, src = o.src, src2 = o.src2;
+  switch (o.kind) {
+    case MX_OP_COPY:
+    case MX_OP_ADD:
+    case MX_OP_MUL:
+    case MX_OP_GATE_APPLY:
+    case MX_OP_GELU:
+    case MX_OP_LRELU:
+    case MX_OP_SIGMOID: {
+      const mx_buf& db = g.bufs[size_t(dst)];
+      if (db.c * db.h * db.w != o.n)
+        throw Error(fmt("op %d: an elementwise op over %lld values on a %lldx%lldx%lld buffer is not supported", oi,
+                        (long long)o.n, (long long)db.c, (long long)db.h, (long long)db.w));
+      int kind = o.kind;
+      float slope = o.slope;
+      st.run = [G, kind, dst, src, src2, slope](cudaStream_t s) {
+        View d = view_of(*G, dst), a = view_of(*G, src);
+        View b{nullptr, 0, 0, 0};
+        if (src2 >= 0) b = view_of(*G, src2);
+        switch (kind) {
+          case MX_OP_COPY: launch_ew<EW_COPY>(s, d, a, b, slope); break;
+          case MX_OP_ADD: launch_ew<EW_ADD>(s, d, a, b, slope); break;
+          case MX_OP_MUL: launch_ew<EW_MUL>(s, d, a, b, slope); break;
+          case MX_OP_GATE_APPLY: launch_ew<EW_GATE>(s, d, a, b, slope); break;
+          case MX_OP_GELU: launch_ew<EW_GELU>(s, d, a, b, slope); break;
+          case MX_OP_LRELU: launch_ew<EW_LRELU>(s, d, a, b, slope); break;
+          default: launch_ew<EW_SIGMOID>(s, d, a, b, slope); break;
+        }
+      };
+      break;
+    }
+    case MX_OP_CHAN_LN: {
+      int64_t ws = put(W(o.scale)), wb = put(W(o.bias));
+      st.run = [G, P, dst, src, ws, wb](cudaStream_t s) {
+        View d = view_of(*G, dst), x = view_of(*G, src);
+        if (aligned4(d) && aligned4(x))
+          chan_ln_kernel4<<<blocks_for(x.npix, 128), 128, 0, s>>>(x.npix, int(x.c), x.ptr, x.stride, P(ws), P(wb),
+                                                                  d.ptr, d.stride, kLnEps);
+        else
+          chan_ln_kernel1<<<blocks_for(x.npix, 128), 128, 0, s>>>(x.npix, int(x.c), x.ptr, x.stride, P(ws), P(wb),
+                                                                  d.ptr, d.stride, kLnEps);
+      };
+      break;
+    }
+    case MX_OP_CHAN_MEAN: {
+      st.run = [G, dst, src](cudaStream_t s) {
+        View d = view_of(*G, dst), x = view_of(*G, src);
+        chan_mean_kernel<<<unsigned(x.c), 512, 0, s>>>(x.npix, x.ptr, x.stride, d.ptr);
+      };
+      break;
+    }
+    case MX_OP_CHAN_SCALE: {
+      st.run = [G, dst, src, src2](cudaStream_t s) {
+        View d = view_of(*G, dst), x = view_of(*G, src), sc = view_of(*G, src2);
+        chan_scale_kernel<<<blocks_for(x.npix * x.c, TPB), TPB, 0, s>>>(x.npix, int(x.c), x.ptr, x.stride, sc.ptr,
+                                                                        d.ptr, d.stride);
+      };
+      break;
+    }
+    case MX_OP_CONV1X1: {
+      int64_t wo = put(W(o.w)), bo = put(W(o.bias));  // [c_out][c_in]
+      int ci = o.c_in, co = o.c_out;
+      st.run = [G, P, dst, src, wo, bo, ci, co](cudaStream_t s) {
+        View d = view_of(*G, dst), x = view_of(*G, src);
+        ProbConv1x1 p{x.ptr, x.stride, P(wo), P(bo), d.ptr, d.stride, x.npix, co, ci};
+        if (co <= 32) launch_gemm<64, 32>(s, p, 1);
+        else launch_gemm<64, 64>(s, p, 1);
+      };
+      break;
+    }
+    case MX_OP_CONV3X3:
+    case MX_OP_CONV4X4S2: {
+      int ks = o.kind == MX_OP_CONV3X3 ? 3 : 4;
+      int ci = o.c_in, co = o.c_out;
+      // [co][ci][k][k] -> [co][tap][ci]
+      auto w = W(o.w);
+      std::vector<float> wt(w.size());
+      for (int oc = 0; oc < co; ++oc)
+        for (int ic = 0; ic < ci; ++ic)
+          for (int t = 0; t < ks * ks; ++t)
+            wt[(size_t(oc) * ks * ks + t) * ci + ic] = w[(size_t(oc) * ci + ic) * ks * ks + t];
+      int64_t wo = put(wt), bo = put(W(o.bias));
+      int h = o.h, wd = o.wd;
+      int oh = ks == 3 ? h : o.oh, ow = ks == 3 ? wd : o.ow;
+      int stride = ks == 3 ? 1 : 2, pt = ks == 3 ? 1 : o.pad_top, pl = ks == 3 ? 1 : o.pad_left;
+      st.run = [G, P, dst, src, wo, bo, ci, co, h, wd, oh, ow, ks, stride, pt, pl](cudaStream_t s) {
+        View d = view_of(*G, dst), x = view_of(*G, src);
+        ProbConvKxK p{x.ptr, x.stride, P(wo), P(bo), d.ptr, d.stride, int64_t(oh) * ow, co, ks * ks * ci,
+                      ci, h, wd, oh, ow, ks, stride, pt, pl};
+        if (co <= 32) launch_gemm<64, 32>(s, p, 1);
+        else launch_gemm<64, 64>(s, p, 1);
+      };
+      break;
+    }
+    case MX_OP_CONVT2X2: {
+      int ci = o.c_in, co = o.c_out;
+      // [ci][co][2][2] (flipped) -> [tap*co + o][ci]
+      auto w = W(o.w);
+      std::vector<float> wt(w.size());
+      for (int ic = 0; ic < ci; ++ic)
+        for (int oc = 0; oc < co; ++oc)
+          for (int t = 0; t < 4; ++t) wt[(size_t(t) * co + oc) * ci + ic] = w[(size_t(ic) * co + oc) * 4 + t];
+      int64_t wo = put(wt), bo = put(W(o.bias));
+      int wd = o.wd;
+      st.run = [G, P, dst, src, wo, bo, ci, co, wd](cudaStream_t s) {
+        View d = view_of(*G, dst), x = view_of(*G, src);
+        ProbConvT p{x.ptr, x.stride, P(wo), P(bo), d.ptr, d.stride, x.npix, 4 * co, ci, co, wd};
+        launch_gemm<64, 64>(s, p, 1);
+      };
+      break;
+    }
+    case MX_OP_GATE_MM: {
+      int64_t wo = put(W(o.w)), bo = put(W(o.bias));  // [out][in]
+      int c = o.c, outer = o.outer, inner = o.inner, mode = o.mode;
+      st.run = [G, P, dst, src, wo, bo, c, outer, inner, mode](cudaStream_t s) {
+        View d = view_of(*G, dst), x = view_of(*G, src);
+        if (mode == 0) {
+          ProbGate0 p{x.ptr, x.stride, P(wo), P(bo), d.ptr, d.stride, outer, inner * c, outer, c, inner};
+          launch_gemm<64, 64>(s, p, 1);
+        } else {
+          ProbGate1 p{x.ptr, x.stride, P(wo), P(bo), d.ptr, d.stride, inner, c, inner, inner};
+          if (c <= 32) launch_gemm<64, 32>(s, p, outer);
+          else launch_gemm<64, 64>(s, p, outer);
+        }
+      };
+      break;
+    }
+    case MX_OP_BLOCK_PERM: {
+      const mx_op op = o;
+      if (int64_t(o.gh) * o.fh != o.h || int64_t(o.gw) * o.fw != o.wd)
+        throw Error(fmt("op %d: a %dx%d blocking of a %dx%d plane drops pixels; the executor needs plans whose "
+                        "planes the blocks tile exactly (the pad-to-64 pipeline always does)",
+                        oi, o.gh * o.fh, o.gw * o.fw, o.h, o.wd));
+      st.run = [G, op](cudaStream_t s) {
+        View d = view_of(*G, op.dst), x = view_of(*G, op.src);
+        int64_t total = int64_t(op.h) * op.wd * op.c;
+        block_perm_kernel<<<blocks_for(total, TPB), TPB, 0, s>>>(total, op.c, op.wd, op.gw, op.fh, op.fw,
+                                                                 op.gh * op.gw, op.fh * op.fw, op.swap, op.forward,
+                                                                 x.ptr, x.stride, d.ptr, d.stride);
+      };
+      break;
+    }
+    case MX_OP_DOWN_S: {
+      const mx_op op = o;
+      st.run = [G, op](cudaStream_t s) {
+        View d = view_of(*G, op.dst), x = view_of(*G, op.src);
+        int64_t total = int64_t(op.oh) * op.ow * op.c;
+        down_s_kernel<<<blocks_for(total, TPB), TPB, 0, s>>>(total, op.c, op.wd, op.ow, op.stride, op.off, x.ptr,
+                                                             x.stride, d.ptr, d.stride);
+      };
+      break;
+    }
+    case MX_OP_RESIZE: {
+      const mx_op op = o;
+      HostTaps tx = make_taps(o.win, o.wout, 1 << 30), ty = make_taps(o.hin, o.hout, 64);
+      int64_t tx_j0 = int64_t(g.pool.put(tx.j0)), tx_w0 = int64_t(g.pool.put(tx.w0)),
+              tx_c = int64_t(g.pool.put(tx.cnt)), tx_w = int64_t(g.pool.put(tx.w)),
+              tx_s = int64_t(g.pool.put(tx.wsum));
+      int64_t ty_j0 = int64_t(g.pool.put(ty.j0)), ty_w0 = int64_t(g.pool.put(ty.w0)),
+              ty_c = int64_t(g.pool.put(ty.cnt)), ty_w = int64_t(g.pool.put(ty.w)),
+              ty_s = int64_t(g.pool.put(ty.wsum));
+      st.kernels = 2;
+      st.run = [G, op, tx_j0, tx_w0, tx_c, tx_w, tx_s, ty_j0, ty_w0, ty_c, ty_w, ty_s](cudaStream_t s) {
+        auto I = [G](int64_t off) { return reinterpret_cast<const int*>(G->pool.dev + off); };
+        auto F = [G](int64_t off) { return reinterpret_cast<const float*>(G->pool.dev + off); };
+        View d = view_of(*G, op.dst), x = view_of(*G, op.src), t = view_of(*G, op.tmp);
+        TapTable TX{I(tx_j0), I(tx_w0), I(tx_c), F(tx_w), F(tx_s)};
+        TapTable TY{I(ty_j0), I(ty_w0), I(ty_c), F(ty_w), F(ty_s)};
+        int64_t t1 = int64_t(op.hin) * op.wout * op.c;
+        resize_h_kernel<<<blocks_for(t1, TPB), TPB, 0, s>>>(t1, op.c, op.win, op.wout, TX, x.ptr, x.stride, t.ptr,
+                                                            t.stride);
+        int64_t t2 = int64_t(op.hout) * op.wout * op.c;
+        resize_v_kernel<<<blocks_for(t2, TPB), TPB, 0, s>>>(t2, op.c, op.hin, op.hout, op.wout, TY, t.ptr, t.stride,
+                                                            d.ptr, d.stride);
+      };
+      break;
+    }
+    default:
+      throw Error(fmt("op %d: unknown op kind %d", oi, o.kind));
+  }
+  g.step_of_op[size_t(oi)] = int(g.steps.size());
+  g.steps.push_back(std::move(st));
+}
+
+void build_boundary_steps(mx_gpu& g) {
+  mx_gpu* G = &g;
+  int32_t in = g.input, out = g.output;
+  Step a{-1, 1, [G, in](cudaStream_t s) {
+           View d = view_of(*G, in);
+           nchw_to_nhwc_kernel<<<blocks_for(d.npix * d.c, TPB), TPB, 0, s>>>(d.npix, int(d.c), G->io_in, d.ptr,
+                                                                             d.stride);
+         }};
+  Step b{-1, 1, [G, out](cudaStream_t s) {
+           View x = view_of(*G, out);
+           nhwc_to_nchw_kernel<<<blocks_for(x.npix * x.c, TPB), TPB, 0, s>>>(x.npix, int(x.c), x.ptr, x.stride,
+                                                                             G->io_out);
+         }};
+  g.steps.insert(g.steps.begin(), std::move(a));
+  for (auto& v : g.step_of_op) v += 1;
+  g.steps.push_back(std::move(b));
+}
+
+void capture_graph(mx_gpu& g) {
+  if (g.graph_exec) return;
+  MX_CUDA(cudaStreamBeginCapture(g.stream, cudaStreamCaptureModeThreadLocal));
+  try {
+    for (auto& st : g.steps) st.run(g.stream);
+  } catch (...) {
+    cudaGraph_t tmp;
+    cudaStreamEndCapture(g.stream, &tmp);
+    if (tmp) cudaGraphDestroy(tmp);
+    throw;
+  }
+  MX_CUDA(cudaStreamEndCapture(g.stream, &g.graph));
+  MX_CUDA(cudaGraphInstantiate(&g.graph_exec, g.graph, 0));
+}
+
+int64_t len_of(const mx_buf& b) { return b.c * b.h * b.w; }
+
+}  // namespace
+
+const char* describe_kind(int k) {
+  static const char* names[] = {"copy", "add", "mul", "gate", "gelu", "lrelu", "sigmoid", "chanln", "chanmean",
+                                "chanscale", "conv1x1", "conv3x3", "convdown", "convt", "gatemm", "blockperm",
+                                "resize", "down"};
+  return (k >= 0 && k < MX_OP_KINDS) ? names[k] : "?";
+}
+
+}  // namespace mx
+
+using namespace mx;
+
+extern "C" {
+
+int mx_driver_ready(void) {
+  return guard([&] {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) throw Error(std::string("cuda: ") + cudaGetErrorString(e), MX_E_NO_DEVICE);
+    if (n == 0) throw Error("cuda: no CUDA device is visible", MX_E_NO_DEVICE);
+  });
+}
+
+int mx_device_count(int* count) {
+  return guard([&] {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) n = 0;
+    if (count) *count = n;
+    if (e != cudaSuccess) throw Error(std::string("cuda: ") + cudaGetErrorString(e), MX_E_NO_DEVICE);
+  });
+}
+
+int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) {
+  std::unique_ptr<mx_gpu> g;
+  int rc = guard([&] {
+    if (!plan || !out) throw Error("mx_gpu_new: null argument");
+    if (plan->input < 0 || plan->output < 0 || plan->n_ops <= 0) throw Error("mx_gpu_new: empty plan");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+      throw Error("cuda: no CUDA device is visible", MX_E_NO_DEVICE);
+    if (device < 0 || device >= ndev) throw Error(fmt("cuda: device %d does not exist (%d visible)", device, ndev));
+    DevicePin pin(device);
+    g = std::make_unique<mx_gpu>();
+    g->device = device;
+    g->bufs.assign(plan->bufs, plan->bufs + plan->n_bufs);
+    g->offs.assign(plan->offs, plan->offs + plan->n_bufs);
+    g->alias_parent.assign(plan->alias_parent, plan->alias_parent + plan->n_bufs);
+    g->ops.assign(plan->ops, plan->ops + plan->n_ops);
+    g->input = plan->input;
+    g->output = plan->output;
+    g->arena_len = plan->arena_len;
+    g->shape = plan->shape;
+    for (int32_t i = 0; i < plan->n_ops; ++i)
+      for (int32_t w : {plan->ops[i].w, plan->ops[i].bias, plan->ops[i].scale})
+        if (w >= 0 && (w >= plan->n_weights || (plan->weight_lens[w] > 0 && !plan->weights[w])))
+          throw Error(fmt("op %d names weight %d, which the plan does not carry", i, w));
+    g->step_of_op.assign(size_t(plan->n_ops), -1);
+    for (int32_t i = 0; i < plan->n_ops; ++i) plan_op(*g, *plan, i);
+    build_boundary_steps(*g);
+    for (auto& st : g->steps) g->kernels += st.kernels;
+
+    // Size the pass before allocating it, and refuse it with the numbers
+    // (src/exec_gpu.rs:96-146).
+    size_t free_b = 0, total_b = 0;
+    MX_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    int64_t arena_bytes = plan->arena_len * 4;
+    int64_t io_bytes = (len_of(g->bufs[size_t(g->input)]) + len_of(g->bufs[size_t(g->output)])) * 4;
+    int64_t need = arena_bytes + int64_t(g->pool.size()) + io_bytes;
+    if (need > int64_t(free_b))
+      throw Error(fmt("not enough device memory for a %lldx%lld pass\n"
+                      "maxim: the arena needs %lld MiB and the weights %lld MiB; %lld MiB is free\n"
+                      "maxim: the arena is exact - it is the plan's own packed size, not an estimate - so this is "
+                      "a hard limit, not a guess",
+                      (long long)plan->shape.w, (long long)plan->shape.h, (long long)(arena_bytes >> 20),
+                      (long long)(g->pool.size() >> 20), (long long)(free_b >> 20)),
+                  MX_E_OOM);
+    MX_CUDA(cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking));
+    cudaError_t e = cudaMalloc(&g->arena, size_t(arena_bytes > 0 ? arena_bytes : 4));
+    if (e != cudaSuccess)
+      throw Error(fmt("the arena for %lldx%lld (%lld MiB) did not fit after all, with %lld MiB free: %s",
+                      (long long)plan->shape.w, (long long)plan->shape.h, (long long)(arena_bytes >> 20),
+                      (long long)(free_b >> 20), cudaGetErrorString(e)),
+                  MX_E_OOM);
+    MX_CUDA(cudaMalloc(&g->pool.dev, std::max<size_t>(g->pool.size(), 256)));
+    MX_CUDA(cudaMemcpy(g->pool.dev, g->pool.host.data(), g->pool.size(), cudaMemcpyHostToDevice));
+    g->pool.host.clear();
+    g->pool.host.shrink_to_fit();
+    MX_CUDA(cudaMalloc(&g->io_in, size_t(len_of(g->bufs[size_t(g->input)]) * 4)));
+    MX_CUDA(cudaMalloc(&g->io_out, size_t(len_of(g->bufs[size_t(g->output)]) * 4)));
+    cudaDeviceProp prop;
+    MX_CUDA(cudaGetDeviceProperties(&prop, device));
+    g->name = prop.name;
+    *out = g.release();
+  });
+  if (rc != MX_OK && g) mx_gpu_free(g.release());
+  return rc;
+}
+
+void mx_gpu_free(mx_gpu* g) {
+  if (!g) return;
+  cudaSetDevice(g->device);
+  if (g->stream) cudaStreamSynchronize(g->stream);
+  if (g->graph_exec) cudaGraphExecDestroy(g->graph_exec);
+  if (g->graph) cudaGraphDestroy(g->graph);
+  cudaFree(g->arena);
+  cudaFree(g->pool.dev);
+  cudaFree(g->io_in);
+  cudaFree(g->io_out);
+  if (g->stream) cudaStreamDestroy(g->stream);
+  delete g;
+}
+
+int mx_gpu_upload_input(mx_gpu* g, const float* input) {
+  return guard([&] {
+    if (!g || !input) throw Error("mx_gpu_upload_input: null argument");
+    DevicePin pin(g->device);
+    MX_CUDA(cudaMemcpyAsync(g->io_in, input, size_t(len_of(g->bufs[size_t(g->input)]) * 4), cudaMemcpyHostToDevice,
+                            g->stream));
+  });
+}
+
+int mx_gpu_enqueue(mx_gpu* g) {
+  return guard([&] {
+    if (!g) throw Error("mx_gpu_enqueue: null handle");
+    DevicePin pin(g->device);
+    if (g->timeline_on) {
+      // One event before every step and one after the last, one sync at the
+      // end (src/exec_gpu.rs:231-265).
+      size_t n = g->steps.size();
+      std::vector<cudaEvent_t> ev(n + 1);
+      for (auto& e : ev) MX_CUDA(cudaEventCreate(&e));
+      for (size_t i = 0; i < n; ++i) {
+        MX_CUDA(cudaEventRecord(ev[i], g->stream));
+        g->steps[i].run(g->stream);
+      }
+      MX_CUDA(cudaEventRecord(ev[n], g->stream));
+      check_launch();
+      MX_CUDA(cudaEventSynchronize(ev[n]));
+      g->timeline_ms.assign(g->ops.size(), 0.0f);
+      g->timeline_total = 0.0f;
+      for (size_t i = 0; i < n; ++i) {
+        float ms = 0.0f;
+        MX_CUDA(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+        g->timeline_total += ms;
+        int op = g->steps[i].op;
+        if (op >= 0) g->timeline_ms[size_t(op)] += ms;
+      }
+      for (auto& e : ev) cudaEventDestroy(e);
+      return;
+    }
+    capture_graph(*g);
+    MX_CUDA(cudaGraphLaunch(g->graph_exec, g->stream));
+  });
+}
+
+int mx_gpu_download_output(mx_gpu* g, float* output) {
+  return guard([&] {
+    if (!g || !output) throw Error("mx_gpu_download_output: null argument");
+    DevicePin pin(g->device);
+    MX_CUDA(cudaMemcpyAsync(output, g->io_out, size_t(len_of(g->bufs[size_t(g->output)]) * 4),
+                            cudaMemcpyDeviceToHost, g->stream));
+  });
+}
+
+int mx_gpu_sync(mx_gpu* g) {
+  return guard([&] {
+    if (!g) throw Error("mx_gpu_sync: null handle");
+    DevicePin pin(g->device);
+    MX_CUDA(cudaStreamSynchronize(g->stream));
+  });
+}
+
+int mx_gpu_run(mx_gpu* g, const float* input, float* output) {
+  int rc = mx_gpu_upload_input(g, input);
+  if (rc == MX_OK) rc = mx_gpu_enqueue(g);
+  if (rc == MX_OK) rc = mx_gpu_download_output(g, output);
+  if (rc == MX_OK) rc = mx_gpu_sync(g);
+  return rc;
+}
+
+int mx_gpu_begin(mx_gpu* g, const float* input) {
+  return guard([&] {
+    if (!g || !input) throw Error("mx_gpu_begin: null argument");
+    DevicePin pin(g->device);
+    if (std::getenv("MAXIM_POISON"))
+      MX_CUDA(cudaMemsetAsync(g->arena, 0xCD, size_t(g->arena_len) * 4, g->stream));
+    MX_CUDA(cudaMemcpyAsync(g->io_in, input, size_t(len_of(g->bufs[size_t(g->input)]) * 4), cudaMemcpyHostToDevice,
+                            g->stream));
+    g->steps.front().run(g->stream);
+    check_launch();
+    MX_CUDA(cudaStreamSynchronize(g->stream));
+  });
+}
+
+int mx_gpu_step_op(mx_gpu* g, int32_t i) {
+  return guard([&] {
+    if (!g || i < 0 || size_t(i) >= g->ops.size()) throw Error("mx_gpu_step_op: op index out of range");
+    DevicePin pin(g->device);
+    int s = g->step_of_op[size_t(i)];
+    if (s >= 0) g->steps[size_t(s)].run(g->stream);
+    check_launch();
+    MX_CUDA(cudaStreamSynchronize(g->stream));
+  });
+}
+
+int mx_gpu_read_buf(mx_gpu* g, int32_t id, float* out, int64_t len) {
+  return guard([&] {
+    if (!g || !out || id < 0 || size_t(id) >= g->bufs.size()) throw Error("mx_gpu_read_buf: bad argument");
+    if (len != len_of(g->bufs[size_t(id)])) throw Error("mx_gpu_read_buf: length does not match the buffer");
+    DevicePin pin(g->device);
+    View v = view_of(*g, id);
+    float* tmp = nullptr;
+    MX_CUDA(cudaMalloc(&tmp, size_t(std::max<int64_t>(len, 1)) * 4));
+    nhwc_to_nchw_kernel<<<blocks_for(v.npix * v.c, TPB), TPB, 0, g->stream>>>(v.npix, int(v.c), v.ptr, v.stride, tmp);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, tmp, size_t(len) * 4, cudaMemcpyDeviceToHost, g->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) throw Error(std::string("read_buf: ") + cudaGetErrorString(e), MX_E_CUDA);
+  });
+}
+
+int mx_gpu_read_arena(mx_gpu* g, float* out, int64_t len) {
+  return guard([&] {
+    if (!g || !out || len != g->arena_len) throw Error("mx_gpu_read_arena: bad argument");
+    DevicePin pin(g->device);
+    MX_CUDA(cudaMemcpyAsync(out, g->arena, size_t(len) * 4, cudaMemcpyDeviceToHost, g->stream));
+    MX_CUDA(cudaStreamSynchronize(g->stream));
+  });
+}
+
+int mx_gpu_set_timeline(mx_gpu* g, int on) {
+  return guard([&] {
+    if (!g) throw Error("mx_gpu_set_timeline: null handle");
+    g->timeline_on = on != 0;
+  });
+}
+
+int mx_gpu_timeline(mx_gpu* g, float* per_op_ms, int32_t n_ops, float* total_ms) {
+  return guard([&] {
+    if (!g) throw Error("mx_gpu_timeline: null handle");
+    if (g->timeline_ms.empty()) throw Error("no timeline recorded: turn it on and run a pass first");
+    if (per_op_ms) {
+      if (size_t(n_ops) != g->ops.size()) throw Error("mx_gpu_timeline: n_ops does not match the plan");
+      memcpy(per_op_ms, g->timeline_ms.data(), g->ops.size() * 4);
+    }
+    if (total_ms) *total_ms = g->timeline_total;
+  });
+}
+
+int mx_gpu_get_stats(mx_gpu* g, mx_gpu_stats* s) {
+  return guard([&] {
+    if (!g || !s) throw Error("mx_gpu_get_stats: null argument");
+    memset(s, 0, sizeof(*s));
+    snprintf(s->device_name, sizeof(s->device_name), "%s", g->name.c_str());
+    s->arena_bytes = g->arena_len * 4;
+    s->weight_bytes = g->weight_bytes;
+    s->pool_bytes = 0;
+    s->ops = int64_t(g->ops.size());
+    s->kernels = g->kernels;
+  });
+}
+
+}  // extern "C"
