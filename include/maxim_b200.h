@@ -152,6 +152,13 @@ int mx_gpu_upload_input(mx_gpu* g, const float* input);
 int mx_gpu_enqueue(mx_gpu* g);
 int mx_gpu_download_output(mx_gpu* g, float* output);
 int mx_gpu_sync(mx_gpu* g);
+/* The same two copies from / to DEVICE memory of the handle's device (a
+ * batch of images already resident in HBM): device-to-device, async. */
+int mx_gpu_upload_input_device(mx_gpu* g, const float* dev_input);
+int mx_gpu_download_output_device(mx_gpu* g, float* dev_output);
+/* The handle's CUDA stream (a cudaStream_t, as an opaque pointer) so a caller
+ * can order its own work or record timing events against the pass. */
+int mx_gpu_stream(mx_gpu* g, void** stream);
 
 /* `Gpu::begin` / `step_op` / `read_buf` / `read_into` / `read_arena`
  * (src/exec_gpu.rs:329-357): the op-by-op walk behind `--verify-gpu`.

@@ -76,6 +76,9 @@ _SIGS = {
     "mx_gpu_enqueue": (ctypes.c_int, [ctypes.c_void_p]),
     "mx_gpu_download_output": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "mx_gpu_sync": (ctypes.c_int, [ctypes.c_void_p]),
+    "mx_gpu_stream": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "mx_gpu_upload_input_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "mx_gpu_download_output_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "mx_gpu_begin": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "mx_gpu_step_op": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32]),
     "mx_gpu_read_buf": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64]),
@@ -292,6 +295,19 @@ class Gpu:
 
     def download_output(self, out):
         check(lib().mx_gpu_download_output(self._h, _ptr(out)), "download")
+
+    def stream(self):
+        """The handle's cudaStream_t as an integer (for torch.cuda.ExternalStream)."""
+        s = ctypes.c_void_p()
+        check(lib().mx_gpu_stream(self._h, ctypes.byref(s)), "stream")
+        return s.value or 0
+
+    def upload_input_device(self, dev_ptr):
+        """Copy the input from device memory (an integer address on this device)."""
+        check(lib().mx_gpu_upload_input_device(self._h, ctypes.c_void_p(dev_ptr)), "upload (device)")
+
+    def download_output_device(self, dev_ptr):
+        check(lib().mx_gpu_download_output_device(self._h, ctypes.c_void_p(dev_ptr)), "download (device)")
 
     def sync(self):
         check(lib().mx_gpu_sync(self._h), "sync")

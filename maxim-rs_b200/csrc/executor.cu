@@ -544,6 +544,31 @@ int mx_gpu_upload_input(mx_gpu* g, const float* input) {
   });
 }
 
+int mx_gpu_upload_input_device(mx_gpu* g, const float* dev_input) {
+  return guard([&] {
+    if (!g || !dev_input) throw Error("mx_gpu_upload_input_device: null argument");
+    DevicePin pin(g->device);
+    MX_CUDA(cudaMemcpyAsync(g->io_in, dev_input, size_t(len_of(g->bufs[size_t(g->input)]) * 4),
+                            cudaMemcpyDeviceToDevice, g->stream));
+  });
+}
+
+int mx_gpu_download_output_device(mx_gpu* g, float* dev_output) {
+  return guard([&] {
+    if (!g || !dev_output) throw Error("mx_gpu_download_output_device: null argument");
+    DevicePin pin(g->device);
+    MX_CUDA(cudaMemcpyAsync(dev_output, g->io_out, size_t(len_of(g->bufs[size_t(g->output)]) * 4),
+                            cudaMemcpyDeviceToDevice, g->stream));
+  });
+}
+
+int mx_gpu_stream(mx_gpu* g, void** stream) {
+  return guard([&] {
+    if (!g || !stream) throw Error("mx_gpu_stream: null argument");
+    *stream = static_cast<void*>(g->stream);
+  });
+}
+
 int mx_gpu_enqueue(mx_gpu* g) {
   return guard([&] {
     if (!g) throw Error("mx_gpu_enqueue: null handle");

@@ -1,0 +1,64 @@
+"""Algorithmic work per op: FLOPs (2 per multiply-add) and fp32 bytes moved if
+each op reads its inputs and writes its output exactly once (weights once).
+
+These are the numerators of every roofline figure this project reports; they
+depend only on the plan, never on how a kernel happens to move its data.
+"""
+import collections
+
+KINDS = ["copy", "add", "mul", "gate_apply", "gelu", "lrelu", "sigmoid", "chan_ln", "chan_mean", "chan_scale",
+         "conv1x1", "conv3x3", "conv4x4s2", "convt2x2", "gate_mm", "block_perm", "resize", "down_s"]
+
+
+def op_work(plan, op):
+    """(flops, bytes) of one op."""
+    k = KINDS[op.kind]
+    def n(b):
+        c, h, w = plan.buf(b)
+        return c * h * w
+    if k in ("copy", "gelu", "lrelu", "sigmoid"):
+        return (op.n if k != "copy" else 0), 8 * op.n
+    if k in ("add", "mul", "gate_apply"):
+        return op.n, 12 * op.n
+    if k == "chan_ln":
+        e = op.c * op.hw
+        return 8 * e, 8 * e + 8 * op.c
+    if k == "chan_mean":
+        return op.c * op.hw, 4 * (op.c * op.hw + op.c)
+    if k == "chan_scale":
+        return op.c * op.hw, 8 * op.c * op.hw + 4 * op.c
+    if k == "conv1x1":
+        m = op.h * op.wd
+        return 2 * m * op.c_in * op.c_out, 4 * (m * (op.c_in + op.c_out) + op.c_in * op.c_out + op.c_out)
+    if k == "conv3x3":
+        m = op.h * op.wd
+        return 18 * m * op.c_in * op.c_out, 4 * (m * (op.c_in + op.c_out) + 9 * op.c_in * op.c_out + op.c_out)
+    if k == "conv4x4s2":
+        m = op.oh * op.ow
+        return 32 * m * op.c_in * op.c_out, 4 * (op.h * op.wd * op.c_in + m * op.c_out + 16 * op.c_in * op.c_out)
+    if k == "convt2x2":
+        m = op.h * op.wd
+        return 8 * m * op.c_in * op.c_out, 4 * (m * op.c_in + 4 * m * op.c_out + 4 * op.c_in * op.c_out)
+    if k == "gate_mm":
+        nn = op.outer if op.mode == 0 else op.inner
+        e = op.c * op.outer * op.inner
+        return 2 * e * nn, 4 * (2 * e + nn * nn + nn)
+    if k == "block_perm":
+        return 0, 8 * n(op.dst)
+    if k == "resize":
+        return 0, 4 * (op.c * op.hin * op.win + op.c * op.hout * op.wout)
+    if k == "down_s":
+        return 0, 8 * op.c * op.oh * op.ow
+    return 0, 0
+
+
+def census(plan):
+    """{kind: [ops, flops, bytes]} over the whole plan."""
+    out = collections.OrderedDict()
+    for op in plan.ops():
+        f, b = op_work(plan, op)
+        e = out.setdefault(KINDS[op.kind], [0, 0, 0])
+        e[0] += 1
+        e[1] += f
+        e[2] += b
+    return out

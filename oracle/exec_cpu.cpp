@@ -35,6 +35,7 @@
 #include <cstdint>
 #include <cstring>
 #include <functional>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -48,6 +49,8 @@ constexpr float kEps = 1e-6f;  // src/model.rs:35
 constexpr int64_t PB = 256;    // pixels per conv1x1 task tile (exec_cpu.rs:37)
 
 // A fixed pool of workers; run(n, f) calls f(0..n-1) across them and waits.
+// Each run is its own Job with its own counters, so a worker still leaving
+// the previous run can never claim (or count) a task of the next one.
 class Pool {
  public:
   explicit Pool(int threads) : n_(std::max(1, threads)) {
@@ -69,28 +72,33 @@ class Pool {
       for (int64_t i = 0; i < tasks; ++i) f(i);
       return;
     }
+    auto job = std::make_shared<Job>();
+    job->f = &f;
+    job->total = tasks;
     {
       std::lock_guard<std::mutex> l(m_);
-      f_ = &f;
-      total_ = tasks;
-      next_.store(0);
-      done_.store(0);
+      job_ = job;
       ++gen_;
     }
     cv_.notify_all();
-    work();
+    work(*job);
     std::unique_lock<std::mutex> l(m_);
-    done_cv_.wait(l, [&] { return done_.load() == total_; });
-    f_ = nullptr;
+    done_cv_.wait(l, [&] { return job->done.load() == job->total; });
+    job_.reset();
   }
 
  private:
-  void work() {
+  struct Job {
+    const std::function<void(int64_t)>* f = nullptr;
+    int64_t total = 0;
+    std::atomic<int64_t> next{0}, done{0};
+  };
+  void work(Job& j) {
     for (;;) {
-      int64_t i = next_.fetch_add(1);
-      if (i >= total_) break;
-      (*f_)(i);
-      if (done_.fetch_add(1) + 1 == total_) {
+      int64_t i = j.next.fetch_add(1);
+      if (i >= j.total) break;
+      (*j.f)(i);
+      if (j.done.fetch_add(1) + 1 == j.total) {
         std::lock_guard<std::mutex> l(m_);
         done_cv_.notify_all();
       }
@@ -99,23 +107,22 @@ class Pool {
   void loop() {
     uint64_t seen = 0;
     for (;;) {
+      std::shared_ptr<Job> j;
       {
         std::unique_lock<std::mutex> l(m_);
         cv_.wait(l, [&] { return gen_ != seen; });
         seen = gen_;
         if (stop_) return;
-        if (!f_) continue;
+        j = job_;
       }
-      work();
+      if (j) work(*j);
     }
   }
   int n_;
   std::vector<std::thread> workers_;
   std::mutex m_;
   std::condition_variable cv_, done_cv_;
-  const std::function<void(int64_t)>* f_ = nullptr;
-  int64_t total_ = 0;
-  std::atomic<int64_t> next_{0}, done_{0};
+  std::shared_ptr<Job> job_;
   uint64_t gen_ = 0;
   bool stop_ = false;
 };

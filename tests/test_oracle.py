@@ -1,0 +1,71 @@
+"""The CPU oracle (oracle/exec_cpu.cpp, a restatement of the reference's
+src/exec_cpu.rs) is pinned here against the reference itself: golden fixtures
+computed by the reference's PyTorch transcription (tools/reference.py) on the
+same seeded weights and inputs (tests/golden/make_golden.py).
+
+The reference's own bar for its tensor-by-tensor comparison is relative RMS
+<= 1e-4 (tools/compare.py:57); its CPU executor agreed with reference.py to
+~1e-5 max abs on real weights (docs/DEVELOPING.md:213-218). Both sides are
+fp32 with different summation orders, so the match is statistical, not exact.
+Parity of the last ulp of erf/exp is not pinned: the reference's CPU twins of
+those live in an un-vendored dependency; the oracle uses libm.
+"""
+import hashlib
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN_CASES, golden, psnr, rel_rms
+
+
+def weights_digest(params):
+    h = hashlib.sha256()
+    for k in sorted(params):
+        h.update(k.encode())
+        h.update(np.ascontiguousarray(params[k], np.float32).tobytes())
+    return h.hexdigest()
+
+
+@pytest.mark.parametrize("case", GOLDEN_CASES)
+def test_oracle_matches_reference_transcription(case, mx, synth, oracle, checkpoint):
+    z = golden(case)
+    variant, seed, gain, rich = str(z["meta_variant"]), int(z["meta_seed"]), float(z["meta_gain"]), bool(
+        z["meta_rich"])
+    params = synth.make_params(variant, seed, gain, rich)
+    assert weights_digest(params) == str(z["meta_weights_sha256"]), "the synthetic weight generator changed"
+    w = mx.Weights(checkpoint(variant, seed, gain, rich))
+    assert w.variant == variant
+    img = z["input"]
+    plan = mx.Plan(w, img.shape[1], img.shape[2], dumps=True)
+    arena = oracle.run(plan, img)
+    out = oracle.take(plan, arena, plan.output)
+    assert rel_rms(z["final"], out) <= 1e-4
+    assert psnr(z["final"], out) >= 90.0
+    dumps = dict(plan.dumps())
+    for key in z.files:
+        if key.startswith("t/"):
+            got = oracle.take(plan, arena, dumps[key[2:]])
+            assert got.shape == z[key].shape, key
+            assert rel_rms(z[key], got) <= 1e-4, key
+
+
+def test_oracle_is_thread_count_independent(mx, oracle, checkpoint):
+    """Every output element's summation order is fixed by the op, not by the
+    split, so 1 thread and many give identical bits (the reference's own
+    parallel/serial guarantee, src/exec_cpu.rs:1-20)."""
+    z = golden("s2_64_rich")
+    w = mx.Weights(checkpoint("S-2", 5, 0.5, True))
+    plan = mx.Plan(w, 64, 64)
+    a = oracle.output(plan, z["input"], threads=1)
+    b = oracle.output(plan, z["input"], threads=4)
+    assert np.array_equal(a, b)
+
+
+def test_dumps_do_not_change_the_result(mx, oracle, checkpoint):
+    """`tests/packing.rs:54-67`: naming buffers extends their live ranges, and
+    must not change a single bit of the output."""
+    z = golden("s2_64_he")
+    w = mx.Weights(checkpoint("S-2", 0, 1.0, False))
+    named = oracle.output(mx.Plan(w, 64, 64, dumps=True), z["input"])
+    bare = oracle.output(mx.Plan(w, 64, 64, dumps=False), z["input"])
+    assert np.array_equal(named, bare)
