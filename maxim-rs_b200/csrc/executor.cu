@@ -26,9 +26,12 @@
 #include <string>
 #include <vector>
 
+#include <cudaTypedefs.h>
+
 #include "common.h"
 #include "gpu_common.cuh"
 #include "kernels_simt.cuh"
+#include "kernels_umma.cuh"
 #include "maxim_b200.h"
 
 namespace mx {
@@ -99,6 +102,59 @@ struct Step {
   int op;       // plan op index, -1 for the boundary transposes
   int kernels;  // launches it makes
   std::function<void(cudaStream_t)> run;
+  // Runs once after the arena and the weight pool exist (tensor maps need
+  // final device addresses).
+  std::function<void()> prepare;
+};
+
+// Weights split for the 3-pass TF32 products: hi = w rounded to TF32
+// (nearest, ties to even), lo = w - hi (exact in fp32).
+void split_tf32(const std::vector<float>& w, std::vector<float>& hi, std::vector<float>& lo) {
+  hi.resize(w.size());
+  lo.resize(w.size());
+  for (size_t i = 0; i < w.size(); ++i) {
+    uint32_t b;
+    memcpy(&b, &w[i], 4);
+    uint32_t r = (b + 0xFFFu + ((b >> 13) & 1u)) & 0xFFFFE000u;
+    float h;
+    memcpy(&h, &r, 4);
+    if (!std::isfinite(h)) h = w[i];
+    hi[i] = h;
+    lo[i] = w[i] - h;
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    MX_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !p) throw Error("cuTensorMapEncodeTiled is unavailable", MX_E_CUDA);
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// A tiled fp32 tensor map with 128-byte swizzle (the UMMA canonical layout).
+// dims / box innermost first; strides in bytes for dims 1..rank-1.
+CUtensorMap make_tensor_map(const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                            const uint32_t* box) {
+  CUtensorMap m;
+  uint32_t es[5] = {1, 1, 1, 1, 1};
+  CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, cuuint32_t(rank), const_cast<void*>(base),
+                                    dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error(fmt("cuTensorMapEncodeTiled failed (%d)", int(r)), MX_E_CUDA);
+  return m;
+}
+
+// The four tensor maps and the launch parameters of one tensor-core conv.
+struct UmmaOp {
+  CUtensorMap a, b, blo, d;
+  UmmaConvParams p;
+  int n = 0, taps = 1, grid = 0, smem = 0;
 };
 
 }  // namespace
@@ -127,7 +183,11 @@ struct mx_gpu {
   std::vector<float> timeline_ms;
   float timeline_total = 0.0f;
   int64_t kernels = 0;
+  int64_t umma_ops = 0;
   std::string name;
+  int* status = nullptr;  // device status word the tensor-core kernels write
+  int sms = 148;
+  bool use_umma = true;
 };
 
 namespace mx {
@@ -181,6 +241,141 @@ void launch_gemm(cudaStream_t s, const P& p, int batch) {
 void check_launch() {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw Error(std::string("kernel launch: ") + cudaGetErrorString(e), MX_E_CUDA);
+}
+
+// Element offset (into the arena), pixel stride and channel count of a
+// buffer's NHWC view, known before any device memory exists.
+struct ViewMeta {
+  int64_t off, stride, c, npix;
+};
+ViewMeta meta_of(const mx_gpu& g, int32_t id) {
+  int32_t base = root_of(g, id);
+  const mx_buf& b = g.bufs[size_t(id)];
+  int64_t hw = b.h * b.w;
+  int64_t ch0 = hw ? (g.offs[size_t(id)] - g.offs[size_t(base)]) / hw : 0;
+  return {g.offs[size_t(base)] + ch0, g.bufs[size_t(base)].c, b.c, hw};
+}
+
+// Whether a conv runs on the tensor-core kernel: TMA needs 16-byte aligned
+// rows and strides; the kernel takes K in blocks of 32 channels and
+// N = c_out in {32, 64, 128, 256}.
+bool umma_eligible(const mx_gpu& g, const mx_op& o) {
+  if (!g.use_umma) return false;
+  if (o.kind != MX_OP_CONV1X1 && o.kind != MX_OP_CONV3X3) return false;
+  if (o.c_in % 32 != 0) return false;
+  if (o.c_out != 32 && o.c_out != 64 && o.c_out != 128 && o.c_out != 256) return false;
+  ViewMeta x = meta_of(g, o.src), d = meta_of(g, o.dst);
+  if (x.off % 4 || x.stride % 4 || d.off % 4 || d.stride % 4) return false;
+  if (x.c != o.c_in || d.c != o.c_out || x.npix != int64_t(o.h) * o.wd) return false;
+  return true;
+}
+
+template <int N, int TAPS>
+void umma_attr() {
+  MX_CUDA(cudaFuncSetAttribute(umma_conv_kernel<N, TAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               UmmaCfg<N>::SMEM_BYTES));
+}
+void umma_attrs_once() {
+  static bool done = false;
+  if (done) return;
+  umma_attr<32, 1>();
+  umma_attr<64, 1>();
+  umma_attr<128, 1>();
+  umma_attr<256, 1>();
+  umma_attr<32, 9>();
+  umma_attr<64, 9>();
+  umma_attr<128, 9>();
+  umma_attr<256, 9>();
+  done = true;
+}
+int umma_smem(int n) {
+  switch (n) {
+    case 32: return UmmaCfg<32>::SMEM_BYTES;
+    case 64: return UmmaCfg<64>::SMEM_BYTES;
+    case 128: return UmmaCfg<128>::SMEM_BYTES;
+    default: return UmmaCfg<256>::SMEM_BYTES;
+  }
+}
+void launch_umma(cudaStream_t s, const UmmaOp& u) {
+#define MX_UMMA_CASE(NN, TT)                                                                      \
+  if (u.n == NN && u.taps == TT) {                                                                \
+    umma_conv_kernel<NN, TT><<<unsigned(u.grid), 320, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.p);   \
+    return;                                                                                       \
+  }
+  MX_UMMA_CASE(32, 1)
+  MX_UMMA_CASE(64, 1)
+  MX_UMMA_CASE(128, 1)
+  MX_UMMA_CASE(256, 1)
+  MX_UMMA_CASE(32, 9)
+  MX_UMMA_CASE(64, 9)
+  MX_UMMA_CASE(128, 9)
+  MX_UMMA_CASE(256, 9)
+#undef MX_UMMA_CASE
+  throw Error(fmt("no tensor-core kernel for N=%d taps=%d", u.n, u.taps));
+}
+
+// The tensor-core step of a 1x1 or 3x3 conv: split weights into TF32 hi/lo
+// in [c_out][tap][c_in] order, then build the tensor maps once the arena
+// and the pool have their final addresses.
+Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const std::vector<float>& w_ktap,
+                    const std::vector<float>& bias) {
+  const int taps = o.kind == MX_OP_CONV3X3 ? 9 : 1;
+  std::vector<float> hi, lo;
+  split_tf32(w_ktap, hi, lo);
+  const int64_t ho = int64_t(g.pool.put(hi)), lo_off = int64_t(g.pool.put(lo));
+  g.weight_bytes += int64_t(2 * hi.size() * 4);
+  int64_t bo = -1;
+  if (!bias.empty()) {
+    bo = int64_t(g.pool.put(bias));
+    g.weight_bytes += int64_t(bias.size() * 4);
+  }
+  auto u = std::make_shared<UmmaOp>();
+  mx_gpu* G = &g;
+  const mx_op op = o;
+  ++g.umma_ops;
+  Step st{oi, 1, nullptr, nullptr};
+  st.prepare = [G, u, op, taps, ho, lo_off, bo]() {
+    View x = view_of(*G, op.src), d = view_of(*G, op.dst);
+    const int n = op.c_out, ci = op.c_in, H = op.h, W = op.wd;
+    const uint64_t K = uint64_t(taps) * ci;
+    const float* whi = reinterpret_cast<const float*>(G->pool.dev + ho);
+    const float* wlo = reinterpret_cast<const float*>(G->pool.dev + lo_off);
+    {
+      uint64_t dims[2] = {K, uint64_t(n)}, str[1] = {K * 4};
+      uint32_t box[2] = {32, uint32_t(n)};
+      u->b = make_tensor_map(whi, 2, dims, str, box);
+      u->blo = make_tensor_map(wlo, 2, dims, str, box);
+    }
+    if (taps == 1) {
+      uint64_t da[2] = {uint64_t(ci), uint64_t(x.npix)}, sa[1] = {uint64_t(x.stride) * 4};
+      uint32_t ba[2] = {32, 128};
+      u->a = make_tensor_map(x.ptr, 2, da, sa, ba);
+      uint64_t dd[2] = {uint64_t(n), uint64_t(d.npix)}, sd[1] = {uint64_t(d.stride) * 4};
+      u->d = make_tensor_map(d.ptr, 2, dd, sd, ba);
+      u->p.tiles = int((x.npix + 127) / 128);
+      u->p.tiles_x = 0;
+    } else {
+      uint64_t da[3] = {uint64_t(ci), uint64_t(W), uint64_t(H)};
+      uint64_t sa[2] = {uint64_t(x.stride) * 4, uint64_t(W) * uint64_t(x.stride) * 4};
+      uint32_t ba[3] = {32, 16, 8};
+      u->a = make_tensor_map(x.ptr, 3, da, sa, ba);
+      uint64_t dd[3] = {uint64_t(n), uint64_t(W), uint64_t(H)};
+      uint64_t sd[2] = {uint64_t(d.stride) * 4, uint64_t(W) * uint64_t(d.stride) * 4};
+      u->d = make_tensor_map(d.ptr, 3, dd, sd, ba);
+      u->p.tiles_x = (W + 15) / 16;
+      u->p.tiles = u->p.tiles_x * ((H + 7) / 8);
+    }
+    u->p.kb_per_tap = ci / 32;
+    u->p.c_in = ci;
+    u->p.bias = bo < 0 ? nullptr : reinterpret_cast<const float*>(G->pool.dev + bo);
+    u->p.status = G->status;
+    u->n = n;
+    u->taps = taps;
+    u->grid = std::min(u->p.tiles, G->sms);
+    u->smem = umma_smem(n);
+  };
+  st.run = [u](cudaStream_t s) { launch_umma(s, *u); };
+  return st;
 }
 
 // Build the step for one op. Weight layouts are converted here and recorded
@@ -262,6 +457,10 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
       break;
     }
     case MX_OP_CONV1X1: {
+      if (umma_eligible(g, o)) {
+        st = umma_conv_step(g, oi, o, W(o.w), W(o.bias));
+        break;
+      }
       int64_t wo = put(W(o.w)), bo = put(W(o.bias));  // [c_out][c_in]
       int ci = o.c_in, co = o.c_out;
       st.run = [G, P, dst, src, wo, bo, ci, co](cudaStream_t s) {
@@ -283,6 +482,10 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
         for (int ic = 0; ic < ci; ++ic)
           for (int t = 0; t < ks * ks; ++t)
             wt[(size_t(oc) * ks * ks + t) * ci + ic] = w[(size_t(oc) * ci + ic) * ks * ks + t];
+      if (umma_eligible(g, o)) {
+        st = umma_conv_step(g, oi, o, wt, W(o.bias));
+        break;
+      }
       int64_t wo = put(wt), bo = put(W(o.bias));
       int h = o.h, wd = o.wd;
       int oh = ks == 3 ? h : o.oh, ow = ks == 3 ? wd : o.ow;
@@ -421,6 +624,66 @@ void capture_graph(mx_gpu& g) {
 
 int64_t len_of(const mx_buf& b) { return b.c * b.h * b.w; }
 
+// After a synchronisation: a tensor-core kernel that gave up waiting on its
+// own pipeline leaves a nonzero code in the status word. Report and clear it.
+void check_status(mx_gpu& g) {
+  int code = 0;
+  MX_CUDA(cudaMemcpy(&code, g.status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code) {
+    MX_CUDA(cudaMemset(g.status, 0, sizeof(int)));
+    throw Error(fmt("a tensor-core kernel gave up waiting on its pipeline (code 0x%x); its output is invalid", code),
+                MX_E_DEVICE);
+  }
+}
+
+// Every weight an op names must be present with exactly the length the op's
+// layout needs; a plan built without a checkpoint (empty blobs) is refused
+// here rather than read out of bounds.
+void validate_weights(const mx_plan& plan) {
+  auto need = [&](int32_t oi, int32_t id, int64_t n, const char* what) {
+    if (id < 0) return;
+    if (id >= plan.n_weights)
+      throw Error(fmt("op %d: %s names weight %d, past the plan's %d weights", oi, what, id, plan.n_weights));
+    if (plan.weight_lens[id] != n || (n > 0 && !plan.weights[id]))
+      throw Error(fmt("op %d: %s (weight %d) holds %lld values, the op needs %lld - a plan built without a "
+                      "checkpoint cannot run",
+                      oi, what, id, (long long)plan.weight_lens[id], (long long)n));
+  };
+  for (int32_t i = 0; i < plan.n_ops; ++i) {
+    const mx_op& o = plan.ops[i];
+    switch (o.kind) {
+      case MX_OP_CHAN_LN:
+        need(i, o.scale, o.c, "LayerNorm scale");
+        need(i, o.bias, o.c, "LayerNorm bias");
+        break;
+      case MX_OP_CONV1X1:
+        need(i, o.w, int64_t(o.c_in) * o.c_out, "kernel");
+        need(i, o.bias, o.c_out, "bias");
+        break;
+      case MX_OP_CONV3X3:
+        need(i, o.w, int64_t(o.c_in) * o.c_out * 9, "kernel");
+        need(i, o.bias, o.c_out, "bias");
+        break;
+      case MX_OP_CONV4X4S2:
+        need(i, o.w, int64_t(o.c_in) * o.c_out * 16, "kernel");
+        need(i, o.bias, o.c_out, "bias");
+        break;
+      case MX_OP_CONVT2X2:
+        need(i, o.w, int64_t(o.c_in) * o.c_out * 4, "kernel");
+        need(i, o.bias, o.c_out, "bias");
+        break;
+      case MX_OP_GATE_MM: {
+        int64_t n = o.mode == 0 ? o.outer : o.inner;
+        need(i, o.w, n * n, "gating kernel");
+        need(i, o.bias, n, "gating bias");
+        break;
+      }
+      default:
+        break;
+    }
+  }
+}
+
 }  // namespace
 
 const char* describe_kind(int k) {
@@ -475,10 +738,8 @@ int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) {
     g->output = plan->output;
     g->arena_len = plan->arena_len;
     g->shape = plan->shape;
-    for (int32_t i = 0; i < plan->n_ops; ++i)
-      for (int32_t w : {plan->ops[i].w, plan->ops[i].bias, plan->ops[i].scale})
-        if (w >= 0 && (w >= plan->n_weights || (plan->weight_lens[w] > 0 && !plan->weights[w])))
-          throw Error(fmt("op %d names weight %d, which the plan does not carry", i, w));
+    validate_weights(*plan);
+    g->use_umma = std::getenv("MAXIM_NO_UMMA") == nullptr;
     g->step_of_op.assign(size_t(plan->n_ops), -1);
     for (int32_t i = 0; i < plan->n_ops; ++i) plan_op(*g, *plan, i);
     build_boundary_steps(*g);
@@ -512,9 +773,21 @@ int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) {
     g->pool.host.shrink_to_fit();
     MX_CUDA(cudaMalloc(&g->io_in, size_t(len_of(g->bufs[size_t(g->input)]) * 4)));
     MX_CUDA(cudaMalloc(&g->io_out, size_t(len_of(g->bufs[size_t(g->output)]) * 4)));
+    MX_CUDA(cudaMalloc(&g->status, sizeof(int)));
+    MX_CUDA(cudaMemset(g->status, 0, sizeof(int)));
     cudaDeviceProp prop;
     MX_CUDA(cudaGetDeviceProperties(&prop, device));
     g->name = prop.name;
+    g->sms = prop.multiProcessorCount;
+    if (g->umma_ops) {
+      if (prop.major != 10)
+        throw Error(fmt("%s is compute capability %d.%d; this build's tensor-core kernels are sm_100a only",
+                        prop.name, prop.major, prop.minor),
+                    MX_E_NO_DEVICE);
+      umma_attrs_once();
+    }
+    for (auto& st : g->steps)
+      if (st.prepare) st.prepare();
     *out = g.release();
   });
   if (rc != MX_OK && g) mx_gpu_free(g.release());
@@ -531,6 +804,7 @@ void mx_gpu_free(mx_gpu* g) {
   cudaFree(g->pool.dev);
   cudaFree(g->io_in);
   cudaFree(g->io_out);
+  cudaFree(g->status);
   if (g->stream) cudaStreamDestroy(g->stream);
   delete g;
 }
@@ -586,6 +860,7 @@ int mx_gpu_enqueue(mx_gpu* g) {
       MX_CUDA(cudaEventRecord(ev[n], g->stream));
       check_launch();
       MX_CUDA(cudaEventSynchronize(ev[n]));
+      check_status(*g);
       g->timeline_ms.assign(g->ops.size(), 0.0f);
       g->timeline_total = 0.0f;
       for (size_t i = 0; i < n; ++i) {
@@ -617,6 +892,7 @@ int mx_gpu_sync(mx_gpu* g) {
     if (!g) throw Error("mx_gpu_sync: null handle");
     DevicePin pin(g->device);
     MX_CUDA(cudaStreamSynchronize(g->stream));
+    check_status(*g);
   });
 }
 
@@ -639,6 +915,7 @@ int mx_gpu_begin(mx_gpu* g, const float* input) {
     g->steps.front().run(g->stream);
     check_launch();
     MX_CUDA(cudaStreamSynchronize(g->stream));
+    check_status(*g);
   });
 }
 
@@ -650,6 +927,7 @@ int mx_gpu_step_op(mx_gpu* g, int32_t i) {
     if (s >= 0) g->steps[size_t(s)].run(g->stream);
     check_launch();
     MX_CUDA(cudaStreamSynchronize(g->stream));
+    check_status(*g);
   });
 }
 

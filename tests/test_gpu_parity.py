@@ -73,6 +73,31 @@ def test_gpu_per_op_lockstep(mx, oracle, checkpoint):
     assert not bad, bad[:10]
 
 
+def test_gpu_per_op_lockstep_multi_tile(mx, synth, oracle, checkpoint):
+    """The same walk at 256x320: every tensor-core conv now has more output
+    tiles than the GPU has SMs, so each persistent CTA cycles its pipeline
+    stages and both TMEM accumulators several times."""
+    w = mx.Weights(checkpoint("S-1", 7, 0.5, True))
+    img = synth.image_uniform(synth.input_rng(7), 256, 320)
+    plan = mx.Plan(w, 256, 320)
+    gpu = mx.Gpu(plan)
+    gpu.begin(img)
+    arena = oracle.new_arena(plan, img)
+    bad = []
+    for i, op in enumerate(plan.ops()):
+        oracle.run_range(plan, arena, i, i + 1)
+        gpu.step_op(i)
+        cpu = oracle.take(plan, arena, op.dst)
+        got = gpu.read_buf(op.dst)
+        scale = max(float(np.abs(cpu).max()), 1e-6)
+        err = float(np.abs(got.astype(np.float64) - cpu).max())
+        if not err <= 1e-3 * scale:
+            bad.append((i, op.kind, err / scale))
+    assert not bad, bad[:10]
+    out = gpu.run(img)
+    assert psnr(oracle.output(plan, img), out) >= 50.0
+
+
 def test_gpu_read_arena_and_stats(mx, checkpoint):
     z, w, img = golden_setup(mx, checkpoint, "m1_64")
     plan = mx.Plan(w, 64, 64)
@@ -99,11 +124,17 @@ def test_timeline_covers_every_op(mx, checkpoint):
     assert per.shape == (plan.n_ops,) and total > 0 and (per >= 0).all()
 
 
-def test_oversized_pass_is_refused_before_allocating(mx):
+def test_oversized_pass_is_refused_before_allocating(mx, checkpoint):
     """`Gpu::new` sizes the pass and refuses it with the numbers
     (src/exec_gpu.rs:96-146): 16384 x 16384 needs far more than 180 GB."""
-    plan = mx.Plan(variant="S-1", h=16384, w=16384)
+    plan = mx.Plan(mx.Weights(checkpoint("S-1", 11)), 16384, 16384)
     with pytest.raises(mx.MaximError, match="not enough device memory"):
+        mx.Gpu(plan)
+
+
+def test_plan_without_weights_is_refused(mx):
+    plan = mx.Plan(variant="S-1", h=64, w=64)
+    with pytest.raises(mx.MaximError, match="without a checkpoint"):
         mx.Gpu(plan)
 
 
