@@ -153,8 +153,8 @@ CUtensorMap make_tensor_map(const void* base, int rank, const uint64_t* dims, co
 // The four tensor maps and the launch parameters of one tensor-core conv.
 struct UmmaOp {
   CUtensorMap a, b, blo, d;
-  UmmaConvParams p;
-  int n = 0, taps = 1, grid = 0, smem = 0;
+  UmmaConvParams p{};
+  int n = 0, taps = 1, mode = 0, grid = 0, smem = 0;
 };
 
 }  // namespace
@@ -270,22 +270,30 @@ bool umma_eligible(const mx_gpu& g, const mx_op& o) {
   return true;
 }
 
-template <int N, int TAPS>
-void umma_attr() {
-  MX_CUDA(cudaFuncSetAttribute(umma_conv_kernel<N, TAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               UmmaCfg<N>::SMEM_BYTES));
+// Whether a gating matmul runs on the tensor-core kernel.
+bool umma_gate_eligible(const mx_gpu& g, const mx_op& o) {
+  if (!g.use_umma || o.kind != MX_OP_GATE_MM) return false;
+  const int n = o.mode == 0 ? o.outer : o.inner;
+  if (n != 32 && n != 64 && n != 128 && n != 256) return false;
+  if (o.c % 32 != 0) return false;
+  ViewMeta x = meta_of(g, o.src), d = meta_of(g, o.dst);
+  if (x.off % 4 || x.stride % 4 || d.off % 4 || d.stride % 4) return false;
+  if (x.c != o.c || d.c != o.c || x.npix != int64_t(o.outer) * o.inner) return false;
+  return true;
 }
+
+#define MX_UMMA_INSTANCES(X) \
+  X(32, 0) X(64, 0) X(128, 0) X(256, 0) X(32, 1) X(64, 1) X(128, 1) X(256, 1) \
+  X(32, 2) X(64, 2) X(128, 2) X(256, 2) X(32, 3) X(64, 3) X(128, 3) X(256, 3)
+
 void umma_attrs_once() {
   static bool done = false;
   if (done) return;
-  umma_attr<32, 1>();
-  umma_attr<64, 1>();
-  umma_attr<128, 1>();
-  umma_attr<256, 1>();
-  umma_attr<32, 9>();
-  umma_attr<64, 9>();
-  umma_attr<128, 9>();
-  umma_attr<256, 9>();
+#define MX_UMMA_ATTR(NN, MM)                                                                       \
+  MX_CUDA(cudaFuncSetAttribute(umma_conv_kernel<NN, MM>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                               UmmaCfg<NN>::SMEM_BYTES));
+  MX_UMMA_INSTANCES(MX_UMMA_ATTR)
+#undef MX_UMMA_ATTR
   done = true;
 }
 int umma_smem(int n) {
@@ -297,21 +305,77 @@ int umma_smem(int n) {
   }
 }
 void launch_umma(cudaStream_t s, const UmmaOp& u) {
-#define MX_UMMA_CASE(NN, TT)                                                                      \
-  if (u.n == NN && u.taps == TT) {                                                                \
-    umma_conv_kernel<NN, TT><<<unsigned(u.grid), 320, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.p);   \
+#define MX_UMMA_CASE(NN, MM)                                                                      \
+  if (u.n == NN && u.mode == MM) {                                                                \
+    umma_conv_kernel<NN, MM><<<unsigned(u.grid), 320, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.p);   \
     return;                                                                                       \
   }
-  MX_UMMA_CASE(32, 1)
-  MX_UMMA_CASE(64, 1)
-  MX_UMMA_CASE(128, 1)
-  MX_UMMA_CASE(256, 1)
-  MX_UMMA_CASE(32, 9)
-  MX_UMMA_CASE(64, 9)
-  MX_UMMA_CASE(128, 9)
-  MX_UMMA_CASE(256, 9)
+  MX_UMMA_INSTANCES(MX_UMMA_CASE)
 #undef MX_UMMA_CASE
-  throw Error(fmt("no tensor-core kernel for N=%d taps=%d", u.n, u.taps));
+  throw Error(fmt("no tensor-core kernel for N=%d mode=%d", u.n, u.mode));
+}
+
+// The tensor-core step of a gating matmul over a blocked buffer (pixels in
+// block order g * pp + q, NHWC). Block gating (mode 1) contracts q inside a
+// block, grid gating (mode 0) contracts the cell g; A is the activation
+// (MN-major), B = W[a][t] (K-major), D = activation-shaped.
+Step umma_gate_step(mx_gpu& g, int32_t oi, const mx_op& o, const std::vector<float>& w,
+                    const std::vector<float>& bias) {
+  std::vector<float> hi, lo;
+  split_tf32(w, hi, lo);
+  const int64_t ho = int64_t(g.pool.put(hi)), lo_off = int64_t(g.pool.put(lo));
+  g.weight_bytes += int64_t(2 * hi.size() * 4);
+  int64_t bo = -1;
+  if (!bias.empty()) {
+    bo = int64_t(g.pool.put(bias));
+    g.weight_bytes += int64_t(bias.size() * 4);
+  }
+  auto u = std::make_shared<UmmaOp>();
+  mx_gpu* G = &g;
+  const mx_op op = o;
+  ++g.umma_ops;
+  Step st{oi, 1, nullptr, nullptr};
+  st.prepare = [G, u, op, ho, lo_off, bo]() {
+    View x = view_of(*G, op.src), d = view_of(*G, op.dst);
+    const uint64_t gg = uint64_t(op.outer), pp = uint64_t(op.inner), c = uint64_t(op.c);
+    const int n = op.mode == 0 ? op.outer : op.inner;  // the contracted (and produced) axis
+    const float* whi = reinterpret_cast<const float*>(G->pool.dev + ho);
+    const float* wlo = reinterpret_cast<const float*>(G->pool.dev + lo_off);
+    {
+      uint64_t dims[2] = {uint64_t(n), uint64_t(n)}, str[1] = {uint64_t(n) * 4};
+      uint32_t box[2] = {32, uint32_t(n)};
+      u->b = make_tensor_map(whi, 2, dims, str, box);
+      u->blo = make_tensor_map(wlo, 2, dims, str, box);
+    }
+    // dims (channel, q, g), strides ascending: q steps one pixel, g one block.
+    uint64_t dims[3] = {c, pp, gg};
+    uint64_t sa[2] = {uint64_t(x.stride) * 4, pp * uint64_t(x.stride) * 4};
+    uint64_t sd[2] = {uint64_t(d.stride) * 4, pp * uint64_t(d.stride) * 4};
+    uint32_t box[3];
+    if (op.mode == 1) {  // block gating: box (32 channels, 32 q, 4 blocks)
+      box[0] = 32, box[1] = 32, box[2] = 4;
+      u->mode = MODE_GATE;
+      u->p.groups = int(gg);
+    } else {  // grid gating: per-position box (32 channels, 1 q, 32 cells)
+      box[0] = 32, box[1] = 1, box[2] = 32;
+      u->mode = MODE_GATE_GRID;
+      u->p.groups = int(pp);
+    }
+    u->a = make_tensor_map(x.ptr, 3, dims, sa, box);
+    u->d = make_tensor_map(d.ptr, 3, dims, sd, box);
+    u->p.tiles_x = (u->p.groups + 3) / 4;
+    u->p.tiles = u->p.tiles_x * int(c / 32);
+    u->p.kb_per_tap = n / 32;
+    u->p.c_in = n;
+    u->p.bias = bo < 0 ? nullptr : reinterpret_cast<const float*>(G->pool.dev + bo);
+    u->p.status = G->status;
+    u->n = n;
+    u->taps = 1;
+    u->grid = std::min(u->p.tiles, G->sms);
+    u->smem = umma_smem(n);
+  };
+  st.run = [u](cudaStream_t s) { launch_umma(s, *u); };
+  return st;
 }
 
 // The tensor-core step of a 1x1 or 3x3 conv: split weights into TF32 hi/lo
@@ -371,6 +435,7 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const std::vector<flo
     u->p.status = G->status;
     u->n = n;
     u->taps = taps;
+    u->mode = taps == 9 ? MODE_CONV3 : MODE_CONV1;
     u->grid = std::min(u->p.tiles, G->sms);
     u->smem = umma_smem(n);
   };
@@ -517,6 +582,10 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
       break;
     }
     case MX_OP_GATE_MM: {
+      if (umma_gate_eligible(g, o)) {
+        st = umma_gate_step(g, oi, o, W(o.w), W(o.bias));
+        break;
+      }
       int64_t wo = put(W(o.w)), bo = put(W(o.bias));  // [out][in]
       int c = o.c, outer = o.outer, inner = o.inner, mode = o.mode;
       st.run = [G, P, dst, src, wo, bo, c, outer, inner, mode](cudaStream_t s) {

@@ -1,27 +1,39 @@
-// Tensor-core implicit-GEMM convolution for sm_100a: tcgen05.mma kind::tf32
-// with FP32 accumulators in TMEM, operands staged by TMA.
+// Tensor-core contractions for sm_100a: tcgen05.mma kind::tf32 with FP32
+// accumulators in TMEM, operands staged by TMA (no multicast).
 //
-//   D[pixel][co] = bias[co] + sum_{tap, ci} X[pixel + off(tap)][ci] * W[co][tap][ci]
+// One persistent kernel, three problem shapes (MODE):
+//   MODE_CONV1  1x1 conv / Dense:  D[pix][co] = b[co] + sum_ci X[pix][ci] W[co][ci]
+//               M = 128 pixels of the flat pixel axis, K = c_in
+//   MODE_CONV3  3x3 pad-1 conv:    K = (tap, ci); each tap's A block is a
+//               shifted 3-D TMA box (8 rows x 16 columns x 32 channels) whose
+//               out-of-image part TMA fills with zeros - the padding is free
+//   MODE_GATE   gMLP gating Dense over a spatial axis of a blocked buffer:
+//               D[(grp, c)][a] = b[a] + sum_t X[grp, t][c] W[a][t]
+//               (MODE_GATE / MODE_GATE_GRID)
+//               M = 4 groups x 32 channels, N = a, K = t. The activation is
+//               the MN-major operand: for each t, 32 channels are contiguous
+//               in NHWC, which is one 128-byte row of the canonical SW128
+//               MN-major atom; the 3-D box (32 ch, 32 t, 4 groups) lands
+//               exactly in that layout. Block gating (t = position inside a
+//               block) and grid gating (t = the cell) differ only in the
+//               tensor map's strides.
 //
-// covers the 1x1 convs / Dense channel mixing (TAPS = 1, pixels as a flat
-// M axis) and the 3x3 pad-1 convs (TAPS = 9, 8x16-pixel tiles, each tap a
-// shifted 3-D TMA box whose out-of-image part TMA fills with zeros - the
-// padding costs nothing).
-//
-// Precision: each product is computed as a 3-pass TF32 split,
+// Precision: every product is a 3-pass TF32 split,
 //   a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi,
 // with a_hi exactly representable in TF32 (low 13 mantissa bits cleared) and
-// a_lo = a - a_hi, so the sum carries ~21 significant bits per product and
-// accumulates in FP32 - the fp32 accuracy class the parity bars need (plain
-// TF32 measured 46-48 dB against the fp32 CPU path under the He-normal init,
-// below the 50 dB bar). The weights' hi / lo pair is split on the host.
+// a_lo = a - a_hi, so each product carries ~21 significant bits and all of
+// them accumulate in FP32 - the fp32 accuracy class the parity bars need
+// (plain TF32 measured 46-48 dB against the fp32 CPU path under the
+// He-normal init, below the 50 dB bar). Weights are split on the host.
 //
 // Warp roles (320 threads, one CTA per SM, persistent over output tiles):
-//   warp 0      TMA producer: A box (16 KB), B and B_lo blocks per k-block
+//   warp 0      TMA producer: A block (16 KB), B and B_lo blocks per k-block
 //   warp 1      TMEM owner and MMA issuer (one thread)
 //   warps 2-5   split: A -> (A_hi in place, A_lo beside it) per k-block
 //   warps 6-9   epilogue: TMEM -> registers -> +bias -> swizzled smem -> TMA store
 // Two TMEM accumulators let the epilogue of tile i overlap the MMAs of i+1.
+// Every mbarrier wait is bounded in time; a wait that runs out records a code
+// in the status word, the kernel unwinds and frees its TMEM.
 #pragma once
 
 #include <cuda.h>
@@ -30,12 +42,19 @@
 
 namespace mx {
 
+// MODE_GATE: block gating (t = position inside a block, groups = blocks);
+// MODE_GATE_GRID: grid gating (t = the cell, groups = positions in a cell).
+// The grid case loads and stores its 4 groups as 4 separate boxes so every
+// tensor map keeps its strides in ascending order.
+enum : int { MODE_CONV1 = 0, MODE_CONV3 = 1, MODE_GATE = 2, MODE_GATE_GRID = 3 };
+
 struct UmmaConvParams {
-  int tiles;       // output tiles (128 pixels each)
-  int tiles_x;     // TAPS == 9: tiles per image row (width / 16)
-  int kb_per_tap;  // c_in / 32
-  int c_in;
-  const float* bias;  // [c_out] or null
+  int tiles;       // output tiles
+  int tiles_x;     // CONV3: tiles per image row (width / 16); GATE: group tiles (ceil(groups / 4))
+  int kb_per_tap;  // k-blocks (of 32) per tap
+  int c_in;        // K per tap (CONV) / K (GATE)
+  int groups;      // GATE_GRID: positions per cell (boxes past it are skipped)
+  const float* bias;  // per output column, or null
   int* status;        // device status word (0 = ok)
 };
 
@@ -58,13 +77,14 @@ enum : int {
   kErrEpilogue = 0x105,
 };
 
-template <int N, int TAPS>
+template <int N, int MODE>
 __global__ void __launch_bounds__(320, 1)
     umma_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmD,
                      UmmaConvParams p) {
   using C = UmmaCfg<N>;
   using namespace sm100;
+  constexpr int TAPS = MODE == MODE_CONV3 ? 9 : 1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = base + C::STAGES * C::STAGE_BYTES;
@@ -79,6 +99,20 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = TAPS * p.kb_per_tap;
+
+  // Tile t -> its origin: CONV1 (m0), CONV3 (x0, y0), GATE (group g0, channel block cc).
+  auto decode = [&](int t, int& a0, int& a1) {
+    if (MODE == MODE_CONV1) {
+      a0 = t * 128;
+      a1 = 0;
+    } else if (MODE == MODE_CONV3) {
+      a0 = (t % p.tiles_x) * 16;
+      a1 = (t / p.tiles_x) * 8;
+    } else {
+      a0 = (t % p.tiles_x) * 4;  // first group of the tile
+      a1 = (t / p.tiles_x) * 32;  // first channel
+    }
+  };
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -116,13 +150,8 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       uint32_t it = 0;
       for (int t = blockIdx.x; t < p.tiles && !*vabort; t += gridDim.x) {
-        int m0 = 0, x0 = 0, y0 = 0;
-        if (TAPS == 1) {
-          m0 = t * 128;
-        } else {
-          y0 = (t / p.tiles_x) * 8;
-          x0 = (t % p.tiles_x) * 16;
-        }
+        int a0, a1;
+        decode(t, a0, a1);
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
@@ -132,12 +161,23 @@ __global__ void __launch_bounds__(320, 1)
           }
           uint8_t* st = base + s * C::STAGE_BYTES;
           const int tap = kb / p.kb_per_tap, cb = kb % p.kb_per_tap;
-          mbar_arrive_expect_tx(&full[s], C::A_BYTES + 2 * C::B_BYTES);
-          if (TAPS == 1) {
-            tma_load_2d(st, &tmA, &full[s], cb * 32, m0);
-          } else {
+          int a_bytes = C::A_BYTES;
+          if (MODE == MODE_GATE_GRID) a_bytes = 4096 * min(4, p.groups - a0);
+          mbar_arrive_expect_tx(&full[s], a_bytes + 2 * C::B_BYTES);
+          if (MODE == MODE_CONV1) {
+            tma_load_2d(st, &tmA, &full[s], cb * 32, a0);
+          } else if (MODE == MODE_CONV3) {
             const int ky = tap / 3, kx = tap % 3;
-            tma_load_3d(st, &tmA, &full[s], cb * 32, x0 + kx - 1, y0 + ky - 1);
+            tma_load_3d(st, &tmA, &full[s], cb * 32, a0 + kx - 1, a1 + ky - 1);
+          } else if (MODE == MODE_GATE) {
+            tma_load_3d(st, &tmA, &full[s], a1, kb * 32, a0);
+          } else {
+            // A box past the last position would read nothing; its rows
+            // only feed accumulator rows that are never stored, so it is
+            // skipped and the expected byte count below counts only real boxes.
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+              if (a0 + g < p.groups) tma_load_3d(st + g * 4096, &tmA, &full[s], a1, a0 + g, kb * 32);
           }
           const int kcol = tap * p.c_in + cb * 32;
           tma_load_2d(st + 2 * C::A_BYTES, &tmB, &full[s], kcol, 0);
@@ -148,7 +188,8 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(128, N, 0, 0);
+      constexpr bool GATE = MODE == MODE_GATE || MODE == MODE_GATE_GRID;
+      constexpr uint32_t idesc = idesc_tf32(128, N, GATE ? 1 : 0, 0);
       uint32_t it = 0, tc = 0;
       for (int t = blockIdx.x; t < p.tiles && !*vabort; t += gridDim.x, ++tc) {
         const uint32_t acc = tc & 1, aph = (tc >> 1) & 1;
@@ -172,7 +213,15 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t alo = a + C::A_BYTES, b = a + 2 * C::A_BYTES, blo = b + C::B_BYTES;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint64_t da = desc_kmajor_sw128(a + 32 * k), dalo = desc_kmajor_sw128(alo + 32 * k);
+            uint64_t da, dalo;
+            if (GATE) {
+              // MN-major: k-step k covers K rows 8k..8k+7 of each 4 KB group block.
+              da = desc_mnmajor_sw128(a + 1024 * k, 4096);
+              dalo = desc_mnmajor_sw128(alo + 1024 * k, 4096);
+            } else {
+              da = desc_kmajor_sw128(a + 32 * k);
+              dalo = desc_kmajor_sw128(alo + 32 * k);
+            }
             const uint64_t db = desc_kmajor_sw128(b + 32 * k), dblo = desc_kmajor_sw128(blo + 32 * k);
             mma_tf32(d, dalo, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
             mma_tf32(d, da, dblo, idesc, 1u);
@@ -223,7 +272,7 @@ __global__ void __launch_bounds__(320, 1)
     // ------------------------------------------------------------ epilogue
     const int et = threadIdx.x - 192;  // 0..127
     const int q = warp & 3;            // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;     // tile row (pixel) this thread owns
+    const int row = q * 32 + lane;     // accumulator row this thread owns
     uint32_t tc = 0;
     int chunk = 0;
     for (int t = blockIdx.x; t < p.tiles && !*vabort; t += gridDim.x, ++tc) {
@@ -233,13 +282,8 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       tc_fence_after();
-      int m0 = 0, x0 = 0, y0 = 0;
-      if (TAPS == 1) {
-        m0 = t * 128;
-      } else {
-        y0 = (t / p.tiles_x) * 8;
-        x0 = (t % p.tiles_x) * 16;
-      }
+      int a0, a1;
+      decode(t, a0, a1);
 #pragma unroll 1
       for (int j = 0; j < N / 32; ++j, ++chunk) {
         float v[32];
@@ -257,14 +301,31 @@ __global__ void __launch_bounds__(320, 1)
         }
         uint8_t* sb = staging + (chunk & 1) * (128 * 128);
         named_bar(1, 128);  // the buffer's previous store has been read (see below)
-        float4* rowp = reinterpret_cast<float4*>(sb + row * 128);
+        if (MODE == MODE_GATE || MODE == MODE_GATE_GRID) {
+          // Staging is [group][a][channel]: this thread (group q, channel
+          // lane) writes one float into each of its group's 32 rows.
+          float* g = reinterpret_cast<float*>(sb + q * 4096);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) rowp[i ^ (row & 7)] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          for (int i = 0; i < 32; ++i) {
+            const int r = q * 32 + i;  // row within the 128-row staging tile
+            g[i * 32 + (((lane >> 2) ^ (r & 7)) << 2) + (lane & 3)] = v[i];
+          }
+        } else {
+          float4* rowp = reinterpret_cast<float4*>(sb + row * 128);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            rowp[i ^ (row & 7)] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
         fence_proxy_async_smem();
         named_bar(1, 128);
         if (et == 0) {
-          if (TAPS == 1) tma_store_2d(&tmD, sb, j * 32, m0);
-          else tma_store_3d(&tmD, sb, j * 32, x0, y0);
+          if (MODE == MODE_CONV1) tma_store_2d(&tmD, sb, j * 32, a0);
+          else if (MODE == MODE_CONV3) tma_store_3d(&tmD, sb, j * 32, a0, a1);
+          else if (MODE == MODE_GATE) tma_store_3d(&tmD, sb, a1, j * 32, a0);
+          else
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+              if (a0 + g < p.groups) tma_store_3d(&tmD, sb + g * 4096, a1, a0 + g, j * 32);
           bulk_commit();
           bulk_wait_read<1>();
         }
