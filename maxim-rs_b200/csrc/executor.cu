@@ -139,13 +139,12 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // A tiled fp32 tensor map with 128-byte swizzle (the UMMA canonical layout).
 // dims / box innermost first; strides in bytes for dims 1..rank-1.
 CUtensorMap make_tensor_map(const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
-                            const uint32_t* box) {
+                            const uint32_t* box, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   CUtensorMap m;
   uint32_t es[5] = {1, 1, 1, 1, 1};
   CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, cuuint32_t(rank), const_cast<void*>(base),
-                                    dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                                    dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw Error(fmt("cuTensorMapEncodeTiled failed (%d)", int(r)), MX_E_CUDA);
   return m;
 }
@@ -361,7 +360,9 @@ Step umma_gate_step(mx_gpu& g, int32_t oi, const mx_op& o, const std::vector<flo
       u->mode = MODE_GATE_GRID;
       u->p.groups = int(pp);
     }
-    u->a = make_tensor_map(x.ptr, 3, dims, sa, box);
+    // The activation is the MN-major operand: 32-byte-atom swizzle (see
+    // desc_mnmajor_sw128_32b). The output staging is plain 128-byte swizzle.
+    u->a = make_tensor_map(x.ptr, 3, dims, sa, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     u->d = make_tensor_map(d.ptr, 3, dims, sd, box);
     u->p.tiles_x = (u->p.groups + 3) / 4;
     u->p.tiles = u->p.tiles_x * int(c / 32);

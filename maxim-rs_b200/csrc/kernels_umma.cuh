@@ -216,8 +216,8 @@ __global__ void __launch_bounds__(320, 1)
             uint64_t da, dalo;
             if (GATE) {
               // MN-major: k-step k covers K rows 8k..8k+7 of each 4 KB group block.
-              da = desc_mnmajor_sw128(a + 1024 * k, 4096);
-              dalo = desc_mnmajor_sw128(alo + 1024 * k, 4096);
+              da = desc_mnmajor_sw128_32b(a + 1024 * k, 4096);
+              dalo = desc_mnmajor_sw128_32b(alo + 1024 * k, 4096);
             } else {
               da = desc_kmajor_sw128(a + 32 * k);
               dalo = desc_kmajor_sw128(alo + 32 * k);

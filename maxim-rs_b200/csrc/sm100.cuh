@@ -183,16 +183,20 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t addr) {
   d |= uint64_t(2) << 61;                 // SWIZZLE_128B
   return d;
 }
-// The same for an MN-major operand: 128-byte rows of 32 fp32 along MN, one
-// row per K index, 8 K-rows per 1024-byte atom; `lbo` is the byte distance
-// between consecutive 32-wide MN chunks.
-__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t addr, uint32_t lbo) {
+// An MN-major TF32 operand. The only shared-memory layout tcgen05 accepts
+// for a 32-bit MN-major operand is the 128-byte swizzle with 32-byte
+// atomicity (layout type 1): 128-byte rows of 32 fp32 along MN, one row per
+// K index, 4 K-rows per 512-byte atom, 32-byte chunks XOR-permuted by the row
+// index (what TMA writes with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B). `lbo` is
+// the byte distance between consecutive 32-wide MN chunks; consecutive
+// 4-row atoms along K are 512 bytes apart.
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128_32b(uint32_t addr, uint32_t lbo) {
   uint64_t d = 0;
   d |= uint64_t((addr >> 4) & 0x3FFF);
   d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
-  d |= uint64_t(1024 >> 4) << 32;
+  d |= uint64_t(512 >> 4) << 32;
   d |= uint64_t(1) << 46;
-  d |= uint64_t(2) << 61;
+  d |= uint64_t(1) << 61;  // SWIZZLE_128B_BASE32B
   return d;
 }
 // Instruction descriptor: kind::tf32, FP32 accumulate, M x N, operand majors.
