@@ -247,10 +247,13 @@ __global__ void __launch_bounds__(320, 1)
           ok = false;
           break;
         }
-        float4* a = reinterpret_cast<float4*>(base + s * C::STAGE_BYTES) + tid * 8;
-        float4* alo = reinterpret_cast<float4*>(base + s * C::STAGE_BYTES + C::A_BYTES) + tid * 8;
+        // Elementwise, so the layout does not matter; a warp touches 32
+        // consecutive float4 (512 contiguous bytes) per access, which keeps
+        // every shared-memory access free of bank conflicts.
+        float4* a = reinterpret_cast<float4*>(base + s * C::STAGE_BYTES) + tid;
+        float4* alo = reinterpret_cast<float4*>(base + s * C::STAGE_BYTES + C::A_BYTES) + tid;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 8 * 128; i += 128) {
           float4 v = a[i], h, l;
           h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
           h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
