@@ -31,6 +31,7 @@
 #include "common.h"
 #include "gpu_common.cuh"
 #include "kernels_simt.cuh"
+#include "kernels_mem.cuh"
 #include "kernels_umma.cuh"
 #include "maxim_b200.h"
 
@@ -187,6 +188,8 @@ struct mx_gpu {
   int* status = nullptr;  // device status word the tensor-core kernels write
   int sms = 148;
   bool use_umma = true;
+  float* scratch = nullptr;  // per-op scratch (the channel-mean partial sums)
+  int64_t scratch_len = 0;   // floats
 };
 
 namespace mx {
@@ -498,27 +501,57 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
       int64_t ws = put(W(o.scale)), wb = put(W(o.bias));
       st.run = [G, P, dst, src, ws, wb](cudaStream_t s) {
         View d = view_of(*G, dst), x = view_of(*G, src);
-        if (aligned4(d) && aligned4(x))
-          chan_ln_kernel4<<<blocks_for(x.npix, 128), 128, 0, s>>>(x.npix, int(x.c), x.ptr, x.stride, P(ws), P(wb),
-                                                                  d.ptr, d.stride, kLnEps);
-        else
-          chan_ln_kernel1<<<blocks_for(x.npix, 128), 128, 0, s>>>(x.npix, int(x.c), x.ptr, x.stride, P(ws), P(wb),
-                                                                  d.ptr, d.stride, kLnEps);
+        const int c = int(x.c), np = int(x.npix);
+        if (aligned4(d) && aligned4(x) && (c == 32 || c == 64 || c == 128 || c == 256)) {
+          const int pb = c <= 64 ? 128 : (c == 128 ? 64 : 32);
+          const unsigned grid = unsigned((np + pb - 1) / pb);
+          const size_t smem = size_t(pb) * (c + 1) * sizeof(float);
+          const int sx = int(x.stride), sy = int(d.stride);
+          if (c == 32) chan_ln_tile_kernel<32><<<grid, 128, smem, s>>>(np, x.ptr, sx, P(ws), P(wb), d.ptr, sy, kLnEps);
+          else if (c == 64) chan_ln_tile_kernel<64><<<grid, 128, smem, s>>>(np, x.ptr, sx, P(ws), P(wb), d.ptr, sy, kLnEps);
+          else if (c == 128) chan_ln_tile_kernel<128><<<grid, 128, smem, s>>>(np, x.ptr, sx, P(ws), P(wb), d.ptr, sy, kLnEps);
+          else chan_ln_tile_kernel<256><<<grid, 128, smem, s>>>(np, x.ptr, sx, P(ws), P(wb), d.ptr, sy, kLnEps);
+        } else if (aligned4(d) && aligned4(x)) {
+          chan_ln_kernel4<<<blocks_for(x.npix, 128), 128, 0, s>>>(x.npix, c, x.ptr, x.stride, P(ws), P(wb), d.ptr,
+                                                                  d.stride, kLnEps);
+        } else {
+          chan_ln_kernel1<<<blocks_for(x.npix, 128), 128, 0, s>>>(x.npix, c, x.ptr, x.stride, P(ws), P(wb), d.ptr,
+                                                                  d.stride, kLnEps);
+        }
       };
       break;
     }
     case MX_OP_CHAN_MEAN: {
-      st.run = [G, dst, src](cudaStream_t s) {
+      // Two phases over a scratch of per-block partial sums (deterministic).
+      const int64_t npix = int64_t(o.hw);
+      const int nb = int(std::max<int64_t>(1, std::min<int64_t>((npix + 511) / 512, 1024)));
+      const int per = int((npix + nb - 1) / nb);
+      g.scratch_len = std::max<int64_t>(g.scratch_len, int64_t(nb) * o.c);
+      st.kernels = 2;
+      st.run = [G, dst, src, nb, per](cudaStream_t s) {
         View d = view_of(*G, dst), x = view_of(*G, src);
-        chan_mean_kernel<<<unsigned(x.c), 512, 0, s>>>(x.npix, x.ptr, x.stride, d.ptr);
+        if (aligned4(x) && x.c <= 1024) {
+          const int c4 = int(x.c / 4);
+          chan_mean_partial_kernel<<<unsigned(nb), 256, 0, s>>>(int(x.npix), c4, per, x.ptr, int(x.stride),
+                                                                G->scratch);
+          chan_mean_final_kernel<<<blocks_for(x.c, 128), 128, 0, s>>>(nb, int(x.c), int(x.npix), G->scratch, d.ptr);
+        } else {
+          chan_mean_kernel<<<unsigned(x.c), 512, 0, s>>>(x.npix, x.ptr, x.stride, d.ptr);
+        }
       };
       break;
     }
     case MX_OP_CHAN_SCALE: {
       st.run = [G, dst, src, src2](cudaStream_t s) {
         View d = view_of(*G, dst), x = view_of(*G, src), sc = view_of(*G, src2);
-        chan_scale_kernel<<<blocks_for(x.npix * x.c, TPB), TPB, 0, s>>>(x.npix, int(x.c), x.ptr, x.stride, sc.ptr,
-                                                                        d.ptr, d.stride);
+        if (aligned4(d) && aligned4(x) && aligned4(sc)) {
+          const int c4 = int(x.c / 4), total4 = int(x.npix) * c4;
+          chan_scale4_kernel<<<blocks_for(total4, TPB), TPB, 0, s>>>(total4, c4, x.ptr, int(x.stride), sc.ptr, d.ptr,
+                                                                     int(d.stride));
+        } else {
+          chan_scale_kernel<<<blocks_for(x.npix * x.c, TPB), TPB, 0, s>>>(x.npix, int(x.c), x.ptr, x.stride, sc.ptr,
+                                                                          d.ptr, d.stride);
+        }
       };
       break;
     }
@@ -610,6 +643,13 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
                         oi, o.gh * o.fh, o.gw * o.fw, o.h, o.wd));
       st.run = [G, op](cudaStream_t s) {
         View d = view_of(*G, op.dst), x = view_of(*G, op.src);
+        if (aligned4(d) && aligned4(x)) {
+          const int c4 = op.c / 4, total4 = op.h * op.wd * c4;
+          block_perm4_kernel<<<blocks_for(total4, TPB), TPB, 0, s>>>(total4, c4, op.wd, op.gw, op.fh, op.fw,
+                                                                     op.gh * op.gw, op.fh * op.fw, op.swap, op.forward,
+                                                                     x.ptr, int(x.stride), d.ptr, int(d.stride));
+          return;
+        }
         int64_t total = int64_t(op.h) * op.wd * op.c;
         block_perm_kernel<<<blocks_for(total, TPB), TPB, 0, s>>>(total, op.c, op.wd, op.gw, op.fh, op.fw,
                                                                  op.gh * op.gw, op.fh * op.fw, op.swap, op.forward,
@@ -641,6 +681,17 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
         auto I = [G](int64_t off) { return reinterpret_cast<const int*>(G->pool.dev + off); };
         auto F = [G](int64_t off) { return reinterpret_cast<const float*>(G->pool.dev + off); };
         View d = view_of(*G, op.dst), x = view_of(*G, op.src), t = view_of(*G, op.tmp);
+        if (aligned4(d) && aligned4(x) && aligned4(t)) {
+          TapTable4 TX{I(tx_j0), I(tx_w0), I(tx_c), F(tx_w), F(tx_s)};
+          TapTable4 TY{I(ty_j0), I(ty_w0), I(ty_c), F(ty_w), F(ty_s)};
+          const int c4 = op.c / 4;
+          const int t1 = op.hin * op.wout * c4, t2 = op.hout * op.wout * c4;
+          resize_h4_kernel<<<blocks_for(t1, TPB), TPB, 0, s>>>(t1, c4, op.win, op.wout, TX, x.ptr, int(x.stride),
+                                                               t.ptr, int(t.stride));
+          resize_v4_kernel<<<blocks_for(t2, TPB), TPB, 0, s>>>(t2, c4, op.wout, TY, t.ptr, int(t.stride), d.ptr,
+                                                               int(d.stride));
+          return;
+        }
         TapTable TX{I(tx_j0), I(tx_w0), I(tx_c), F(tx_w), F(tx_s)};
         TapTable TY{I(ty_j0), I(ty_w0), I(ty_c), F(ty_w), F(ty_s)};
         int64_t t1 = int64_t(op.hin) * op.wout * op.c;
@@ -821,7 +872,11 @@ int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) {
     MX_CUDA(cudaMemGetInfo(&free_b, &total_b));
     int64_t arena_bytes = plan->arena_len * 4;
     int64_t io_bytes = (len_of(g->bufs[size_t(g->input)]) + len_of(g->bufs[size_t(g->output)])) * 4;
-    int64_t need = arena_bytes + int64_t(g->pool.size()) + io_bytes;
+    for (const mx_buf& b : g->bufs)
+      if (len_of(b) >= (int64_t(1) << 31))
+        throw Error(fmt("a %lldx%lldx%lld activation has 2^31 or more elements; images this large are not supported",
+                        (long long)b.c, (long long)b.h, (long long)b.w));
+    int64_t need = arena_bytes + int64_t(g->pool.size()) + io_bytes + g->scratch_len * 4;
     if (need > int64_t(free_b))
       throw Error(fmt("not enough device memory for a %lldx%lld pass\n"
                       "maxim: the arena needs %lld MiB and the weights %lld MiB; %lld MiB is free\n"
@@ -843,6 +898,7 @@ int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) {
     g->pool.host.shrink_to_fit();
     MX_CUDA(cudaMalloc(&g->io_in, size_t(len_of(g->bufs[size_t(g->input)]) * 4)));
     MX_CUDA(cudaMalloc(&g->io_out, size_t(len_of(g->bufs[size_t(g->output)]) * 4)));
+    if (g->scratch_len > 0) MX_CUDA(cudaMalloc(&g->scratch, size_t(g->scratch_len) * 4));
     MX_CUDA(cudaMalloc(&g->status, sizeof(int)));
     MX_CUDA(cudaMemset(g->status, 0, sizeof(int)));
     cudaDeviceProp prop;
@@ -875,6 +931,7 @@ void mx_gpu_free(mx_gpu* g) {
   cudaFree(g->io_in);
   cudaFree(g->io_out);
   cudaFree(g->status);
+  cudaFree(g->scratch);
   if (g->stream) cudaStreamDestroy(g->stream);
   delete g;
 }

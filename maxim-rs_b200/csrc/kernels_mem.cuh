@@ -1,0 +1,196 @@
+// Memory-bound op kernels, vectorised: every thread moves 16 bytes per access
+// and consecutive threads touch consecutive addresses, with 32-bit index
+// arithmetic (every tensor here has fewer than 2^31 elements; the host checks).
+//
+// These take the executor's NHWC views when channels come in multiples of 4
+// and views are 16-byte aligned; the scalar kernels in kernels_simt.cuh cover
+// everything else.
+#pragma once
+
+#include "gpu_common.cuh"
+
+namespace mx {
+
+// Space <-> blocked permutation of whole pixels, 4 channels per thread
+// (src/exec_cpu.rs:1078-1103; blocked index e = g * psz + q).
+__global__ void block_perm4_kernel(int total4, int c4, int wd, int gw, int fh, int fw, int gsz, int psz, int swap,
+                                   int forward, const float* __restrict__ src, int ss, float* __restrict__ dst,
+                                   int sd) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total4) return;
+  int e = i / c4;
+  int ch = (i - e * c4) * 4;
+  int g, q;
+  if (swap) {
+    q = e / gsz;
+    g = e - q * gsz;
+  } else {
+    g = e / psz;
+    q = e - g * psz;
+  }
+  int gy = g / gw, gx = g - gy * gw, fy = q / fw, fx = q - fy * fw;
+  int pix = (gy * fh + fy) * wd + gx * fw + fx;
+  if (forward)
+    *reinterpret_cast<float4*>(dst + size_t(e) * sd + ch) =
+        *reinterpret_cast<const float4*>(src + size_t(pix) * ss + ch);
+  else
+    *reinterpret_cast<float4*>(dst + size_t(pix) * sd + ch) =
+        *reinterpret_cast<const float4*>(src + size_t(e) * ss + ch);
+}
+
+// Channel LayerNorm of P pixels per 128-thread block. The block's pixels are
+// staged through shared memory (rows padded to C+1 floats so a thread walking
+// its own row is conflict-free), then each pixel's statistics are taken
+// serially in channel order - the reference's exact order (s1, s2 ascending,
+// m = s1/c, var = s2/c - m*m, rstd = 1/sqrt(max(var,0)+eps),
+// y = (x-m)*rstd*w + b; src/exec_cpu.rs:396-433) - with non-contracting
+// intrinsics, so the result is bit-identical to the CPU path.
+template <int C>
+__global__ void __launch_bounds__(128) chan_ln_tile_kernel(int npix, const float* __restrict__ x, int sx,
+                                                           const float* __restrict__ w, const float* __restrict__ b,
+                                                           float* __restrict__ y, int sy, float eps) {
+  constexpr int P = C <= 64 ? 128 : (C == 128 ? 64 : 32);
+  constexpr int C4 = C / 4, R = C + 1;
+  extern __shared__ float tile[];  // P * R
+  const int p0 = blockIdx.x * P;
+  const int np = min(P, npix - p0);
+  for (int idx = threadIdx.x; idx < np * C4; idx += 128) {
+    int r = idx / C4, c = (idx - r * C4) * 4;
+    float4 v = *reinterpret_cast<const float4*>(x + size_t(p0 + r) * sx + c);
+    float* t = tile + r * R + c;
+    t[0] = v.x;
+    t[1] = v.y;
+    t[2] = v.z;
+    t[3] = v.w;
+  }
+  __syncthreads();
+  if (threadIdx.x < np) {
+    float* t = tile + threadIdx.x * R;
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll 8
+    for (int i = 0; i < C; ++i) {
+      float v = t[i];
+      s1 = __fadd_rn(s1, v);
+      s2 = __fadd_rn(s2, __fmul_rn(v, v));
+    }
+    const float nf = float(C);
+    float m = __fdiv_rn(s1, nf);
+    float var = __fsub_rn(__fdiv_rn(s2, nf), __fmul_rn(m, m));
+    float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(fmaxf(var, 0.0f), eps)));
+#pragma unroll 8
+    for (int i = 0; i < C; ++i) t[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(t[i], m), rstd), __ldg(w + i)), __ldg(b + i));
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < np * C4; idx += 128) {
+    int r = idx / C4, c = (idx - r * C4) * 4;
+    const float* t = tile + r * R + c;
+    *reinterpret_cast<float4*>(y + size_t(p0 + r) * sy + c) = make_float4(t[0], t[1], t[2], t[3]);
+  }
+}
+
+// Per-channel mean over the pixels (the CALayer squeeze) in two deterministic
+// phases: block b sums its own pixel range per channel into part[b][c];
+// then one thread per channel adds the blocks' partials in block order.
+// 256 threads = R pixel rows x C4 channel quads.
+__global__ void __launch_bounds__(256) chan_mean_partial_kernel(int npix, int c4, int per_block,
+                                                                const float* __restrict__ x, int sx,
+                                                                float* __restrict__ part) {
+  __shared__ float4 red[256];
+  const int rows = 256 / c4;
+  const int r = threadIdx.x / c4, q = threadIdx.x - r * c4;
+  const int p0 = blockIdx.x * per_block, p1 = min(npix, p0 + per_block);
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (r < rows)
+    for (int p = p0 + r; p < p1; p += rows) {
+      float4 v = *reinterpret_cast<const float4*>(x + size_t(p) * sx + q * 4);
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+  red[threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.x < c4) {
+    float4 t = red[threadIdx.x];
+    for (int k = 1; k < rows; ++k) {
+      float4 u = red[k * c4 + threadIdx.x];
+      t.x += u.x;
+      t.y += u.y;
+      t.z += u.z;
+      t.w += u.w;
+    }
+    *reinterpret_cast<float4*>(part + size_t(blockIdx.x) * c4 * 4 + threadIdx.x * 4) = t;
+  }
+}
+
+__global__ void chan_mean_final_kernel(int nblocks, int c, int npix, const float* __restrict__ part,
+                                       float* __restrict__ out) {
+  int ch = blockIdx.x * blockDim.x + threadIdx.x;
+  if (ch >= c) return;
+  float s = 0.0f;
+  for (int b = 0; b < nblocks; ++b) s += part[size_t(b) * c + ch];
+  out[ch] = s / float(npix);
+}
+
+// out[p][c] = x[p][c] * s[c], 4 channels per thread.
+__global__ void chan_scale4_kernel(int total4, int c4, const float* __restrict__ x, int sx,
+                                   const float* __restrict__ s, float* __restrict__ d, int sd) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total4) return;
+  int p = i / c4, c = (i - p * c4) * 4;
+  float4 v = *reinterpret_cast<const float4*>(x + size_t(p) * sx + c);
+  float4 g = *reinterpret_cast<const float4*>(s + c);
+  *reinterpret_cast<float4*>(d + size_t(p) * sd + c) = make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w);
+}
+
+// Resize passes, 4 channels per thread, same tap tables and the same
+// per-channel arithmetic as the scalar kernels (acc over taps ascending with
+// non-contracting ops, then acc / wsum if wsum > 0).
+struct TapTable4 {
+  const int* j0;
+  const int* w0;
+  const int* cnt;
+  const float* w;
+  const float* wsum;
+};
+
+__device__ __forceinline__ void tap_acc(float4& acc, float w, float4 v) {
+  acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
+  acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
+  acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
+  acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+}
+__device__ __forceinline__ float4 tap_norm(float4 acc, float sm) {
+  if (sm > 0.0f)
+    return make_float4(__fdiv_rn(acc.x, sm), __fdiv_rn(acc.y, sm), __fdiv_rn(acc.z, sm), __fdiv_rn(acc.w, sm));
+  return acc;
+}
+
+__global__ void resize_h4_kernel(int total4, int c4, int win, int wout, TapTable4 t, const float* __restrict__ src,
+                                 int ss, float* __restrict__ dst, int sd) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total4) return;  // total4 = rows * wout * c4
+  int p = i / c4, c = (i - p * c4) * 4;
+  int row = p / wout, xo = p - row * wout;
+  int j0 = __ldg(t.j0 + xo), w0 = __ldg(t.w0 + xo), n = __ldg(t.cnt + xo);
+  const float* s = src + (size_t(row) * win + j0) * ss + c;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < n; ++k) tap_acc(acc, __ldg(t.w + w0 + k), *reinterpret_cast<const float4*>(s + size_t(k) * ss));
+  *reinterpret_cast<float4*>(dst + size_t(p) * sd + c) = tap_norm(acc, __ldg(t.wsum + xo));
+}
+
+__global__ void resize_v4_kernel(int total4, int c4, int wout, TapTable4 t, const float* __restrict__ src, int ss,
+                                 float* __restrict__ dst, int sd) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total4) return;  // total4 = hout * wout * c4
+  int p = i / c4, c = (i - p * c4) * 4;
+  int yo = p / wout, x = p - yo * wout;
+  int j0 = __ldg(t.j0 + yo), w0 = __ldg(t.w0 + yo), n = __ldg(t.cnt + yo);
+  const float* s = src + (size_t(j0) * wout + x) * ss + c;
+  const size_t step = size_t(wout) * ss;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < n; ++k) tap_acc(acc, __ldg(t.w + w0 + k), *reinterpret_cast<const float4*>(s + k * step));
+  *reinterpret_cast<float4*>(dst + size_t(p) * sd + c) = tap_norm(acc, __ldg(t.wsum + yo));
+}
+
+}  // namespace mx
