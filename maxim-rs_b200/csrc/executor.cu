@@ -872,10 +872,6 @@ int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) {
     MX_CUDA(cudaMemGetInfo(&free_b, &total_b));
     int64_t arena_bytes = plan->arena_len * 4;
     int64_t io_bytes = (len_of(g->bufs[size_t(g->input)]) + len_of(g->bufs[size_t(g->output)])) * 4;
-    for (const mx_buf& b : g->bufs)
-      if (len_of(b) >= (int64_t(1) << 31))
-        throw Error(fmt("a %lldx%lldx%lld activation has 2^31 or more elements; images this large are not supported",
-                        (long long)b.c, (long long)b.h, (long long)b.w));
     int64_t need = arena_bytes + int64_t(g->pool.size()) + io_bytes + g->scratch_len * 4;
     if (need > int64_t(free_b))
       throw Error(fmt("not enough device memory for a %lldx%lld pass\n"
@@ -885,6 +881,11 @@ int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) {
                       (long long)plan->shape.w, (long long)plan->shape.h, (long long)(arena_bytes >> 20),
                       (long long)(g->pool.size() >> 20), (long long)(free_b >> 20)),
                   MX_E_OOM);
+    // The vectorised kernels index with 32 bits.
+    for (const mx_buf& b : g->bufs)
+      if (len_of(b) >= (int64_t(1) << 31))
+        throw Error(fmt("a %lldx%lldx%lld activation has 2^31 or more elements; images this large are not supported",
+                        (long long)b.c, (long long)b.h, (long long)b.w));
     MX_CUDA(cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking));
     cudaError_t e = cudaMalloc(&g->arena, size_t(arena_bytes > 0 ? arena_bytes : 4));
     if (e != cudaSuccess)
