@@ -198,6 +198,57 @@ def traffic_from_profiles(kind):
     return None
 
 
+def run_timeline(args):
+    """Per-op-family device time of one pass (CUDA events around every op on
+    the executor's stream), plus the most expensive op shapes. The same
+    census the reference's `--profile` prints (src/main.rs:586-656)."""
+    import collections
+    mx = importlib.import_module("maxim-rs_b200")
+    work = importlib.import_module("maxim-rs_b200.work")
+    synth = importlib.import_module("maxim-rs_b200.synth")
+    path = checkpoint_path() if args.variant == VARIANT else os.path.join(
+        tempfile.gettempdir(), "maxim_b200_%s.safetensors" % args.variant)
+    synth.checkpoint(path, args.variant, W_SEED)
+    img = synth.image_uniform(synth.input_rng(IN_SEED), args.height, args.width)
+    padded, _ = mx.preprocess(img, 64)
+    plan = mx.Plan(mx.Weights(path), padded.shape[1], padded.shape[2])
+    gpu = mx.Gpu(plan)
+    for _ in range(args.warmup):
+        gpu.run(padded)
+    gpu.set_timeline(True)
+    gpu.run(padded)
+    per, tot = gpu.timeline()
+    fam = collections.defaultdict(lambda: [0, 0.0, 0, 0])
+    shp = collections.defaultdict(lambda: [0, 0.0, 0, 0])
+    for i, o in enumerate(plan.ops()):
+        f, b = work.op_work(plan, o)
+        k = work.KINDS[o.kind]
+        if k in ("conv1x1", "conv3x3", "conv4x4s2", "convt2x2"):
+            d = "%s %d->%d @%dx%d" % (k, o.c_in, o.c_out, o.h, o.wd)
+        elif k == "gate_mm":
+            d = "gate_mm c=%d %dx%d mode%d" % (o.c, o.outer, o.inner, o.mode)
+        else:
+            c, h, w = plan.buf(o.dst)
+            d = "%s %dx%dx%d" % (k, c, h, w)
+        for tab, key in ((fam, k), (shp, d)):
+            e = tab[key]
+            e[0] += 1
+            e[1] += float(per[i])
+            e[2] += f
+            e[3] += b
+    print("%s %dx%d (padded %dx%d): one pass %.2f ms, %d ops, %d kernel launches" % (
+        args.variant, args.width, args.height, padded.shape[2], padded.shape[1], tot, plan.n_ops,
+        gpu.stats()["kernels"]))
+    print("%-12s %5s %9s %6s %9s %9s" % ("kind", "ops", "ms", "share", "TFLOP/s", "GB/s"))
+    for k, (n, ms, f, b) in sorted(fam.items(), key=lambda kv: -kv[1][1]):
+        print("%-12s %5d %9.2f %5.1f%% %9.1f %9.0f" % (k, n, ms, 100 * ms / tot, f / ms / 1e9, b / ms / 1e6))
+    print("top shapes:")
+    for k, (n, ms, f, b) in sorted(shp.items(), key=lambda kv: -kv[1][1])[:20]:
+        print("  %8.2f ms %4dx  %-40s %7.1f TFLOP/s %6.0f GB/s" % (ms, n, k, f / ms / 1e9, b / ms / 1e6))
+    gpu.close()
+    return 0
+
+
 def run_native(args):
     import torch
     import torch.distributed as dist
@@ -345,10 +396,17 @@ def main():
     ap.add_argument("--batch", type=int, default=4, help="images per GPU per step")
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--timeline", action="store_true",
+                    help="print the per-op-family device time of one pass and exit (no JSON line)")
+    ap.add_argument("--variant", default=VARIANT, help="--timeline only: model variant")
+    ap.add_argument("--height", type=int, default=IMG_H, help="--timeline only: image height")
+    ap.add_argument("--width", type=int, default=IMG_W, help="--timeline only: image width")
     args = ap.parse_args()
     if args.warmup < 3:
         log("bench: raising --warmup to 3")
         args.warmup = 3
+    if args.timeline:
+        return run_timeline(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_native(args)

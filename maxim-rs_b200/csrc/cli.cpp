@@ -1,0 +1,201 @@
+// `maxim`: restore one image with a MAXIM checkpoint on a B200
+// (the reference's CLI, src/main.rs:17-156, over this library's C ABI).
+//
+//     maxim -m maxim-s3.safetensors -i in.png -o out.png
+//
+// The plan is built for the padded input shape (reflect pad to a multiple of
+// 64, src/image.rs:171-207), run on the GPU executor, and the result is
+// cropped back the way the reference eval script does. There is no CPU
+// backend here: a missing driver is an error, never a silent fallback.
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <unistd.h>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "maxim_b200.h"
+
+namespace {
+
+const char* kVersion = "0.1.0";
+
+[[noreturn]] void usage() {
+  fprintf(stderr,
+          "maxim %s - MAXIM image restoration on B200 (sm_100a)\n\n"
+          "USAGE:\n    maxim --model <weights.safetensors> -i <in.png> -o <out.png> [options]\n\n"
+          "OPTIONS:\n"
+          "    -m, --model <path>    converted .safetensors checkpoint\n"
+          "    -i, --input <path>    input PNG, or - for stdin (default: stdin)\n"
+          "    -o, --output <path>   output PNG, or - for stdout (default: stdout)\n"
+          "        --device <dev>    gpu (the only backend of this build)\n"
+          "        --gpu             same as --device gpu\n"
+          "        --gpu-index <n>   which CUDA device (default 0)\n"
+          "        --profile         per-op-kind device time of the pass\n"
+          "        --factor <n>      pad to a multiple of n (default 64, as the reference)\n"
+          "    -q, --quiet           no progress output\n"
+          "    -h, --help            this text\n"
+          "    -V, --version         print the version\n",
+          kVersion);
+  exit(2);
+}
+
+std::string last_error() {
+  char buf[4096];
+  mx_last_error(buf, sizeof(buf));
+  return buf;
+}
+
+int fail(const std::string& what) {
+  fprintf(stderr, "maxim: %s%s\n", what.empty() ? "" : (what + ": ").c_str(), last_error().c_str());
+  return 1;
+}
+
+std::vector<uint8_t> read_all(FILE* f) {
+  std::vector<uint8_t> v;
+  uint8_t buf[1 << 16];
+  size_t n;
+  while ((n = fread(buf, 1, sizeof(buf), f)) > 0) v.insert(v.end(), buf, buf + n);
+  return v;
+}
+
+const char* kKind[] = {"copy", "add", "mul", "gate", "gelu", "lrelu", "sigmoid", "chanln", "chanmean",
+                       "chanscale", "conv1x1", "conv3x3", "convdown", "convt", "gatemm", "blockperm",
+                       "resize", "down"};
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  if (argc < 2) usage();
+  std::string model, input = "-", output = "-", device = "gpu";
+  int gpu_index = 0, factor = 64;
+  bool quiet = false, profile = false;
+  for (int i = 1; i < argc; ++i) {
+    std::string a = argv[i];
+    auto next = [&]() -> std::string {
+      if (i + 1 >= argc) usage();
+      return argv[++i];
+    };
+    if (a == "-m" || a == "--model") model = next();
+    else if (a == "-i" || a == "--input") input = next();
+    else if (a == "-o" || a == "--output") output = next();
+    else if (a == "--device") device = next();
+    else if (a == "--gpu") device = "gpu";
+    else if (a == "--cpu") device = "cpu";
+    else if (a == "--gpu-index") gpu_index = atoi(next().c_str());
+    else if (a == "--factor") factor = atoi(next().c_str());
+    else if (a == "--profile" || a == "--timeline") profile = true;
+    else if (a == "-q" || a == "--quiet") quiet = true;
+    else if (a == "-h" || a == "--help") usage();
+    else if (a == "-V" || a == "--version") {
+      printf("maxim %s\n", kVersion);
+      return 0;
+    } else {
+      fprintf(stderr, "maxim: unknown argument `%s`\n", a.c_str());
+      usage();
+    }
+  }
+  if (model.empty()) {
+    fprintf(stderr, "maxim: --model is required\n");
+    usage();
+  }
+  if (device != "gpu") {
+    fprintf(stderr, "maxim: this build runs on the GPU only (there is no CPU backend); got --device %s\n",
+            device.c_str());
+    return 1;
+  }
+  if (factor <= 0) factor = 64;
+
+  mx_weights* w = nullptr;
+  if (mx_weights_open(model.c_str(), &w) != MX_OK) return fail("");
+  char variant[16];
+  mx_weights_variant(w, variant, sizeof(variant));
+
+  mx_image img{};
+  if (input == "-") {
+    auto bytes = read_all(stdin);
+    if (mx_png_read_mem(bytes.data(), bytes.size(), &img) != MX_OK) return fail("stdin");
+  } else if (mx_png_read(input.c_str(), &img) != MX_OK) {
+    return fail("");
+  }
+  mx_image padded{};
+  int32_t even_h = 0, even_w = 0;
+  if (mx_preprocess(&img, factor, &padded, &even_h, &even_w) != MX_OK) return fail("");
+  if (!quiet)
+    fprintf(stderr, "maxim %s: %dx%d -> padded %dx%d (even %dx%d), variant %s\n", kVersion, img.w, img.h, padded.w,
+            padded.h, even_w, even_h, variant);
+
+  auto t0 = std::chrono::steady_clock::now();
+  mx_plan_handle* plan = nullptr;
+  if (mx_plan_build(w, padded.h, padded.w, 0, &plan) != MX_OK) return fail("");
+  const mx_plan* pv = mx_plan_view(plan);
+  if (!quiet)
+    fprintf(stderr, "maxim: plan %d ops, %d buffers, arena %.1f MiB\n", pv->n_ops, pv->n_bufs,
+            pv->arena_len * 4.0 / 1048576.0);
+
+  if (mx_driver_ready() != MX_OK) return fail("cuda");
+  mx_gpu* gpu = nullptr;
+  if (mx_gpu_new(gpu_index, pv, &gpu) != MX_OK) return fail("");
+  mx_gpu_stats st{};
+  mx_gpu_get_stats(gpu, &st);
+  if (!quiet)
+    fprintf(stderr, "maxim: device %s, %lld kernel launches per pass, weights %.1f MiB\n", st.device_name,
+            (long long)st.kernels, st.weight_bytes / 1048576.0);
+  if (profile) mx_gpu_set_timeline(gpu, 1);
+  const size_t n_out = size_t(pv->bufs[pv->output].c * pv->bufs[pv->output].h * pv->bufs[pv->output].w);
+  std::vector<float> out(n_out);
+  auto t1 = std::chrono::steady_clock::now();
+  if (mx_gpu_run(gpu, padded.data, out.data()) != MX_OK) return fail("");
+  auto t2 = std::chrono::steady_clock::now();
+  if (!quiet)
+    fprintf(stderr, "maxim: setup %.2fs, pass %.1f ms\n", std::chrono::duration<double>(t1 - t0).count(),
+            std::chrono::duration<double, std::milli>(t2 - t1).count());
+  if (profile) {
+    std::vector<float> per(size_t(pv->n_ops));
+    float total = 0.0f;
+    if (mx_gpu_timeline(gpu, per.data(), pv->n_ops, &total) == MX_OK) {
+      std::map<std::string, std::pair<double, int>> by;
+      for (int32_t i = 0; i < pv->n_ops; ++i) {
+        auto& e = by[kKind[pv->ops[i].kind]];
+        e.first += per[size_t(i)];
+        e.second += 1;
+      }
+      printf("timeline: %.2f ms total, %d ops\n%-10s %7s %9s %7s\n", total, pv->n_ops, "op", "count", "total ms",
+             "share");
+      for (auto& kv : by)
+        printf("%-10s %7d %9.2f %6.1f%%\n", kv.first.c_str(), kv.second.second, kv.second.first,
+               100.0 * kv.second.first / (total > 0 ? total : 1));
+    }
+  }
+  mx_image pred{3, int32_t(padded.h), int32_t(padded.w), out.data()};
+  mx_image cropped{};
+  if (mx_crop_out(&pred, img.h, img.w, even_h, even_w, &cropped) != MX_OK) return fail("");
+  if (output == "-") {
+    // The library writes files; stream through a temporary for stdout.
+    char tmpl[] = "/tmp/maxim_out_XXXXXX";
+    int fd = mkstemp(tmpl);
+    if (fd < 0) {
+      fprintf(stderr, "maxim: cannot create a temporary file for stdout\n");
+      return 1;
+    }
+    close(fd);
+    if (mx_png_write(tmpl, &cropped) != MX_OK) return fail("stdout");
+    FILE* f = fopen(tmpl, "rb");
+    auto bytes = read_all(f);
+    fclose(f);
+    unlink(tmpl);
+    fwrite(bytes.data(), 1, bytes.size(), stdout);
+  } else {
+    if (mx_png_write(output.c_str(), &cropped) != MX_OK) return fail("");
+    if (!quiet) fprintf(stderr, "maxim: wrote %s\n", output.c_str());
+  }
+  mx_image_free(&cropped);
+  mx_image_free(&padded);
+  mx_image_free(&img);
+  mx_gpu_free(gpu);
+  mx_plan_free(plan);
+  mx_weights_free(w);
+  return 0;
+}
