@@ -188,6 +188,29 @@ typedef struct mx_gpu_stats {
 } mx_gpu_stats;
 int mx_gpu_get_stats(mx_gpu* g, mx_gpu_stats* s);
 
+/* The per-channel mean (the CALayer squeeze) of an NHWC tensor in device
+ * memory, computed without allocating anything. This entry point has no
+ * counterpart in the reference.
+ *
+ * It is for callers that cannot call cudaMalloc: an engine that gives the GPU
+ * a fixed memory budget up front, code running inside a CUDA stream capture
+ * (where allocation is not allowed), or a service whose allocator forbids
+ * stray allocations. The caller passes the input x (npix pixels, c channels
+ * contiguous, pixel_stride floats between pixels, 16-byte aligned) and the
+ * output out (c floats), both in device memory; the partial sums live in one
+ * fixed 1 MiB device array inside the library (held on every GPU that loads
+ * it, until the process exits) instead of in allocated scratch.
+ * Limits: c a multiple of 4 and at most 1024; npix and npix * pixel_stride
+ * below 2^31. Larger sizes are rejected with MX_E_INVALID.
+ * The first call on each device looks up that device's address of the array
+ * (with the device current) and caches it; make that first call before any
+ * stream capture. All calls share the array, so calls that overlap on the
+ * GPU (unordered streams) race on it; each call overwrites every partial it
+ * reads, so nothing needs clearing between calls. `stream` is a cudaStream_t
+ * (null for the legacy default stream); the call is asynchronous on it. */
+int mx_channel_mean_noalloc(const float* x, int64_t npix, int32_t c, int64_t pixel_stride, float* out,
+                            void* stream);
+
 /* ================================================= 2. the host contract ==== */
 
 typedef struct mx_weights mx_weights;

@@ -87,6 +87,8 @@ _SIGS = {
     "mx_gpu_timeline": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                        ctypes.POINTER(ctypes.c_float)]),
     "mx_gpu_get_stats": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(mx_gpu_stats)]),
+    "mx_channel_mean_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int64,
+                                               ctypes.c_void_p, ctypes.c_void_p]),
     "mx_weights_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
     "mx_weights_free": (None, [ctypes.c_void_p]),
     "mx_weights_variant": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]),
@@ -344,6 +346,13 @@ class Gpu:
         check(lib().mx_gpu_get_stats(self._h, ctypes.byref(s)))
         return {"device_name": s.device_name.decode(), "arena_bytes": s.arena_bytes,
                 "weight_bytes": s.weight_bytes, "pool_bytes": s.pool_bytes, "ops": s.ops, "kernels": s.kernels}
+
+
+def channel_mean_noalloc(x_ptr, npix, c, pixel_stride, out_ptr, stream=0):
+    """`mx_channel_mean_noalloc`: the channel mean of an NHWC tensor already in
+    device memory (integer device addresses), using no allocation."""
+    check(lib().mx_channel_mean_noalloc(ctypes.c_void_p(x_ptr), npix, c, pixel_stride, ctypes.c_void_p(out_ptr),
+                                        ctypes.c_void_p(stream)), "channel mean (no allocation)")
 
 
 def _image_to_np(img):

@@ -10,6 +10,8 @@
 #include "gpu_common.cuh"
 
 namespace mx {
+// Internal linkage: more than one translation unit includes these kernels.
+namespace {
 
 // Space <-> blocked permutation of whole pixels, 4 channels per thread
 // (src/exec_cpu.rs:1078-1103; blocked index e = g * psz + q).
@@ -193,4 +195,5 @@ __global__ void resize_v4_kernel(int total4, int c4, int wout, TapTable4 t, cons
   *reinterpret_cast<float4*>(dst + size_t(p) * sd + c) = tap_norm(acc, __ldg(t.wsum + yo));
 }
 
+}  // namespace
 }  // namespace mx
