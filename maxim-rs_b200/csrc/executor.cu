@@ -31,6 +31,7 @@
 #include "common.h"
 #include "gpu_common.cuh"
 #include "kernels_simt.cuh"
+#include "kernels_conv3.cuh"
 #include "kernels_mem.cuh"
 #include "kernels_umma.cuh"
 #include "maxim_b200.h"
@@ -140,9 +141,12 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // A tiled fp32 tensor map with 128-byte swizzle (the UMMA canonical layout).
 // dims / box innermost first; strides in bytes for dims 1..rank-1.
 CUtensorMap make_tensor_map(const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
-                            const uint32_t* box, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+                            const uint32_t* box, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B,
+                            const uint32_t* elem_strides = nullptr) {
   CUtensorMap m;
   uint32_t es[5] = {1, 1, 1, 1, 1};
+  if (elem_strides)
+    for (int i = 0; i < rank; ++i) es[i] = elem_strides[i];
   CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, cuuint32_t(rank), const_cast<void*>(base),
                                     dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -263,7 +267,7 @@ ViewMeta meta_of(const mx_gpu& g, int32_t id) {
 // N = c_out in {32, 64, 128, 256}.
 bool umma_eligible(const mx_gpu& g, const mx_op& o) {
   if (!g.use_umma) return false;
-  if (o.kind != MX_OP_CONV1X1 && o.kind != MX_OP_CONV3X3) return false;
+  if (o.kind != MX_OP_CONV1X1 && o.kind != MX_OP_CONV3X3 && o.kind != MX_OP_CONV4X4S2) return false;
   if (o.c_in % 32 != 0) return false;
   if (o.c_out != 32 && o.c_out != 64 && o.c_out != 128 && o.c_out != 256) return false;
   ViewMeta x = meta_of(g, o.src), d = meta_of(g, o.dst);
@@ -284,9 +288,10 @@ bool umma_gate_eligible(const mx_gpu& g, const mx_op& o) {
   return true;
 }
 
-#define MX_UMMA_INSTANCES(X) \
+#define MX_UMMA_INSTANCES(X)                                                    \
   X(32, 0) X(64, 0) X(128, 0) X(256, 0) X(32, 1) X(64, 1) X(128, 1) X(256, 1) \
-  X(32, 2) X(64, 2) X(128, 2) X(256, 2) X(32, 3) X(64, 3) X(128, 3) X(256, 3)
+  X(32, 2) X(64, 2) X(128, 2) X(256, 2) X(32, 3) X(64, 3) X(128, 3) X(256, 3) \
+  X(32, 4) X(64, 4) X(128, 4) X(256, 4)
 
 void umma_attrs_once() {
   static bool done = false;
@@ -387,7 +392,7 @@ Step umma_gate_step(mx_gpu& g, int32_t oi, const mx_op& o, const std::vector<flo
 // and the pool have their final addresses.
 Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const std::vector<float>& w_ktap,
                     const std::vector<float>& bias) {
-  const int taps = o.kind == MX_OP_CONV3X3 ? 9 : 1;
+  const int taps = o.kind == MX_OP_CONV3X3 ? 9 : (o.kind == MX_OP_CONV4X4S2 ? 16 : 1);
   std::vector<float> hi, lo;
   split_tf32(w_ktap, hi, lo);
   const int64_t ho = int64_t(g.pool.put(hi)), lo_off = int64_t(g.pool.put(lo));
@@ -423,15 +428,26 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const std::vector<flo
       u->p.tiles = int((x.npix + 127) / 128);
       u->p.tiles_x = 0;
     } else {
+      // 8x16 output-pixel tiles. The 3x3 conv's A box is the same 8x16
+      // window shifted per tap; the stride-2 conv's box spans 16x32 input
+      // pixels read every second pixel in both dimensions.
+      const int OH = taps == 16 ? op.oh : H, OW = taps == 16 ? op.ow : W;
       uint64_t da[3] = {uint64_t(ci), uint64_t(W), uint64_t(H)};
       uint64_t sa[2] = {uint64_t(x.stride) * 4, uint64_t(W) * uint64_t(x.stride) * 4};
       uint32_t ba[3] = {32, 16, 8};
-      u->a = make_tensor_map(x.ptr, 3, da, sa, ba);
-      uint64_t dd[3] = {uint64_t(n), uint64_t(W), uint64_t(H)};
-      uint64_t sd[2] = {uint64_t(d.stride) * 4, uint64_t(W) * uint64_t(d.stride) * 4};
+      if (taps == 16) {
+        uint32_t ba2[3] = {32, 32, 16}, es[3] = {1, 2, 2};
+        u->a = make_tensor_map(x.ptr, 3, da, sa, ba2, CU_TENSOR_MAP_SWIZZLE_128B, es);
+      } else {
+        u->a = make_tensor_map(x.ptr, 3, da, sa, ba);
+      }
+      uint64_t dd[3] = {uint64_t(n), uint64_t(OW), uint64_t(OH)};
+      uint64_t sd[2] = {uint64_t(d.stride) * 4, uint64_t(OW) * uint64_t(d.stride) * 4};
       u->d = make_tensor_map(d.ptr, 3, dd, sd, ba);
-      u->p.tiles_x = (W + 15) / 16;
-      u->p.tiles = u->p.tiles_x * ((H + 7) / 8);
+      u->p.tiles_x = (OW + 15) / 16;
+      u->p.tiles = u->p.tiles_x * ((OH + 7) / 8);
+      u->p.pad_t = op.pad_top;
+      u->p.pad_l = op.pad_left;
     }
     u->p.kb_per_tap = ci / 32;
     u->p.c_in = ci;
@@ -439,7 +455,7 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const std::vector<flo
     u->p.status = G->status;
     u->n = n;
     u->taps = taps;
-    u->mode = taps == 9 ? MODE_CONV3 : MODE_CONV1;
+    u->mode = taps == 9 ? MODE_CONV3 : (taps == 16 ? MODE_CONV4 : MODE_CONV1);
     u->grid = std::min(u->p.tiles, G->sms);
     u->smem = umma_smem(n);
   };
@@ -587,6 +603,22 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
       }
       int64_t wo = put(wt), bo = put(W(o.bias));
       int h = o.h, wd = o.wd;
+      if (ks == 3 && (ci == 3 || co == 3)) {
+        // The image-facing convs (3 input or 3 output channels).
+        st.run = [G, P, dst, src, wo, bo, ci, co, h, wd](cudaStream_t s) {
+          View d = view_of(*G, dst), x = view_of(*G, src);
+          if (ci == 3) {
+            dim3 grid(unsigned((h * wd + 127) / 128), unsigned((co + 31) / 32));
+            conv3x3_cin3_kernel<<<grid, 128, 0, s>>>(h, wd, co, x.ptr, int(x.stride), P(wo), P(bo), d.ptr,
+                                                     int(d.stride));
+          } else {
+            dim3 grid(unsigned((wd + 15) / 16), unsigned((h + 15) / 16));
+            conv3x3_cout3_kernel<<<grid, 256, 0, s>>>(h, wd, ci, x.ptr, int(x.stride), P(wo), P(bo), d.ptr,
+                                                      int(d.stride));
+          }
+        };
+        break;
+      }
       int oh = ks == 3 ? h : o.oh, ow = ks == 3 ? wd : o.ow;
       int stride = ks == 3 ? 1 : 2, pt = ks == 3 ? 1 : o.pad_top, pl = ks == 3 ? 1 : o.pad_left;
       st.run = [G, P, dst, src, wo, bo, ci, co, h, wd, oh, ow, ks, stride, pt, pl](cudaStream_t s) {

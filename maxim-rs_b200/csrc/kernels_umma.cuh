@@ -46,7 +46,9 @@ namespace mx {
 // MODE_GATE_GRID: grid gating (t = the cell, groups = positions in a cell).
 // The grid case loads and stores its 4 groups as 4 separate boxes so every
 // tensor map keeps its strides in ascending order.
-enum : int { MODE_CONV1 = 0, MODE_CONV3 = 1, MODE_GATE = 2, MODE_GATE_GRID = 3 };
+// MODE_CONV4: the 4x4 stride-2 SAME conv (Conv_down); its A box is read with
+// a TMA traversal stride of 2 in both spatial dimensions.
+enum : int { MODE_CONV1 = 0, MODE_CONV3 = 1, MODE_GATE = 2, MODE_GATE_GRID = 3, MODE_CONV4 = 4 };
 
 struct UmmaConvParams {
   int tiles;       // output tiles
@@ -54,6 +56,7 @@ struct UmmaConvParams {
   int kb_per_tap;  // k-blocks (of 32) per tap
   int c_in;        // K per tap (CONV) / K (GATE)
   int groups;      // GATE_GRID: positions per cell (boxes past it are skipped)
+  int pad_t, pad_l;  // CONV4: SAME padding before the first row / column
   const float* bias;  // per output column, or null
   int* status;        // device status word (0 = ok)
 };
@@ -84,7 +87,8 @@ __global__ void __launch_bounds__(320, 1)
                      UmmaConvParams p) {
   using C = UmmaCfg<N>;
   using namespace sm100;
-  constexpr int TAPS = MODE == MODE_CONV3 ? 9 : 1;
+  constexpr int TAPS = MODE == MODE_CONV3 ? 9 : (MODE == MODE_CONV4 ? 16 : 1);
+  constexpr bool SPATIAL = MODE == MODE_CONV3 || MODE == MODE_CONV4;  // 8x16-pixel output tiles
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = base + C::STAGES * C::STAGE_BYTES;
@@ -105,7 +109,7 @@ __global__ void __launch_bounds__(320, 1)
     if (MODE == MODE_CONV1) {
       a0 = t * 128;
       a1 = 0;
-    } else if (MODE == MODE_CONV3) {
+    } else if (SPATIAL) {
       a0 = (t % p.tiles_x) * 16;
       a1 = (t / p.tiles_x) * 8;
     } else {
@@ -169,6 +173,11 @@ __global__ void __launch_bounds__(320, 1)
           } else if (MODE == MODE_CONV3) {
             const int ky = tap / 3, kx = tap % 3;
             tma_load_3d(st, &tmA, &full[s], cb * 32, a0 + kx - 1, a1 + ky - 1);
+          } else if (MODE == MODE_CONV4) {
+            // Output pixel (oy, ox) reads input (2oy + ky - pt, 2ox + kx - pl):
+            // the tensor map steps 2 input pixels per box element.
+            const int ky = tap >> 2, kx = tap & 3;
+            tma_load_3d(st, &tmA, &full[s], cb * 32, 2 * a0 + kx - p.pad_l, 2 * a1 + ky - p.pad_t);
           } else if (MODE == MODE_GATE) {
             tma_load_3d(st, &tmA, &full[s], a1, kb * 32, a0);
           } else {
@@ -323,7 +332,7 @@ __global__ void __launch_bounds__(320, 1)
         named_bar(1, 128);
         if (et == 0) {
           if (MODE == MODE_CONV1) tma_store_2d(&tmD, sb, j * 32, a0);
-          else if (MODE == MODE_CONV3) tma_store_3d(&tmD, sb, j * 32, a0, a1);
+          else if (SPATIAL) tma_store_3d(&tmD, sb, j * 32, a0, a1);
           else if (MODE == MODE_GATE) tma_store_3d(&tmD, sb, a1, j * 32, a0);
           else
 #pragma unroll
