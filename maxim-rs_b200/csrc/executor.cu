@@ -109,20 +109,27 @@ struct Step {
   std::function<void()> prepare;
 };
 
-// Weights split for the 3-pass TF32 products: hi = w rounded to TF32
-// (nearest, ties to even), lo = w - hi (exact in fp32).
+// w rounded to the nearest TF32 value (ties to even), as fp32 with the low
+// 13 mantissa bits clear; values whose rounding would overflow stay as they are.
+float round_tf32(float w) {
+  uint32_t b;
+  memcpy(&b, &w, 4);
+  uint32_t r = (b + 0xFFFu + ((b >> 13) & 1u)) & 0xFFFFE000u;
+  float h;
+  memcpy(&h, &r, 4);
+  return std::isfinite(h) ? h : w;
+}
+
+// Weights split for the 3-pass TF32 products: hi = w rounded to TF32, lo =
+// the remainder w - hi (exact in fp32) rounded to TF32 in turn, so the tensor
+// core reads both exactly.
 void split_tf32(const std::vector<float>& w, std::vector<float>& hi, std::vector<float>& lo) {
   hi.resize(w.size());
   lo.resize(w.size());
   for (size_t i = 0; i < w.size(); ++i) {
-    uint32_t b;
-    memcpy(&b, &w[i], 4);
-    uint32_t r = (b + 0xFFFu + ((b >> 13) & 1u)) & 0xFFFFE000u;
-    float h;
-    memcpy(&h, &r, 4);
-    if (!std::isfinite(h)) h = w[i];
+    const float h = round_tf32(w[i]);
     hi[i] = h;
-    lo[i] = w[i] - h;
+    lo[i] = round_tf32(w[i] - h);
   }
 }
 

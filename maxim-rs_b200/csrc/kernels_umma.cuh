@@ -20,18 +20,22 @@
 //
 // Precision: every product is a 3-pass TF32 split,
 //   a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi,
-// with a_hi exactly representable in TF32 (low 13 mantissa bits cleared) and
-// a_lo = a - a_hi, so each product carries ~21 significant bits and all of
-// them accumulate in FP32 - the fp32 accuracy class the parity bars need
-// (plain TF32 measured 46-48 dB against the fp32 CPU path under the
-// He-normal init, below the 50 dB bar). Weights are split on the host.
+// with a_hi = a rounded to the nearest TF32 value and a_lo = a - a_hi rounded
+// to TF32 again, so each product carries ~22 significant bits (plain TF32
+// measured 46-48 dB against the fp32 CPU path under the He-normal init, below
+// the 50 dB bar). Weights are split on the host, activations in the kernel.
+// The hi*hi products and the two cross terms accumulate in separate TMEM
+// regions, added in fp32 by the epilogue: the tensor core rounds its fp32
+// accumulator at every MMA, and with one region the full-size running sum
+// took three such roundings per k-step instead of one.
 //
 // Warp roles (320 threads, one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: A block (16 KB), B and B_lo blocks per k-block
 //   warp 1      TMEM owner and MMA issuer (one thread)
 //   warps 2-5   split: A -> (A_hi in place, A_lo beside it) per k-block
 //   warps 6-9   epilogue: TMEM -> registers -> +bias -> swizzled smem -> TMA store
-// Two TMEM accumulators let the epilogue of tile i overlap the MMAs of i+1.
+// Two accumulator sets (N <= 128) let the epilogue of tile i overlap the MMAs
+// of tile i+1; N = 256 has room for one set only.
 // Every mbarrier wait is bounded in time; a wait that runs out records a code
 // in the status word, the kernel unwinds and frees its TMEM.
 #pragma once
@@ -68,7 +72,12 @@ struct UmmaCfg {
   static constexpr int B_BYTES = N * 128;    // N rows x 32 fp32
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   static constexpr int STAGING_BYTES = 2 * 128 * 128;
-  static constexpr int TMEM_COLS = 2 * N;
+  // An accumulator set is two N-column fp32 regions: the hi*hi products and
+  // the two cross terms, summed once in the epilogue. Sets are double
+  // buffered (the epilogue drains one tile while the next accumulates) where
+  // two fit in the 512 TMEM columns.
+  static constexpr int ACC_SETS = 4 * N <= 512 ? 2 : 1;
+  static constexpr int TMEM_COLS = ACC_SETS * 2 * N;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 8 * (3 * STAGES + 4) + 16;
 };
 
@@ -79,6 +88,16 @@ enum : int {
   kErrMmaLo = 0x104,
   kErrEpilogue = 0x105,
 };
+
+// Round an fp32 value to the nearest TF32 value (ties to even), returned as
+// fp32 with the low 13 mantissa bits clear, so the tensor core reads it
+// exactly whatever it does with those bits. Finite inputs here are far below
+// the overflow threshold, so the carry never reaches the exponent's top.
+__device__ __forceinline__ float tf32_rne(float v) {
+  uint32_t b = __float_as_uint(v);
+  b = (b + 0xFFFu + ((b >> 13) & 1u)) & 0xFFFFE000u;
+  return __uint_as_float(b);
+}
 
 template <int N, int MODE>
 __global__ void __launch_bounds__(320, 1)
@@ -201,13 +220,13 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t idesc = idesc_tf32(128, N, GATE ? 1 : 0, 0);
       uint32_t it = 0, tc = 0;
       for (int t = blockIdx.x; t < p.tiles && !*vabort; t += gridDim.x, ++tc) {
-        const uint32_t acc = tc & 1, aph = (tc >> 1) & 1;
+        const uint32_t acc = tc % C::ACC_SETS, aph = (tc / C::ACC_SETS) & 1;
         if (!mbar_wait(&acc_empty[acc], aph ^ 1, vabort)) {
           fail(kErrMmaAcc);
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + acc * N;
+        const uint32_t d = tmem + acc * 2 * N, dx = d + N;
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % C::STAGES;
@@ -232,9 +251,14 @@ __global__ void __launch_bounds__(320, 1)
               dalo = desc_kmajor_sw128(alo + 32 * k);
             }
             const uint64_t db = desc_kmajor_sw128(b + 32 * k), dblo = desc_kmajor_sw128(blo + 32 * k);
-            mma_tf32(d, dalo, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-            mma_tf32(d, da, dblo, idesc, 1u);
-            mma_tf32(d, da, db, idesc, 1u);
+            // The running sum of the hi*hi products takes one accumulator
+            // update per k-step; the cross terms, about 2^-12 of its size,
+            // go to their own region, so the accumulator's rounding at each
+            // update is paid once per k-step at full magnitude, not three times.
+            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            mma_tf32(d, da, db, idesc, accum);
+            mma_tf32(dx, dalo, db, idesc, accum);
+            mma_tf32(dx, da, dblo, idesc, 1u);
           }
           mma_commit(&empty[s]);
         }
@@ -264,14 +288,14 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int i = 0; i < 8 * 128; i += 128) {
           float4 v = a[i], h, l;
-          h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-          h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-          h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-          h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-          l.x = v.x - h.x;
-          l.y = v.y - h.y;
-          l.z = v.z - h.z;
-          l.w = v.w - h.w;
+          h.x = tf32_rne(v.x);
+          h.y = tf32_rne(v.y);
+          h.z = tf32_rne(v.z);
+          h.w = tf32_rne(v.w);
+          l.x = tf32_rne(v.x - h.x);
+          l.y = tf32_rne(v.y - h.y);
+          l.z = tf32_rne(v.z - h.z);
+          l.w = tf32_rne(v.w - h.w);
           a[i] = h;
           alo[i] = l;
         }
@@ -288,7 +312,7 @@ __global__ void __launch_bounds__(320, 1)
     uint32_t tc = 0;
     int chunk = 0;
     for (int t = blockIdx.x; t < p.tiles && !*vabort; t += gridDim.x, ++tc) {
-      const uint32_t acc = tc & 1, aph = (tc >> 1) & 1;
+      const uint32_t acc = tc % C::ACC_SETS, aph = (tc / C::ACC_SETS) & 1;
       if (!mbar_wait(&acc_full[acc], aph, vabort)) {
         fail(kErrEpilogue);
         break;
@@ -298,8 +322,12 @@ __global__ void __launch_bounds__(320, 1)
       decode(t, a0, a1);
 #pragma unroll 1
       for (int j = 0; j < N / 32; ++j, ++chunk) {
-        float v[32];
-        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + acc * N + j * 32, v);
+        float v[32], x[32];
+        const uint32_t col = tmem + (uint32_t(q * 32) << 16) + acc * 2 * N + j * 32;
+        tmem_ld32(col, v);
+        tmem_ld32(col + N, x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += x[i];
         if (p.bias) {
           const float4* b4 = reinterpret_cast<const float4*>(p.bias + j * 32);
 #pragma unroll
