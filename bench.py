@@ -218,33 +218,38 @@ def run_timeline(args):
     gpu.set_timeline(True)
     gpu.run(padded)
     per, tot = gpu.timeline()
+    st = gpu.stats()
+    ops = plan.ops()
     fam = collections.defaultdict(lambda: [0, 0.0, 0, 0])
     shp = collections.defaultdict(lambda: [0, 0.0, 0, 0])
-    for i, o in enumerate(plan.ops()):
-        f, b = work.op_work(plan, o)
-        k = work.KINDS[o.kind]
-        if k in ("conv1x1", "conv3x3", "conv4x4s2", "convt2x2"):
+    for p, members in work.schedule_steps(gpu.schedule()).items():
+        o = ops[p]
+        k, f, b = work.step_work(plan, ops, members)
+        kind = work.KINDS[o.kind]
+        if kind in ("conv1x1", "conv3x3", "conv4x4s2", "convt2x2"):
             d = "%s %d->%d @%dx%d" % (k, o.c_in, o.c_out, o.h, o.wd)
-        elif k == "gate_mm":
-            d = "gate_mm c=%d %dx%d mode%d" % (o.c, o.outer, o.inner, o.mode)
+        elif kind == "gate_mm":
+            d = "%s c=%d %dx%d mode%d" % (k, o.c, o.outer, o.inner, o.mode)
         else:
             c, h, w = plan.buf(o.dst)
             d = "%s %dx%dx%d" % (k, c, h, w)
         for tab, key in ((fam, k), (shp, d)):
             e = tab[key]
             e[0] += 1
-            e[1] += float(per[i])
+            e[1] += float(per[p])
             e[2] += f
             e[3] += b
-    print("%s %dx%d (padded %dx%d): one pass %.2f ms, %d ops, %d kernel launches" % (
-        args.variant, args.width, args.height, padded.shape[2], padded.shape[1], tot, plan.n_ops,
-        gpu.stats()["kernels"]))
-    print("%-12s %5s %9s %6s %9s %9s" % ("kind", "ops", "ms", "share", "TFLOP/s", "GB/s"))
+    print("%s %dx%d (padded %dx%d): one pass %.2f ms, %d ops in %d steps (%d fused, %d permutations dropped), "
+          "%d kernel launches" % (args.variant, args.width, args.height, padded.shape[2], padded.shape[1], tot,
+                                  plan.n_ops, st["steps"], st["ops_fused"], st["perms_dropped"], st["kernels"]))
+    print("%-26s %5s %9s %6s %9s %9s" % ("step family", "steps", "ms", "share", "TFLOP/s", "GB/s"))
     for k, (n, ms, f, b) in sorted(fam.items(), key=lambda kv: -kv[1][1]):
-        print("%-12s %5d %9.2f %5.1f%% %9.1f %9.0f" % (k, n, ms, 100 * ms / tot, f / ms / 1e9, b / ms / 1e6))
+        ms_ = max(ms, 1e-9)
+        print("%-26s %5d %9.2f %5.1f%% %9.1f %9.0f" % (k, n, ms, 100 * ms / tot, f / ms_ / 1e9, b / ms_ / 1e6))
     print("top shapes:")
-    for k, (n, ms, f, b) in sorted(shp.items(), key=lambda kv: -kv[1][1])[:20]:
-        print("  %8.2f ms %4dx  %-40s %7.1f TFLOP/s %6.0f GB/s" % (ms, n, k, f / ms / 1e9, b / ms / 1e6))
+    for k, (n, ms, f, b) in sorted(shp.items(), key=lambda kv: -kv[1][1])[:24]:
+        ms_ = max(ms, 1e-9)
+        print("  %8.2f ms %4dx  %-48s %7.1f TFLOP/s %6.0f GB/s" % (ms, n, k, f / ms_ / 1e9, b / ms_ / 1e6))
     gpu.close()
     return 0
 
@@ -339,12 +344,12 @@ def run_native(args):
     per, total = gpu.timeline()
     gpu.set_timeline(False)
     fam = {}
-    for i, op in enumerate(plan.ops()):
-        k = work.KINDS[op.kind]
-        f, b = work.op_work(plan, op)
+    ops = plan.ops()
+    for p, members in work.schedule_steps(gpu.schedule()).items():
+        k, f, b = work.step_work(plan, ops, members)
         e = fam.setdefault(k, [0, 0.0, 0, 0])
         e[0] += 1
-        e[1] += float(per[i])
+        e[1] += float(per[p])
         e[2] += f
         e[3] += b
     dom = max(fam, key=lambda k: fam[k][1])

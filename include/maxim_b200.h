@@ -177,7 +177,13 @@ int mx_gpu_timeline(mx_gpu* g, float* per_op_ms, int32_t n_ops, float* total_ms)
 
 /* `device_name` / `arena_bytes` / `weight_bytes` / `pool_bytes` /
  * `ops_launched` (src/exec_gpu.rs:160-190). `kernels` is the number of kernel
- * launches one pass enqueues. */
+ * launches one pass enqueues. The rest describe the executor's own schedule
+ * of the plan (no counterpart in the reference): `steps` scheduled steps,
+ * `ops_fused` plan ops carried out inside another op's step, `perms_dropped`
+ * block permutations replaced by reading the blocks in place, and
+ * `pass_arena_bytes` the arena that schedule needs (the allocation holds the
+ * larger of it and `arena_bytes`, the plan's own, which op-by-op stepping
+ * uses). */
 typedef struct mx_gpu_stats {
   char device_name[128];
   int64_t arena_bytes;
@@ -185,8 +191,23 @@ typedef struct mx_gpu_stats {
   int64_t pool_bytes;
   int64_t ops;
   int64_t kernels;
+  int64_t steps;
+  int64_t ops_fused;
+  int64_t perms_dropped;
+  int64_t pass_arena_bytes;
 } mx_gpu_stats;
 int mx_gpu_get_stats(mx_gpu* g, mx_gpu_stats* s);
+
+/* Which scheduled step carries out each plan op: primary[i] is the plan op
+ * whose step runs op i (i itself when it is not fused), -1 for an op the
+ * schedule removed. n_ops must be the plan's op count. No counterpart in the
+ * reference (its executor runs every op as its own launch). */
+int mx_gpu_schedule(mx_gpu* g, int32_t* primary, int32_t n_ops);
+
+/* The same schedule worked out on the host alone, without a device: for
+ * tests and tools. `stats` receives steps / ops_fused / perms_dropped /
+ * pass_arena_bytes (other fields zero); `primary` as above (may be null). */
+int mx_plan_schedule(const mx_plan* plan, mx_gpu_stats* stats, int32_t* primary, int32_t n_ops);
 
 /* The per-channel mean (the CALayer squeeze) of an NHWC tensor in device
  * memory, computed without allocating anything. This entry point has no

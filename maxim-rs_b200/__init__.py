@@ -5,7 +5,7 @@ GPU executor and the C++ host contract; this package is its Python binding plus
 the synthetic-checkpoint and synthetic-input generators (`synth`).
 """
 from ._native import (Gpu, MaximError, Plan, Weights, crop_out, device_count, driver_ready, exported_symbols, lib,
-                      param_spec, png_read, png_read_bytes, png_write, preprocess)
+                      param_spec, plan_schedule, png_read, png_read_bytes, png_write, preprocess)
 
 __all__ = ["Gpu", "MaximError", "Plan", "Weights", "crop_out", "device_count", "driver_ready", "exported_symbols",
-           "lib", "param_spec", "png_read", "png_read_bytes", "png_write", "preprocess"]
+           "lib", "param_spec", "plan_schedule", "png_read", "png_read_bytes", "png_write", "preprocess"]

@@ -49,7 +49,8 @@ class mx_plan(ctypes.Structure):
 class mx_gpu_stats(ctypes.Structure):
     _fields_ = [("device_name", ctypes.c_char * 128), ("arena_bytes", ctypes.c_int64),
                 ("weight_bytes", ctypes.c_int64), ("pool_bytes", ctypes.c_int64), ("ops", ctypes.c_int64),
-                ("kernels", ctypes.c_int64)]
+                ("kernels", ctypes.c_int64), ("steps", ctypes.c_int64), ("ops_fused", ctypes.c_int64),
+                ("perms_dropped", ctypes.c_int64), ("pass_arena_bytes", ctypes.c_int64)]
 
 
 class mx_image(ctypes.Structure):
@@ -87,6 +88,9 @@ _SIGS = {
     "mx_gpu_timeline": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                        ctypes.POINTER(ctypes.c_float)]),
     "mx_gpu_get_stats": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(mx_gpu_stats)]),
+    "mx_gpu_schedule": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32]),
+    "mx_plan_schedule": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(mx_gpu_stats), ctypes.c_void_p,
+                                        ctypes.c_int32]),
     "mx_channel_mean_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int64,
                                                ctypes.c_void_p, ctypes.c_void_p]),
     "mx_weights_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
@@ -344,8 +348,29 @@ class Gpu:
     def stats(self):
         s = mx_gpu_stats()
         check(lib().mx_gpu_get_stats(self._h, ctypes.byref(s)))
-        return {"device_name": s.device_name.decode(), "arena_bytes": s.arena_bytes,
-                "weight_bytes": s.weight_bytes, "pool_bytes": s.pool_bytes, "ops": s.ops, "kernels": s.kernels}
+        return _stats_dict(s)
+
+    def schedule(self):
+        """Per plan op, the op whose scheduled step carries it out (-1: removed)."""
+        out = np.zeros(self.plan.n_ops, np.int32)
+        check(lib().mx_gpu_schedule(self._h, _ptr(out), self.plan.n_ops), "schedule")
+        return out
+
+
+def _stats_dict(s):
+    return {"device_name": s.device_name.decode(), "arena_bytes": s.arena_bytes, "weight_bytes": s.weight_bytes,
+            "pool_bytes": s.pool_bytes, "ops": s.ops, "kernels": s.kernels, "steps": s.steps,
+            "ops_fused": s.ops_fused, "perms_dropped": s.perms_dropped, "pass_arena_bytes": s.pass_arena_bytes}
+
+
+def plan_schedule(plan):
+    """`mx_plan_schedule`: the executor's schedule of a plan, worked out on the
+    host: (stats dict, per-op primary op array)."""
+    s = mx_gpu_stats()
+    out = np.zeros(plan.n_ops, np.int32)
+    check(lib().mx_plan_schedule(ctypes.cast(plan.view, ctypes.c_void_p), ctypes.byref(s), _ptr(out), plan.n_ops),
+          "plan schedule")
+    return _stats_dict(s), out
 
 
 def channel_mean_noalloc(x_ptr, npix, c, pixel_stride, out_ptr, stream=0):

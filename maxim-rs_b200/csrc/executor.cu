@@ -2,19 +2,23 @@
 // (src/exec_gpu.rs:48-357) behind the C ABI in include/maxim_b200.h.
 //
 // What differs from the reference, by design:
-//   * Activations live in ONE device arena at the plan's own packed offsets
-//     (the plan's liveness is the contract), but each storage-owning buffer is
-//     laid out NHWC - pixel-major, channels contiguous - instead of NCHW. A
-//     channel view of a wider buffer becomes a strided view (same pixel
-//     stride as its parent), so the model's splits and concatenations still
-//     cost nothing. Host images stay NCHW; the boundary transposes on device.
+//   * Activations live in ONE device arena, each storage-owning buffer laid
+//     out NHWC - pixel-major, channels contiguous - instead of NCHW. A channel
+//     view of a wider buffer becomes a strided view (same pixel stride as its
+//     parent), so the model's splits and concatenations still cost nothing.
+//     Host images stay NCHW; the boundary transposes on device.
+//   * A pass runs the executor's own schedule of the plan (schedule.h): GEMM
+//     epilogues absorb the elementwise op after them, copies are forwarded
+//     into their producers, block permutations are dropped in favour of
+//     gating through 5-D tensor maps, and the arena is re-packed by live
+//     range for that shorter op list (still one allocation).
 //   * Every weight is converted to its kernel's layout and uploaded once, at
 //     construction (resident, not lazy per op).
-//   * The whole op stream - input transpose, every op, output transpose - is
-//     captured once into a CUDA graph and replayed per image: one launch per
-//     pass instead of one host dispatch per op.
-// The per-op walk (begin / step_op / read_buf) stays available for the
-// op-by-op verification and runs each op eagerly, unfused.
+//   * The whole scheduled stream - input transpose, every step, output
+//     transpose - is captured once into a CUDA graph and replayed per image.
+// The per-op walk (begin / step_op / read_buf / read_arena) keeps the plan's
+// own op list and offsets: every op runs eagerly and unfused, and every
+// buffer is where the plan put it.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -22,8 +26,10 @@
 #include <cstdlib>
 #include <cstring>
 #include <functional>
+#include <map>
 #include <memory>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include <cudaTypedefs.h>
@@ -35,6 +41,7 @@
 #include "kernels_mem.cuh"
 #include "kernels_umma.cuh"
 #include "maxim_b200.h"
+#include "schedule.h"
 
 namespace mx {
 
@@ -146,7 +153,11 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // A tiled fp32 tensor map with 128-byte swizzle (the UMMA canonical layout).
-// dims / box innermost first; strides in bytes for dims 1..rank-1.
+// dims / box innermost first; strides in bytes for dims 1..rank-1. Every box
+// row is 128 bytes (32 channels), and many views are channel ranges of wider
+// buffers, so L2 fetches are promoted to 128 bytes only: a 256-byte promotion
+// would also pull in the neighbouring channels of a strided view, doubling
+// the DRAM reads of a 32-channel half of a 64-channel buffer.
 CUtensorMap make_tensor_map(const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
                             const uint32_t* box, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B,
                             const uint32_t* elem_strides = nullptr) {
@@ -156,12 +167,13 @@ CUtensorMap make_tensor_map(const void* base, int rank, const uint64_t* dims, co
     for (int i = 0; i < rank; ++i) es[i] = elem_strides[i];
   CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, cuuint32_t(rank), const_cast<void*>(base),
                                     dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw Error(fmt("cuTensorMapEncodeTiled failed (%d)", int(r)), MX_E_CUDA);
   return m;
 }
 
-// The four tensor maps and the launch parameters of one tensor-core conv.
+// The tensor maps and the launch parameters of one tensor-core conv: A, B
+// (hi, lo) and the output D.
 struct UmmaOp {
   CUtensorMap a, b, blo, d;
   UmmaConvParams p{};
@@ -186,8 +198,15 @@ struct mx_gpu {
   float* io_out = nullptr;  // NCHW staging of the output image
   mx::DevicePool pool;
   int64_t weight_bytes = 0;
-  std::vector<mx::Step> steps;  // full pass: [in-transpose, ops..., out-transpose]
+  std::vector<mx::Step> steps;  // op-by-op walk at the plan's offsets: [in-transpose, ops..., out-transpose]
   std::vector<int> step_of_op;  // op index -> step index
+  std::vector<int64_t> roffs;   // each buffer's offset relative to its root (alignment checks)
+  std::vector<int64_t> foffs;   // the scheduled pass's offsets
+  std::vector<mx::Step> fsteps; // the scheduled pass: [in-transpose, steps..., out-transpose]
+  std::vector<int32_t> primary_of;  // plan op -> the op whose step carries it out (-1: dropped)
+  int64_t farena_len = 0;
+  int perms_dropped = 0, ops_fused = 0;
+  std::map<std::pair<int32_t, int>, int64_t> wcache;  // (weight id, layout tag) -> pool offset
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t graph_exec = nullptr;
   bool timeline_on = false;
@@ -215,13 +234,17 @@ int32_t root_of(const mx_gpu& g, int32_t id) {
   return id;
 }
 
-View view_of(const mx_gpu& g, int32_t id) {
+// A buffer's NHWC view in a given layout (per-buffer float offsets: the
+// plan's, or the scheduled pass's).
+using Layout = std::vector<int64_t>;
+
+View view_of(const mx_gpu& g, const Layout& L, int32_t id) {
   int32_t base = root_of(g, id);
   const mx_buf& b = g.bufs[size_t(id)];
   int64_t hw = b.h * b.w;
-  int64_t ch0 = hw ? (g.offs[size_t(id)] - g.offs[size_t(base)]) / hw : 0;
+  int64_t ch0 = hw ? (L[size_t(id)] - L[size_t(base)]) / hw : 0;
   View v;
-  v.ptr = g.arena + g.offs[size_t(base)] + ch0;
+  v.ptr = g.arena + L[size_t(base)] + ch0;
   v.stride = g.bufs[size_t(base)].c;
   v.c = b.c;
   v.npix = hw;
@@ -261,44 +284,64 @@ void check_launch() {
 struct ViewMeta {
   int64_t off, stride, c, npix;
 };
-ViewMeta meta_of(const mx_gpu& g, int32_t id) {
+ViewMeta meta_of(const mx_gpu& g, const Layout& L, int32_t id) {
   int32_t base = root_of(g, id);
   const mx_buf& b = g.bufs[size_t(id)];
   int64_t hw = b.h * b.w;
-  int64_t ch0 = hw ? (g.offs[size_t(id)] - g.offs[size_t(base)]) / hw : 0;
-  return {g.offs[size_t(base)] + ch0, g.bufs[size_t(base)].c, b.c, hw};
+  int64_t ch0 = hw ? (L[size_t(id)] - L[size_t(base)]) / hw : 0;
+  return {L[size_t(base)] + ch0, g.bufs[size_t(base)].c, b.c, hw};
+}
+
+// Whether a buffer can be read or written by TMA as n channels: 16-byte
+// aligned start and pixel stride.
+bool tma_view(const mx_gpu& g, const Layout& L, int32_t id, int n) {
+  if (id < 0) return false;
+  ViewMeta m = meta_of(g, L, id);
+  return m.c == n && m.off % 4 == 0 && m.stride % 4 == 0;
 }
 
 // Whether a conv runs on the tensor-core kernel: TMA needs 16-byte aligned
 // rows and strides; the kernel takes K in blocks of 32 channels and
 // N = c_out in {32, 64, 128, 256}.
-bool umma_eligible(const mx_gpu& g, const mx_op& o) {
+bool umma_eligible(const mx_gpu& g, const Layout& L, const mx_op& o) {
   if (!g.use_umma) return false;
   if (o.kind != MX_OP_CONV1X1 && o.kind != MX_OP_CONV3X3 && o.kind != MX_OP_CONV4X4S2) return false;
   if (o.c_in % 32 != 0) return false;
   if (o.c_out != 32 && o.c_out != 64 && o.c_out != 128 && o.c_out != 256) return false;
-  ViewMeta x = meta_of(g, o.src), d = meta_of(g, o.dst);
+  ViewMeta x = meta_of(g, L, o.src), d = meta_of(g, L, o.dst);
   if (x.off % 4 || x.stride % 4 || d.off % 4 || d.stride % 4) return false;
   if (x.c != o.c_in || d.c != o.c_out || x.npix != int64_t(o.h) * o.wd) return false;
   return true;
 }
 
 // Whether a gating matmul runs on the tensor-core kernel.
-bool umma_gate_eligible(const mx_gpu& g, const mx_op& o) {
+bool umma_gate_eligible(const mx_gpu& g, const Layout& L, const mx_op& o) {
   if (!g.use_umma || o.kind != MX_OP_GATE_MM) return false;
   const int n = o.mode == 0 ? o.outer : o.inner;
   if (n != 32 && n != 64 && n != 128 && n != 256) return false;
   if (o.c % 32 != 0) return false;
-  ViewMeta x = meta_of(g, o.src), d = meta_of(g, o.dst);
+  ViewMeta x = meta_of(g, L, o.src), d = meta_of(g, L, o.dst);
   if (x.off % 4 || x.stride % 4 || d.off % 4 || d.stride % 4) return false;
   if (x.c != o.c || d.c != o.c || x.npix != int64_t(o.outer) * o.inner) return false;
   return true;
 }
 
-#define MX_UMMA_INSTANCES(X)                                                    \
-  X(32, 0) X(64, 0) X(128, 0) X(256, 0) X(32, 1) X(64, 1) X(128, 1) X(256, 1) \
-  X(32, 2) X(64, 2) X(128, 2) X(256, 2) X(32, 3) X(64, 3) X(128, 3) X(256, 3) \
-  X(32, 4) X(64, 4) X(128, 4) X(256, 4)
+// Whether a gating matmul can read spatial-order data blocked as `perm`
+// describes (MODE_GATE_SP): one box per group must cover 32 consecutive
+// contracted indices as whole rows, so the row length (cells per grid row
+// for grid gating, pixels per block row for block gating) must divide 32.
+bool umma_gate_spatial_ok(const mx_gpu& g, const Layout& L, const mx_op& gate, const mx_op& perm) {
+  if (!umma_gate_eligible(g, L, gate)) return false;
+  const int row = gate.mode == 0 ? perm.gw : perm.fw;
+  if (row <= 0 || row > 32 || 32 % row != 0) return false;
+  return tma_view(g, L, perm.src, gate.c) && perm.c == gate.c;
+}
+
+// Kernel instances: N (columns per tile; 256 output columns run as two
+// 128-column slices) x MODE.
+#define MX_UMMA_INSTANCES(X)                                                                        \
+  X(32, 0) X(64, 0) X(128, 0) X(32, 1) X(64, 1) X(128, 1) X(32, 2) X(64, 2) X(128, 2) X(32, 3) X(64, 3) \
+  X(128, 3) X(32, 4) X(64, 4) X(128, 4) X(32, 5) X(64, 5) X(128, 5)
 
 void umma_attrs_once() {
   static bool done = false;
@@ -314,14 +357,16 @@ int umma_smem(int n) {
   switch (n) {
     case 32: return UmmaCfg<32>::SMEM_BYTES;
     case 64: return UmmaCfg<64>::SMEM_BYTES;
-    case 128: return UmmaCfg<128>::SMEM_BYTES;
-    default: return UmmaCfg<256>::SMEM_BYTES;
+    default: return UmmaCfg<128>::SMEM_BYTES;
   }
 }
+
+// Columns per tile for an output of n columns (32..256), and the slices.
+int umma_tile_n(int n) { return n > 128 ? 128 : n; }
 void launch_umma(cudaStream_t s, const UmmaOp& u) {
 #define MX_UMMA_CASE(NN, MM)                                                                      \
   if (u.n == NN && u.mode == MM) {                                                                \
-    umma_conv_kernel<NN, MM><<<unsigned(u.grid), 320, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.p);   \
+    umma_conv_kernel<NN, MM><<<unsigned(u.grid), kUmmaThreads, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.p); \
     return;                                                                                       \
   }
   MX_UMMA_INSTANCES(MX_UMMA_CASE)
@@ -329,111 +374,174 @@ void launch_umma(cudaStream_t s, const UmmaOp& u) {
   throw Error(fmt("no tensor-core kernel for N=%d mode=%d", u.n, u.mode));
 }
 
-// The tensor-core step of a gating matmul over a blocked buffer (pixels in
-// block order g * pp + q, NHWC). Block gating (mode 1) contracts q inside a
-// block, grid gating (mode 0) contracts the cell g; A is the activation
-// (MN-major), B = W[a][t] (K-major), D = activation-shaped.
-Step umma_gate_step(mx_gpu& g, int32_t oi, const mx_op& o, const std::vector<float>& w,
-                    const std::vector<float>& bias) {
-  std::vector<float> hi, lo;
-  split_tf32(w, hi, lo);
-  const int64_t ho = int64_t(g.pool.put(hi)), lo_off = int64_t(g.pool.put(lo));
-  g.weight_bytes += int64_t(2 * hi.size() * 4);
-  int64_t bo = -1;
-  if (!bias.empty()) {
-    bo = int64_t(g.pool.put(bias));
-    g.weight_bytes += int64_t(bias.size() * 4);
+// Weights in a kernel's layout, uploaded once per (weight, layout) however
+// many steps use them; -1 for an absent weight.
+enum WeightTag : int { WT_RAW = 0, WT_KTAP = 1, WT_HI = 2, WT_LO = 3, WT_KTAP_HI = 4, WT_KTAP_LO = 5, WT_CONVT = 6 };
+int64_t cached(mx_gpu& g, int32_t id, int tag, const std::function<std::vector<float>()>& make) {
+  if (id < 0) return -1;
+  const auto key = std::make_pair(id, tag);
+  auto it = g.wcache.find(key);
+  if (it != g.wcache.end()) return it->second;
+  const std::vector<float> v = make();
+  int64_t off = -1;
+  if (!v.empty()) {
+    off = int64_t(g.pool.put(v));
+    g.weight_bytes += int64_t(v.size() * 4);
   }
+  g.wcache[key] = off;
+  return off;
+}
+
+// What a scheduled step adds to its tensor-core op: the elementwise tail and,
+// for a gating matmul over spatial-order data, the blocking it reads through.
+struct UmmaEpi {
+  int epi = EPI_NONE;
+  int32_t src = -1;
+  float slope = 0.0f;
+  bool spatial = false;
+  mx_op perm{};
+};
+
+// The tensor-core step of a gating matmul. Over a blocked buffer (pixels in
+// block order g * pp + q, NHWC): block gating (mode 1) contracts q inside a
+// block, grid gating (mode 0) contracts the cell g. Over a spatial buffer
+// (E.spatial) the same contraction reads the blocks in place through 5-D
+// tensor maps. A is the activation (MN-major), B = W[a][t] (K-major), D and
+// the epilogue operand are activation-shaped.
+Step umma_gate_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int64_t ho, int64_t lo_off, int64_t bo,
+                    const UmmaEpi& E) {
   auto u = std::make_shared<UmmaOp>();
   mx_gpu* G = &g;
   const mx_op op = o;
   ++g.umma_ops;
   Step st{oi, 1, nullptr, nullptr};
-  st.prepare = [G, u, op, ho, lo_off, bo]() {
-    View x = view_of(*G, op.src), d = view_of(*G, op.dst);
+  st.prepare = [G, L, u, op, ho, lo_off, bo, E]() {
+    View x = view_of(*G, *L, op.src), d = view_of(*G, *L, op.dst);
+    View e = E.epi >= EPI_ADD ? view_of(*G, *L, E.src) : d;
     const uint64_t gg = uint64_t(op.outer), pp = uint64_t(op.inner), c = uint64_t(op.c);
     const int n = op.mode == 0 ? op.outer : op.inner;  // the contracted (and produced) axis
+    const int tn = umma_tile_n(n);
     const float* whi = reinterpret_cast<const float*>(G->pool.dev + ho);
     const float* wlo = reinterpret_cast<const float*>(G->pool.dev + lo_off);
     {
       uint64_t dims[2] = {uint64_t(n), uint64_t(n)}, str[1] = {uint64_t(n) * 4};
-      uint32_t box[2] = {32, uint32_t(n)};
+      uint32_t box[2] = {32, uint32_t(tn)};
       u->b = make_tensor_map(whi, 2, dims, str, box);
       u->blo = make_tensor_map(wlo, 2, dims, str, box);
     }
-    // dims (channel, q, g), strides ascending: q steps one pixel, g one block.
-    uint64_t dims[3] = {c, pp, gg};
-    uint64_t sa[2] = {uint64_t(x.stride) * 4, pp * uint64_t(x.stride) * 4};
-    uint64_t sd[2] = {uint64_t(d.stride) * 4, pp * uint64_t(d.stride) * 4};
-    uint32_t box[3];
-    if (op.mode == 1) {  // block gating: box (32 channels, 32 q, 4 blocks)
-      box[0] = 32, box[1] = 32, box[2] = 4;
-      u->mode = MODE_GATE;
-      u->p.groups = int(gg);
-    } else {  // grid gating: per-position box (32 channels, 1 q, 32 cells)
-      box[0] = 32, box[1] = 1, box[2] = 32;
-      u->mode = MODE_GATE_GRID;
-      u->p.groups = int(pp);
+    u->p.eptr = E.epi >= EPI_ADD ? e.ptr : nullptr;
+    u->p.estride = int(e.stride);
+    u->p.e_pp = int(pp);
+    u->p.sp_shift = 0;
+    if (E.spatial) {
+      // dims (channel, fx, gx, fy, gy), strides ascending; pixel
+      // (gy * fh + fy, gx * fw + fx).
+      const mx_op& P = E.perm;
+      const uint64_t fw = uint64_t(P.fw), gw = uint64_t(P.gw), fh = uint64_t(P.fh), gh = uint64_t(P.gh);
+      uint64_t dims[5] = {c, fw, gw, fh, gh};
+      auto strides = [&](const View& v, uint64_t* sv) {
+        const uint64_t px = uint64_t(v.stride) * 4;
+        sv[0] = px, sv[1] = fw * px, sv[2] = fw * gw * px, sv[3] = fh * fw * gw * px;
+      };
+      uint64_t sa[4], sd[4];
+      strides(x, sa), strides(d, sd);
+      uint32_t box[5];
+      if (op.mode == 0) {  // grid gating: t = cell, a group = a position in the cell
+        box[0] = 32, box[1] = 1, box[2] = uint32_t(gw), box[3] = 1, box[4] = uint32_t(32 / gw);
+        u->p.groups = int(pp);
+      } else {  // block gating: t = position in the block, a group = a block
+        box[0] = 32, box[1] = uint32_t(fw), box[2] = 1, box[3] = uint32_t(32 / fw), box[4] = 1;
+        u->p.groups = int(gg);
+      }
+      u->a = make_tensor_map(x.ptr, 5, dims, sa, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+      u->d = make_tensor_map(d.ptr, 5, dims, sd, box);
+      u->mode = MODE_GATE_SP;
+      u->p.sp_mode = op.mode == 0 ? 0 : 1;
+      u->p.fw = P.fw;
+      u->p.gw = P.gw;
+      u->p.fh = P.fh;
+      u->p.e_w = P.gw * P.fw;
+      const int rowlen = op.mode == 0 ? P.gw : P.fw;
+      while ((1 << u->p.sp_shift) < rowlen) ++u->p.sp_shift;
+    } else {
+      // dims (channel, q, g), strides ascending: q steps one pixel, g one block.
+      uint64_t dims[3] = {c, pp, gg};
+      uint64_t sa[2] = {uint64_t(x.stride) * 4, pp * uint64_t(x.stride) * 4};
+      uint64_t sd[2] = {uint64_t(d.stride) * 4, pp * uint64_t(d.stride) * 4};
+      uint32_t box[3];
+      if (op.mode == 1) {  // block gating: box (32 channels, 32 q, 4 blocks)
+        box[0] = 32, box[1] = 32, box[2] = 4;
+        u->mode = MODE_GATE;
+        u->p.groups = int(gg);
+      } else {  // grid gating: per-position box (32 channels, 1 q, 32 cells)
+        box[0] = 32, box[1] = 1, box[2] = 32;
+        u->mode = MODE_GATE_GRID;
+        u->p.groups = int(pp);
+      }
+      // The activation is the MN-major operand: 32-byte-atom swizzle (see
+      // desc_mnmajor_sw128_32b). The output staging is plain 128-byte swizzle.
+      u->a = make_tensor_map(x.ptr, 3, dims, sa, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+      // The output goes out per epilogue warp, one group at a time.
+      uint32_t bd[3] = {box[0], box[1], 1};
+      if (op.mode == 0) bd[1] = 1, bd[2] = 32;
+      u->d = make_tensor_map(d.ptr, 3, dims, sd, bd);
     }
-    // The activation is the MN-major operand: 32-byte-atom swizzle (see
-    // desc_mnmajor_sw128_32b). The output staging is plain 128-byte swizzle.
-    u->a = make_tensor_map(x.ptr, 3, dims, sa, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
-    u->d = make_tensor_map(d.ptr, 3, dims, sd, box);
+    u->p.n_slices = n / tn;
     u->p.tiles_x = (u->p.groups + 3) / 4;
-    u->p.tiles = u->p.tiles_x * int(c / 32);
+    u->p.tiles = u->p.tiles_x * int(c / 32) * u->p.n_slices;
     u->p.kb_per_tap = n / 32;
     u->p.c_in = n;
+    u->p.epi = E.epi;
+    u->p.slope = E.slope;
     u->p.bias = bo < 0 ? nullptr : reinterpret_cast<const float*>(G->pool.dev + bo);
     u->p.status = G->status;
-    u->n = n;
+    u->n = tn;
     u->taps = 1;
     u->grid = std::min(u->p.tiles, G->sms);
-    u->smem = umma_smem(n);
+    u->smem = umma_smem(tn);
   };
   st.run = [u](cudaStream_t s) { launch_umma(s, *u); };
   return st;
 }
 
-// The tensor-core step of a 1x1 or 3x3 conv: split weights into TF32 hi/lo
-// in [c_out][tap][c_in] order, then build the tensor maps once the arena
-// and the pool have their final addresses.
-Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const std::vector<float>& w_ktap,
-                    const std::vector<float>& bias) {
+// The tensor-core step of a 1x1, 3x3 or 4x4 stride-2 conv over weights split
+// into TF32 hi/lo in [c_out][tap][c_in] order; the tensor maps are built once
+// the arena and the pool have their final addresses.
+Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int64_t ho, int64_t lo_off, int64_t bo,
+                    const UmmaEpi& E) {
   const int taps = o.kind == MX_OP_CONV3X3 ? 9 : (o.kind == MX_OP_CONV4X4S2 ? 16 : 1);
-  std::vector<float> hi, lo;
-  split_tf32(w_ktap, hi, lo);
-  const int64_t ho = int64_t(g.pool.put(hi)), lo_off = int64_t(g.pool.put(lo));
-  g.weight_bytes += int64_t(2 * hi.size() * 4);
-  int64_t bo = -1;
-  if (!bias.empty()) {
-    bo = int64_t(g.pool.put(bias));
-    g.weight_bytes += int64_t(bias.size() * 4);
-  }
   auto u = std::make_shared<UmmaOp>();
   mx_gpu* G = &g;
   const mx_op op = o;
   ++g.umma_ops;
   Step st{oi, 1, nullptr, nullptr};
-  st.prepare = [G, u, op, taps, ho, lo_off, bo]() {
-    View x = view_of(*G, op.src), d = view_of(*G, op.dst);
+  st.prepare = [G, L, u, op, taps, ho, lo_off, bo, E]() {
+    View x = view_of(*G, *L, op.src), d = view_of(*G, *L, op.dst);
+    View e = E.epi >= EPI_ADD ? view_of(*G, *L, E.src) : d;
     const int n = op.c_out, ci = op.c_in, H = op.h, W = op.wd;
+    const int tn = umma_tile_n(n);
     const uint64_t K = uint64_t(taps) * ci;
     const float* whi = reinterpret_cast<const float*>(G->pool.dev + ho);
     const float* wlo = reinterpret_cast<const float*>(G->pool.dev + lo_off);
     {
       uint64_t dims[2] = {K, uint64_t(n)}, str[1] = {K * 4};
-      uint32_t box[2] = {32, uint32_t(n)};
+      uint32_t box[2] = {32, uint32_t(tn)};
       u->b = make_tensor_map(whi, 2, dims, str, box);
       u->blo = make_tensor_map(wlo, 2, dims, str, box);
     }
+    u->p.eptr = E.epi >= EPI_ADD ? e.ptr : nullptr;
+    u->p.estride = int(e.stride);
     if (taps == 1) {
       uint64_t da[2] = {uint64_t(ci), uint64_t(x.npix)}, sa[1] = {uint64_t(x.stride) * 4};
       uint32_t ba[2] = {32, 128};
       u->a = make_tensor_map(x.ptr, 2, da, sa, ba);
+      // The output goes out per epilogue warp: 32 pixels x 32 channels.
       uint64_t dd[2] = {uint64_t(n), uint64_t(d.npix)}, sd[1] = {uint64_t(d.stride) * 4};
-      u->d = make_tensor_map(d.ptr, 2, dd, sd, ba);
+      uint32_t bd[2] = {32, 32};
+      u->d = make_tensor_map(d.ptr, 2, dd, sd, bd);
       u->p.tiles = int((x.npix + 127) / 128);
       u->p.tiles_x = 0;
+      u->p.e_npix = int(d.npix);
     } else {
       // 8x16 output-pixel tiles. The 3x3 conv's A box is the same 8x16
       // window shifted per tap; the stride-2 conv's box spans 16x32 input
@@ -450,40 +558,71 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const std::vector<flo
       }
       uint64_t dd[3] = {uint64_t(n), uint64_t(OW), uint64_t(OH)};
       uint64_t sd[2] = {uint64_t(d.stride) * 4, uint64_t(OW) * uint64_t(d.stride) * 4};
-      u->d = make_tensor_map(d.ptr, 3, dd, sd, ba);
+      uint32_t bd[3] = {32, 16, 2};  // per epilogue warp: two rows of the 8x16 tile
+      u->d = make_tensor_map(d.ptr, 3, dd, sd, bd);
+      u->p.e_w = OW;
+      u->p.e_h = OH;
       u->p.tiles_x = (OW + 15) / 16;
       u->p.tiles = u->p.tiles_x * ((OH + 7) / 8);
       u->p.pad_t = op.pad_top;
       u->p.pad_l = op.pad_left;
     }
+    u->p.n_slices = n / tn;
+    u->p.tiles *= u->p.n_slices;
     u->p.kb_per_tap = ci / 32;
     u->p.c_in = ci;
+    u->p.epi = E.epi;
+    u->p.slope = E.slope;
     u->p.bias = bo < 0 ? nullptr : reinterpret_cast<const float*>(G->pool.dev + bo);
     u->p.status = G->status;
-    u->n = n;
+    u->n = tn;
     u->taps = taps;
     u->mode = taps == 9 ? MODE_CONV3 : (taps == 16 ? MODE_CONV4 : MODE_CONV1);
     u->grid = std::min(u->p.tiles, G->sms);
-    u->smem = umma_smem(n);
+    u->smem = umma_smem(tn);
   };
   st.run = [u](cudaStream_t s) { launch_umma(s, *u); };
   return st;
 }
 
-// Build the step for one op. Weight layouts are converted here and recorded
-// in the pool; pointers are resolved after the pool is uploaded, so each
-// step captures the pool offset and reads the base at run time.
-void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
-  const mx_op o = plan.ops[oi];
+// The TF32 hi/lo halves of a weight in a given layout, uploaded once.
+std::pair<int64_t, int64_t> cached_split(mx_gpu& g, int32_t id, int tag_hi, int tag_lo,
+                                         const std::function<std::vector<float>()>& make) {
+  const auto kh = std::make_pair(id, tag_hi), kl = std::make_pair(id, tag_lo);
+  auto ih = g.wcache.find(kh), il = g.wcache.find(kl);
+  if (ih != g.wcache.end() && il != g.wcache.end()) return {ih->second, il->second};
+  std::vector<float> hi, lo;
+  split_tf32(make(), hi, lo);
+  const int64_t oh = int64_t(g.pool.put(hi)), ol = int64_t(g.pool.put(lo));
+  g.weight_bytes += int64_t(2 * hi.size() * 4);
+  g.wcache[kh] = oh;
+  g.wcache[kl] = ol;
+  return {oh, ol};
+}
+
+// Build the step that runs op `o` (plan op oi, as the plan has it or as the
+// schedule rewrote it, `fs` non-null) over layout L. Weight layouts are
+// converted here and recorded in the pool (once per weight and layout);
+// pointers are resolved after the pool is uploaded, so each step captures the
+// pool offset and reads the base at run time.
+Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const Layout* L, const SchedStep* fs) {
   auto W = [&](int32_t id) -> std::vector<float> {
     if (id < 0) return {};
     return std::vector<float>(plan.weights[id], plan.weights[id] + plan.weight_lens[id]);
   };
-  auto put = [&](const std::vector<float>& v) -> int64_t {
-    if (v.empty()) return -1;
-    g.weight_bytes += int64_t(v.size() * 4);
-    return int64_t(g.pool.put(v));
-  };
+  auto raw = [&](int32_t id) { return cached(g, id, WT_RAW, [&] { return W(id); }); };
+  UmmaEpi E;
+  if (fs) {
+    E.epi = fs->epi;
+    E.src = fs->epi_src;
+    E.slope = fs->epi_slope;
+    if (fs->gate_perm >= 0) {
+      E.spatial = true;
+      E.perm = plan.ops[fs->gate_perm];
+    }
+  }
+  const bool needs_umma = E.epi != EPI_NONE || E.spatial;
+  bool on_umma = false;
   mx_gpu* G = &g;
   auto P = [G](int64_t off) -> const float* {
     return off < 0 ? nullptr : reinterpret_cast<const float*>(G->pool.dev + off);
@@ -504,10 +643,10 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
                         (long long)o.n, (long long)db.c, (long long)db.h, (long long)db.w));
       int kind = o.kind;
       float slope = o.slope;
-      st.run = [G, kind, dst, src, src2, slope](cudaStream_t s) {
-        View d = view_of(*G, dst), a = view_of(*G, src);
+      st.run = [G, L, kind, dst, src, src2, slope](cudaStream_t s) {
+        View d = view_of(*G, *L, dst), a = view_of(*G, *L, src);
         View b{nullptr, 0, 0, 0};
-        if (src2 >= 0) b = view_of(*G, src2);
+        if (src2 >= 0) b = view_of(*G, *L, src2);
         switch (kind) {
           case MX_OP_COPY: launch_ew<EW_COPY>(s, d, a, b, slope); break;
           case MX_OP_ADD: launch_ew<EW_ADD>(s, d, a, b, slope); break;
@@ -521,9 +660,9 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
       break;
     }
     case MX_OP_CHAN_LN: {
-      int64_t ws = put(W(o.scale)), wb = put(W(o.bias));
-      st.run = [G, P, dst, src, ws, wb](cudaStream_t s) {
-        View d = view_of(*G, dst), x = view_of(*G, src);
+      int64_t ws = raw(o.scale), wb = raw(o.bias);
+      st.run = [G, L, P, dst, src, ws, wb](cudaStream_t s) {
+        View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
         const int c = int(x.c), np = int(x.npix);
         if (aligned4(d) && aligned4(x) && (c == 32 || c == 64 || c == 128 || c == 256)) {
           const int pb = c <= 64 ? 128 : (c == 128 ? 64 : 32);
@@ -551,8 +690,8 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
       const int per = int((npix + nb - 1) / nb);
       g.scratch_len = std::max<int64_t>(g.scratch_len, int64_t(nb) * o.c);
       st.kernels = 2;
-      st.run = [G, dst, src, nb, per](cudaStream_t s) {
-        View d = view_of(*G, dst), x = view_of(*G, src);
+      st.run = [G, L, dst, src, nb, per](cudaStream_t s) {
+        View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
         if (aligned4(x) && x.c <= 1024) {
           const int c4 = int(x.c / 4);
           chan_mean_partial_kernel<<<unsigned(nb), 256, 0, s>>>(int(x.npix), c4, per, x.ptr, int(x.stride),
@@ -565,8 +704,8 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
       break;
     }
     case MX_OP_CHAN_SCALE: {
-      st.run = [G, dst, src, src2](cudaStream_t s) {
-        View d = view_of(*G, dst), x = view_of(*G, src), sc = view_of(*G, src2);
+      st.run = [G, L, dst, src, src2](cudaStream_t s) {
+        View d = view_of(*G, *L, dst), x = view_of(*G, *L, src), sc = view_of(*G, *L, src2);
         if (aligned4(d) && aligned4(x) && aligned4(sc)) {
           const int c4 = int(x.c / 4), total4 = int(x.npix) * c4;
           chan_scale4_kernel<<<blocks_for(total4, TPB), TPB, 0, s>>>(total4, c4, x.ptr, int(x.stride), sc.ptr, d.ptr,
@@ -579,14 +718,16 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
       break;
     }
     case MX_OP_CONV1X1: {
-      if (umma_eligible(g, o)) {
-        st = umma_conv_step(g, oi, o, W(o.w), W(o.bias));
+      if (umma_eligible(g, *L, o)) {
+        const auto hl = cached_split(g, o.w, WT_HI, WT_LO, [&] { return W(o.w); });
+        st = umma_conv_step(g, oi, o, L, hl.first, hl.second, raw(o.bias), E);
+        on_umma = true;
         break;
       }
-      int64_t wo = put(W(o.w)), bo = put(W(o.bias));  // [c_out][c_in]
+      int64_t wo = raw(o.w), bo = raw(o.bias);  // [c_out][c_in]
       int ci = o.c_in, co = o.c_out;
-      st.run = [G, P, dst, src, wo, bo, ci, co](cudaStream_t s) {
-        View d = view_of(*G, dst), x = view_of(*G, src);
+      st.run = [G, L, P, dst, src, wo, bo, ci, co](cudaStream_t s) {
+        View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
         ProbConv1x1 p{x.ptr, x.stride, P(wo), P(bo), d.ptr, d.stride, x.npix, co, ci};
         if (co <= 32) launch_gemm<64, 32>(s, p, 1);
         else launch_gemm<64, 64>(s, p, 1);
@@ -598,22 +739,27 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
       int ks = o.kind == MX_OP_CONV3X3 ? 3 : 4;
       int ci = o.c_in, co = o.c_out;
       // [co][ci][k][k] -> [co][tap][ci]
-      auto w = W(o.w);
-      std::vector<float> wt(w.size());
-      for (int oc = 0; oc < co; ++oc)
-        for (int ic = 0; ic < ci; ++ic)
-          for (int t = 0; t < ks * ks; ++t)
-            wt[(size_t(oc) * ks * ks + t) * ci + ic] = w[(size_t(oc) * ci + ic) * ks * ks + t];
-      if (umma_eligible(g, o)) {
-        st = umma_conv_step(g, oi, o, wt, W(o.bias));
+      auto ktap = [&] {
+        auto w = W(o.w);
+        std::vector<float> wt(w.size());
+        for (int oc = 0; oc < co; ++oc)
+          for (int ic = 0; ic < ci; ++ic)
+            for (int t = 0; t < ks * ks; ++t)
+              wt[(size_t(oc) * ks * ks + t) * ci + ic] = w[(size_t(oc) * ci + ic) * ks * ks + t];
+        return wt;
+      };
+      if (umma_eligible(g, *L, o)) {
+        const auto hl = cached_split(g, o.w, WT_KTAP_HI, WT_KTAP_LO, ktap);
+        st = umma_conv_step(g, oi, o, L, hl.first, hl.second, raw(o.bias), E);
+        on_umma = true;
         break;
       }
-      int64_t wo = put(wt), bo = put(W(o.bias));
+      int64_t wo = cached(g, o.w, WT_KTAP, ktap), bo = raw(o.bias);
       int h = o.h, wd = o.wd;
       if (ks == 3 && (ci == 3 || co == 3)) {
         // The image-facing convs (3 input or 3 output channels).
-        st.run = [G, P, dst, src, wo, bo, ci, co, h, wd](cudaStream_t s) {
-          View d = view_of(*G, dst), x = view_of(*G, src);
+        st.run = [G, L, P, dst, src, wo, bo, ci, co, h, wd](cudaStream_t s) {
+          View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
           if (ci == 3) {
             dim3 grid(unsigned((h * wd + 127) / 128), unsigned((co + 31) / 32));
             conv3x3_cin3_kernel<<<grid, 128, 0, s>>>(h, wd, co, x.ptr, int(x.stride), P(wo), P(bo), d.ptr,
@@ -628,8 +774,8 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
       }
       int oh = ks == 3 ? h : o.oh, ow = ks == 3 ? wd : o.ow;
       int stride = ks == 3 ? 1 : 2, pt = ks == 3 ? 1 : o.pad_top, pl = ks == 3 ? 1 : o.pad_left;
-      st.run = [G, P, dst, src, wo, bo, ci, co, h, wd, oh, ow, ks, stride, pt, pl](cudaStream_t s) {
-        View d = view_of(*G, dst), x = view_of(*G, src);
+      st.run = [G, L, P, dst, src, wo, bo, ci, co, h, wd, oh, ow, ks, stride, pt, pl](cudaStream_t s) {
+        View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
         ProbConvKxK p{x.ptr, x.stride, P(wo), P(bo), d.ptr, d.stride, int64_t(oh) * ow, co, ks * ks * ci,
                       ci, h, wd, oh, ow, ks, stride, pt, pl};
         if (co <= 32) launch_gemm<64, 32>(s, p, 1);
@@ -640,29 +786,34 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
     case MX_OP_CONVT2X2: {
       int ci = o.c_in, co = o.c_out;
       // [ci][co][2][2] (flipped) -> [tap*co + o][ci]
-      auto w = W(o.w);
-      std::vector<float> wt(w.size());
-      for (int ic = 0; ic < ci; ++ic)
-        for (int oc = 0; oc < co; ++oc)
-          for (int t = 0; t < 4; ++t) wt[(size_t(t) * co + oc) * ci + ic] = w[(size_t(ic) * co + oc) * 4 + t];
-      int64_t wo = put(wt), bo = put(W(o.bias));
+      int64_t wo = cached(g, o.w, WT_CONVT, [&] {
+        auto w = W(o.w);
+        std::vector<float> wt(w.size());
+        for (int ic = 0; ic < ci; ++ic)
+          for (int oc = 0; oc < co; ++oc)
+            for (int t = 0; t < 4; ++t) wt[(size_t(t) * co + oc) * ci + ic] = w[(size_t(ic) * co + oc) * 4 + t];
+        return wt;
+      });
+      int64_t bo = raw(o.bias);
       int wd = o.wd;
-      st.run = [G, P, dst, src, wo, bo, ci, co, wd](cudaStream_t s) {
-        View d = view_of(*G, dst), x = view_of(*G, src);
+      st.run = [G, L, P, dst, src, wo, bo, ci, co, wd](cudaStream_t s) {
+        View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
         ProbConvT p{x.ptr, x.stride, P(wo), P(bo), d.ptr, d.stride, x.npix, 4 * co, ci, co, wd};
         launch_gemm<64, 64>(s, p, 1);
       };
       break;
     }
     case MX_OP_GATE_MM: {
-      if (umma_gate_eligible(g, o)) {
-        st = umma_gate_step(g, oi, o, W(o.w), W(o.bias));
+      if (umma_gate_eligible(g, *L, o) || E.spatial) {
+        const auto hl = cached_split(g, o.w, WT_HI, WT_LO, [&] { return W(o.w); });
+        st = umma_gate_step(g, oi, o, L, hl.first, hl.second, raw(o.bias), E);
+        on_umma = true;
         break;
       }
-      int64_t wo = put(W(o.w)), bo = put(W(o.bias));  // [out][in]
+      int64_t wo = raw(o.w), bo = raw(o.bias);  // [out][in]
       int c = o.c, outer = o.outer, inner = o.inner, mode = o.mode;
-      st.run = [G, P, dst, src, wo, bo, c, outer, inner, mode](cudaStream_t s) {
-        View d = view_of(*G, dst), x = view_of(*G, src);
+      st.run = [G, L, P, dst, src, wo, bo, c, outer, inner, mode](cudaStream_t s) {
+        View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
         if (mode == 0) {
           ProbGate0 p{x.ptr, x.stride, P(wo), P(bo), d.ptr, d.stride, outer, inner * c, outer, c, inner};
           launch_gemm<64, 64>(s, p, 1);
@@ -680,8 +831,8 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
         throw Error(fmt("op %d: a %dx%d blocking of a %dx%d plane drops pixels; the executor needs plans whose "
                         "planes the blocks tile exactly (the pad-to-64 pipeline always does)",
                         oi, o.gh * o.fh, o.gw * o.fw, o.h, o.wd));
-      st.run = [G, op](cudaStream_t s) {
-        View d = view_of(*G, op.dst), x = view_of(*G, op.src);
+      st.run = [G, L, op](cudaStream_t s) {
+        View d = view_of(*G, *L, op.dst), x = view_of(*G, *L, op.src);
         if (aligned4(d) && aligned4(x)) {
           const int c4 = op.c / 4, total4 = op.h * op.wd * c4;
           block_perm4_kernel<<<blocks_for(total4, TPB), TPB, 0, s>>>(total4, c4, op.wd, op.gw, op.fh, op.fw,
@@ -698,8 +849,8 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
     }
     case MX_OP_DOWN_S: {
       const mx_op op = o;
-      st.run = [G, op](cudaStream_t s) {
-        View d = view_of(*G, op.dst), x = view_of(*G, op.src);
+      st.run = [G, L, op](cudaStream_t s) {
+        View d = view_of(*G, *L, op.dst), x = view_of(*G, *L, op.src);
         int64_t total = int64_t(op.oh) * op.ow * op.c;
         down_s_kernel<<<blocks_for(total, TPB), TPB, 0, s>>>(total, op.c, op.wd, op.ow, op.stride, op.off, x.ptr,
                                                              x.stride, d.ptr, d.stride);
@@ -716,10 +867,10 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
               ty_c = int64_t(g.pool.put(ty.cnt)), ty_w = int64_t(g.pool.put(ty.w)),
               ty_s = int64_t(g.pool.put(ty.wsum));
       st.kernels = 2;
-      st.run = [G, op, tx_j0, tx_w0, tx_c, tx_w, tx_s, ty_j0, ty_w0, ty_c, ty_w, ty_s](cudaStream_t s) {
+      st.run = [G, L, op, tx_j0, tx_w0, tx_c, tx_w, tx_s, ty_j0, ty_w0, ty_c, ty_w, ty_s](cudaStream_t s) {
         auto I = [G](int64_t off) { return reinterpret_cast<const int*>(G->pool.dev + off); };
         auto F = [G](int64_t off) { return reinterpret_cast<const float*>(G->pool.dev + off); };
-        View d = view_of(*G, op.dst), x = view_of(*G, op.src), t = view_of(*G, op.tmp);
+        View d = view_of(*G, *L, op.dst), x = view_of(*G, *L, op.src), t = view_of(*G, *L, op.tmp);
         if (aligned4(d) && aligned4(x) && aligned4(t)) {
           TapTable4 TX{I(tx_j0), I(tx_w0), I(tx_c), F(tx_w), F(tx_s)};
           TapTable4 TY{I(ty_j0), I(ty_w0), I(ty_c), F(ty_w), F(ty_s)};
@@ -745,33 +896,34 @@ void plan_op(mx_gpu& g, const mx_plan& plan, int32_t oi) {
     default:
       throw Error(fmt("op %d: unknown op kind %d", oi, o.kind));
   }
-  g.step_of_op[size_t(oi)] = int(g.steps.size());
-  g.steps.push_back(std::move(st));
+  if (needs_umma && !on_umma)
+    throw Error(fmt("op %d: the schedule fused work into an op that does not run on the tensor-core kernel", oi));
+  return st;
 }
 
-void build_boundary_steps(mx_gpu& g) {
+// Bracket a step list with the boundary transposes (host NCHW <-> arena NHWC).
+void add_boundary_steps(mx_gpu& g, std::vector<Step>& steps, const Layout* L) {
   mx_gpu* G = &g;
   int32_t in = g.input, out = g.output;
-  Step a{-1, 1, [G, in](cudaStream_t s) {
-           View d = view_of(*G, in);
+  Step a{-1, 1, [G, L, in](cudaStream_t s) {
+           View d = view_of(*G, *L, in);
            nchw_to_nhwc_kernel<<<blocks_for(d.npix * d.c, TPB), TPB, 0, s>>>(d.npix, int(d.c), G->io_in, d.ptr,
                                                                              d.stride);
          }};
-  Step b{-1, 1, [G, out](cudaStream_t s) {
-           View x = view_of(*G, out);
+  Step b{-1, 1, [G, L, out](cudaStream_t s) {
+           View x = view_of(*G, *L, out);
            nhwc_to_nchw_kernel<<<blocks_for(x.npix * x.c, TPB), TPB, 0, s>>>(x.npix, int(x.c), x.ptr, x.stride,
                                                                              G->io_out);
          }};
-  g.steps.insert(g.steps.begin(), std::move(a));
-  for (auto& v : g.step_of_op) v += 1;
-  g.steps.push_back(std::move(b));
+  steps.insert(steps.begin(), std::move(a));
+  steps.push_back(std::move(b));
 }
 
 void capture_graph(mx_gpu& g) {
   if (g.graph_exec) return;
   MX_CUDA(cudaStreamBeginCapture(g.stream, cudaStreamCaptureModeThreadLocal));
   try {
-    for (auto& st : g.steps) st.run(g.stream);
+    for (auto& st : g.fsteps) st.run(g.stream);
   } catch (...) {
     cudaGraph_t tmp;
     cudaStreamEndCapture(g.stream, &tmp);
@@ -780,6 +932,38 @@ void capture_graph(mx_gpu& g) {
   }
   MX_CUDA(cudaStreamEndCapture(g.stream, &g.graph));
   MX_CUDA(cudaGraphInstantiate(&g.graph_exec, g.graph, 0));
+}
+
+// The schedule's questions about a plan, answered for layouts whose roots
+// are 256-byte aligned (the schedule's own packing): only a view's channel
+// offset and its root's width decide alignment.
+ScheduleHooks schedule_hooks(const mx_gpu& g) {
+  const mx_gpu* G = &g;
+  ScheduleHooks h;
+  h.umma = [G](const mx_op& o) {
+    return o.kind == MX_OP_GATE_MM ? umma_gate_eligible(*G, G->roffs, o) : umma_eligible(*G, G->roffs, o);
+  };
+  h.gate_spatial = [G](const mx_op& gate, const mx_op& perm) {
+    return umma_gate_spatial_ok(*G, G->roffs, gate, perm) && tma_view(*G, G->roffs, gate.dst, gate.c);
+  };
+  h.tma_view = [G](int32_t b, int n) { return tma_view(*G, G->roffs, b, n); };
+  return h;
+}
+
+// Host-side set-up shared by mx_gpu_new and the schedule inspector: copy the
+// plan's tables and work out the scheduled pass.
+Schedule plan_schedule(mx_gpu& g, const mx_plan& plan) {
+  g.bufs.assign(plan.bufs, plan.bufs + plan.n_bufs);
+  g.offs.assign(plan.offs, plan.offs + plan.n_bufs);
+  g.alias_parent.assign(plan.alias_parent, plan.alias_parent + plan.n_bufs);
+  g.ops.assign(plan.ops, plan.ops + plan.n_ops);
+  g.input = plan.input;
+  g.output = plan.output;
+  g.arena_len = plan.arena_len;
+  g.shape = plan.shape;
+  g.roffs.resize(size_t(plan.n_bufs));
+  for (int32_t b = 0; b < plan.n_bufs; ++b) g.roffs[size_t(b)] = plan.offs[b] - plan.offs[root_of(g, b)];
+  return build_schedule(plan, schedule_hooks(g), std::getenv("MAXIM_NO_FUSE") == nullptr);
 }
 
 int64_t len_of(const mx_buf& b) { return b.c * b.h * b.w; }
@@ -890,33 +1074,43 @@ int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) {
     DevicePin pin(device);
     g = std::make_unique<mx_gpu>();
     g->device = device;
-    g->bufs.assign(plan->bufs, plan->bufs + plan->n_bufs);
-    g->offs.assign(plan->offs, plan->offs + plan->n_bufs);
-    g->alias_parent.assign(plan->alias_parent, plan->alias_parent + plan->n_bufs);
-    g->ops.assign(plan->ops, plan->ops + plan->n_ops);
-    g->input = plan->input;
-    g->output = plan->output;
-    g->arena_len = plan->arena_len;
-    g->shape = plan->shape;
     validate_weights(*plan);
     g->use_umma = std::getenv("MAXIM_NO_UMMA") == nullptr;
+    const Schedule S = plan_schedule(*g, *plan);
+
+    // The op-by-op walk, at the plan's offsets.
     g->step_of_op.assign(size_t(plan->n_ops), -1);
-    for (int32_t i = 0; i < plan->n_ops; ++i) plan_op(*g, *plan, i);
-    build_boundary_steps(*g);
-    for (auto& st : g->steps) g->kernels += st.kernels;
+    for (int32_t i = 0; i < plan->n_ops; ++i) {
+      g->step_of_op[size_t(i)] = int(g->steps.size()) + 1;  // after the input transpose
+      g->steps.push_back(make_step(*g, *plan, plan->ops[i], i, &g->offs, nullptr));
+    }
+    add_boundary_steps(*g, g->steps, &g->offs);
+
+    // The scheduled pass, at its own offsets.
+    g->foffs = S.offs;
+    g->farena_len = S.arena_len;
+    g->perms_dropped = S.perms_dropped;
+    g->ops_fused = S.ops_fused;
+    g->primary_of.assign(size_t(plan->n_ops), -1);
+    for (const SchedStep& ss : S.steps) {
+      g->fsteps.push_back(make_step(*g, *plan, ss.o, ss.op, &g->foffs, &ss));
+      for (int32_t c : ss.covers) g->primary_of[size_t(c)] = ss.op;
+    }
+    add_boundary_steps(*g, g->fsteps, &g->foffs);
+    for (auto& st : g->fsteps) g->kernels += st.kernels;
 
     // Size the pass before allocating it, and refuse it with the numbers
-    // (src/exec_gpu.rs:96-146).
+    // (src/exec_gpu.rs:96-146). One arena serves both walks.
     size_t free_b = 0, total_b = 0;
     MX_CUDA(cudaMemGetInfo(&free_b, &total_b));
-    int64_t arena_bytes = plan->arena_len * 4;
+    int64_t arena_bytes = std::max(plan->arena_len, g->farena_len) * 4;
     int64_t io_bytes = (len_of(g->bufs[size_t(g->input)]) + len_of(g->bufs[size_t(g->output)])) * 4;
     int64_t need = arena_bytes + int64_t(g->pool.size()) + io_bytes + g->scratch_len * 4;
     if (need > int64_t(free_b))
       throw Error(fmt("not enough device memory for a %lldx%lld pass\n"
                       "maxim: the arena needs %lld MiB and the weights %lld MiB; %lld MiB is free\n"
-                      "maxim: the arena is exact - it is the plan's own packed size, not an estimate - so this is "
-                      "a hard limit, not a guess",
+                      "maxim: the arena is exact - the larger of the plan's own packed size and the executor's "
+                      "schedule's, not an estimate - so this is a hard limit, not a guess",
                       (long long)plan->shape.w, (long long)plan->shape.h, (long long)(arena_bytes >> 20),
                       (long long)(g->pool.size() >> 20), (long long)(free_b >> 20)),
                   MX_E_OOM);
@@ -953,6 +1147,8 @@ int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) {
       umma_attrs_once();
     }
     for (auto& st : g->steps)
+      if (st.prepare) st.prepare();
+    for (auto& st : g->fsteps)
       if (st.prepare) st.prepare();
     *out = g.release();
   });
@@ -1017,12 +1213,12 @@ int mx_gpu_enqueue(mx_gpu* g) {
     if (g->timeline_on) {
       // One event before every step and one after the last, one sync at the
       // end (src/exec_gpu.rs:231-265).
-      size_t n = g->steps.size();
+      size_t n = g->fsteps.size();
       std::vector<cudaEvent_t> ev(n + 1);
       for (auto& e : ev) MX_CUDA(cudaEventCreate(&e));
       for (size_t i = 0; i < n; ++i) {
         MX_CUDA(cudaEventRecord(ev[i], g->stream));
-        g->steps[i].run(g->stream);
+        g->fsteps[i].run(g->stream);
       }
       MX_CUDA(cudaEventRecord(ev[n], g->stream));
       check_launch();
@@ -1034,7 +1230,7 @@ int mx_gpu_enqueue(mx_gpu* g) {
         float ms = 0.0f;
         MX_CUDA(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
         g->timeline_total += ms;
-        int op = g->steps[i].op;
+        int op = g->fsteps[i].op;  // a fused step's time goes to its primary op
         if (op >= 0) g->timeline_ms[size_t(op)] += ms;
       }
       for (auto& e : ev) cudaEventDestroy(e);
@@ -1103,7 +1299,7 @@ int mx_gpu_read_buf(mx_gpu* g, int32_t id, float* out, int64_t len) {
     if (!g || !out || id < 0 || size_t(id) >= g->bufs.size()) throw Error("mx_gpu_read_buf: bad argument");
     if (len != len_of(g->bufs[size_t(id)])) throw Error("mx_gpu_read_buf: length does not match the buffer");
     DevicePin pin(g->device);
-    View v = view_of(*g, id);
+    View v = view_of(*g, g->offs, id);
     float* tmp = nullptr;
     MX_CUDA(cudaMalloc(&tmp, size_t(std::max<int64_t>(len, 1)) * 4));
     nhwc_to_nchw_kernel<<<blocks_for(v.npix * v.c, TPB), TPB, 0, g->stream>>>(v.npix, int(v.c), v.ptr, v.stride, tmp);
@@ -1153,6 +1349,40 @@ int mx_gpu_get_stats(mx_gpu* g, mx_gpu_stats* s) {
     s->pool_bytes = 0;
     s->ops = int64_t(g->ops.size());
     s->kernels = g->kernels;
+    s->steps = int64_t(g->fsteps.size()) - 2;
+    s->ops_fused = g->ops_fused;
+    s->perms_dropped = g->perms_dropped;
+    s->pass_arena_bytes = g->farena_len * 4;
+  });
+}
+
+int mx_gpu_schedule(mx_gpu* g, int32_t* primary, int32_t n_ops) {
+  return guard([&] {
+    if (!g || !primary) throw Error("mx_gpu_schedule: null argument");
+    if (size_t(n_ops) != g->ops.size()) throw Error("mx_gpu_schedule: n_ops does not match the plan");
+    memcpy(primary, g->primary_of.data(), g->primary_of.size() * sizeof(int32_t));
+  });
+}
+
+int mx_plan_schedule(const mx_plan* plan, mx_gpu_stats* stats, int32_t* primary, int32_t n_ops) {
+  return guard([&] {
+    if (!plan || !stats) throw Error("mx_plan_schedule: null argument");
+    if (primary && n_ops != plan->n_ops) throw Error("mx_plan_schedule: n_ops does not match the plan");
+    mx_gpu g;
+    g.use_umma = std::getenv("MAXIM_NO_UMMA") == nullptr;
+    const Schedule S = plan_schedule(g, *plan);
+    memset(stats, 0, sizeof(*stats));
+    stats->ops = plan->n_ops;
+    stats->arena_bytes = plan->arena_len * 4;
+    stats->steps = int64_t(S.steps.size());
+    stats->ops_fused = S.ops_fused;
+    stats->perms_dropped = S.perms_dropped;
+    stats->pass_arena_bytes = S.arena_len * 4;
+    if (primary) {
+      for (int32_t i = 0; i < n_ops; ++i) primary[i] = -1;
+      for (const SchedStep& ss : S.steps)
+        for (int32_t c : ss.covers) primary[c] = ss.op;
+    }
   });
 }
 

@@ -29,4 +29,12 @@ struct View {
 
 inline unsigned blocks_for(int64_t n, int threads) { return unsigned((n + threads - 1) / threads); }
 
+#ifdef __CUDACC__
+// The activations, shared by the standalone elementwise kernels and the
+// tensor-core epilogue so a fused step computes exactly what the separate
+// op would (src/exec_cpu.rs: gelu with erf, the logistic sigmoid).
+__device__ __forceinline__ float gelu_f(float a) { return 0.5f * a * (1.0f + erff(a * 0.70710677f)); }
+__device__ __forceinline__ float sigmoid_f(float a) { return 1.0f / (1.0f + expf(-a)); }
+#endif
+
 }  // namespace mx

@@ -20,9 +20,9 @@ __device__ __forceinline__ float ew_apply(float a, float b, float slope) {
   else if constexpr (KIND == EW_ADD) return a + b;
   else if constexpr (KIND == EW_MUL) return a * b;
   else if constexpr (KIND == EW_GATE) return a * (b + 1.0f);  // u * (v + 1)
-  else if constexpr (KIND == EW_GELU) return 0.5f * a * (1.0f + erff(a * 0.70710677f));
+  else if constexpr (KIND == EW_GELU) return gelu_f(a);
   else if constexpr (KIND == EW_LRELU) return a >= 0.0f ? a : slope * a;
-  else return 1.0f / (1.0f + expf(-a));  // sigmoid
+  else return sigmoid_f(a);
 }
 
 // Elementwise over npix x c with strided operands, 4 channels per thread.

@@ -33,7 +33,9 @@
 //   warp 0      TMA producer: A block (16 KB), B and B_lo blocks per k-block
 //   warp 1      TMEM owner and MMA issuer (one thread)
 //   warps 2-5   split: A -> (A_hi in place, A_lo beside it) per k-block
-//   warps 6-9   epilogue: TMEM -> registers -> +bias -> swizzled smem -> TMA store
+//   warps 6-9   epilogue: TMEM -> registers -> +bias -> [elementwise tail, with a
+//               second operand TMA-loaded into the staging tile] -> swizzled
+//               smem -> TMA store
 // Two accumulator sets (N <= 128) let the epilogue of tile i overlap the MMAs
 // of tile i+1; N = 256 has room for one set only.
 // Every mbarrier wait is bounded in time; a wait that runs out records a code
@@ -52,18 +54,88 @@ namespace mx {
 // tensor map keeps its strides in ascending order.
 // MODE_CONV4: the 4x4 stride-2 SAME conv (Conv_down); its A box is read with
 // a TMA traversal stride of 2 in both spatial dimensions.
-enum : int { MODE_CONV1 = 0, MODE_CONV3 = 1, MODE_GATE = 2, MODE_GATE_GRID = 3, MODE_CONV4 = 4 };
+// MODE_GATE_SP: either gating over a SPATIAL (plain NHWC) buffer, read and
+// written through 5-D tensor maps over (channel, fx, gx, fy, gy), pixel
+// (gy * fh + fy, gx * fw + fx), so no blocked copy of the activation exists.
+// Like MODE_GATE_GRID it moves one (32 channel x 32 t) box per group, which
+// lands as the same [group][t][channel] smem tile: grid gating (sp_mode 0,
+// t = cell (gy, gx), group = (fy, fx)) takes 32 / gw rows of gw cells, block
+// gating (sp_mode 1, t = (fy, fx), group = block (gy, gx)) 32 / fw rows of fw
+// positions.
+enum : int { MODE_CONV1 = 0, MODE_CONV3 = 1, MODE_GATE = 2, MODE_GATE_GRID = 3, MODE_CONV4 = 4, MODE_GATE_SP = 5 };
+
+// The elementwise tail applied to each output value v before the store, with
+// e the same element of a second operand (same shape as the output), which
+// the epilogue reads straight from global memory one chunk ahead of its use.
+// Numbering matches the executor's.
+enum : int { UEPI_NONE = 0, UEPI_GELU, UEPI_LRELU, UEPI_SIGMOID, UEPI_ADD, UEPI_MUL, UEPI_GATE };
 
 struct UmmaConvParams {
-  int tiles;       // output tiles
+  int tiles;       // output tiles (output blocks x n_slices)
+  int n_slices;    // N-column slices per output block (the output has n_slices * N columns)
   int tiles_x;     // CONV3: tiles per image row (width / 16); GATE: group tiles (ceil(groups / 4))
   int kb_per_tap;  // k-blocks (of 32) per tap
   int c_in;        // K per tap (CONV) / K (GATE)
-  int groups;      // GATE_GRID: positions per cell (boxes past it are skipped)
+  int groups;      // GATE_GRID / GATE_SP: groups (boxes past the last are skipped)
   int pad_t, pad_l;  // CONV4: SAME padding before the first row / column
+  int sp_mode;        // GATE_SP: 0 grid gating, 1 block gating
+  int fw, gw, fh;     // GATE_SP: block width and height in pixels, blocks per row
+  int sp_shift;       // GATE_SP: log2 of the contracted index's row length (gw or fw)
+  int epi;            // UEPI_*
+  float slope;        // UEPI_LRELU
+  const float* eptr;  // the epilogue's second operand (NHWC view), or null
+  int estride;        // its pixel stride in floats
+  int e_npix;         // CONV1: output pixels
+  int e_w, e_h;       // CONV3 / CONV4: output width, height; GATE_SP: image width
+  int e_pp;           // GATE / GATE_GRID: pixels per block of the blocked buffer
   const float* bias;  // per output column, or null
   int* status;        // device status word (0 = ok)
 };
+
+// GATE_SP: the 5-D coordinates (after the channel) of group G's box whose
+// contracted (or produced) index starts at t0 (a multiple of 32; the index's
+// row length is 1 << sp_shift). The group part (two divisions) is per tile;
+// gate_sp_row gives the per-k-block part with a shift.
+__device__ __forceinline__ void gate_sp_group(const UmmaConvParams& p, int G, int& fx, int& gx, int& fy, int& gy) {
+  if (p.sp_mode == 0) {
+    fx = G % p.fw, fy = G / p.fw, gx = 0, gy = 0;
+  } else {
+    gx = G % p.gw, gy = G / p.gw, fx = 0, fy = 0;
+  }
+}
+__device__ __forceinline__ void gate_sp_coords(const UmmaConvParams& p, int G, int t0, int& fx, int& gx, int& fy,
+                                               int& gy) {
+  gate_sp_group(p, G, fx, gx, fy, gy);
+  if (p.sp_mode == 0) gy = t0 >> p.sp_shift;
+  else fy = t0 >> p.sp_shift;
+}
+
+template <int KIND>
+__device__ __forceinline__ void epi_chunk(float (&v)[16], const float (&e)[16], float slope) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    if (KIND == UEPI_GELU) v[i] = gelu_f(v[i]);
+    else if (KIND == UEPI_LRELU) v[i] = v[i] >= 0.0f ? v[i] : slope * v[i];
+    else if (KIND == UEPI_SIGMOID) v[i] = sigmoid_f(v[i]);
+    else if (KIND == UEPI_ADD) v[i] = v[i] + e[i];
+    else if (KIND == UEPI_MUL) v[i] = e[i] * v[i];
+    else if (KIND == UEPI_GATE) v[i] = e[i] * (v[i] + 1.0f);
+  }
+}
+
+// The tail over one chunk: one uniform branch on the kind, then 16
+// independent straight-line evaluations.
+__device__ __forceinline__ void epi_apply(int kind, float (&v)[16], const float (&e)[16], float slope) {
+  switch (kind) {
+    case UEPI_GELU: epi_chunk<UEPI_GELU>(v, e, slope); break;
+    case UEPI_LRELU: epi_chunk<UEPI_LRELU>(v, e, slope); break;
+    case UEPI_SIGMOID: epi_chunk<UEPI_SIGMOID>(v, e, slope); break;
+    case UEPI_ADD: epi_chunk<UEPI_ADD>(v, e, slope); break;
+    case UEPI_MUL: epi_chunk<UEPI_MUL>(v, e, slope); break;
+    case UEPI_GATE: epi_chunk<UEPI_GATE>(v, e, slope); break;
+    default: break;
+  }
+}
 
 template <int N>
 struct UmmaCfg {
@@ -71,7 +143,7 @@ struct UmmaCfg {
   static constexpr int A_BYTES = 128 * 128;  // 128 rows x 32 fp32
   static constexpr int B_BYTES = N * 128;    // N rows x 32 fp32
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-  static constexpr int STAGING_BYTES = 2 * 128 * 128;
+  static constexpr int STAGING_BYTES = 8 * 4096;  // one 32-row x 32-column buffer per epilogue warp
   // An accumulator set is two N-column fp32 regions: the hi*hi products and
   // the two cross terms, summed once in the epilogue. Sets are double
   // buffered (the epilogue drains one tile while the next accumulates) where
@@ -99,8 +171,10 @@ __device__ __forceinline__ float tf32_rne(float v) {
   return __uint_as_float(b);
 }
 
+constexpr int kUmmaThreads = 448;
+
 template <int N, int MODE>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(kUmmaThreads, 1)
     umma_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmD,
                      UmmaConvParams p) {
@@ -108,6 +182,8 @@ __global__ void __launch_bounds__(320, 1)
   using namespace sm100;
   constexpr int TAPS = MODE == MODE_CONV3 ? 9 : (MODE == MODE_CONV4 ? 16 : 1);
   constexpr bool SPATIAL = MODE == MODE_CONV3 || MODE == MODE_CONV4;  // 8x16-pixel output tiles
+  constexpr bool GATE = MODE == MODE_GATE || MODE == MODE_GATE_GRID || MODE == MODE_GATE_SP;
+  constexpr bool PER_GROUP = MODE == MODE_GATE_GRID || MODE == MODE_GATE_SP;  // one box per group
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = base + C::STAGES * C::STAGE_BYTES;
@@ -123,8 +199,14 @@ __global__ void __launch_bounds__(320, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = TAPS * p.kb_per_tap;
 
-  // Tile t -> its origin: CONV1 (m0), CONV3 (x0, y0), GATE (group g0, channel block cc).
-  auto decode = [&](int t, int& a0, int& a1) {
+  // Tile t -> its origin: CONV1 (first pixel a0), SPATIAL (x0, y0), GATE
+  // (first group a0, first channel a1); n0 = the first output column (of
+  // this N-column slice). The slices of one output block are consecutive
+  // tiles, so the CTAs computing them read the same A tile at about the same
+  // time and all but the first read it from L2.
+  auto decode = [&](int t, int& a0, int& a1, int& n0) {
+    n0 = (t % p.n_slices) * N;
+    t /= p.n_slices;
     if (MODE == MODE_CONV1) {
       a0 = t * 128;
       a1 = 0;
@@ -132,8 +214,8 @@ __global__ void __launch_bounds__(320, 1)
       a0 = (t % p.tiles_x) * 16;
       a1 = (t / p.tiles_x) * 8;
     } else {
-      a0 = (t % p.tiles_x) * 4;  // first group of the tile
-      a1 = (t / p.tiles_x) * 32;  // first channel
+      a0 = (t % p.tiles_x) * 4;
+      a1 = (t / p.tiles_x) * 32;
     }
   };
 
@@ -173,9 +255,22 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       uint32_t it = 0;
       for (int t = blockIdx.x; t < p.tiles && !*vabort; t += gridDim.x) {
-        int a0, a1;
-        decode(t, a0, a1);
+        int a0, a1, n0;
+        decode(t, a0, a1, n0);
+        // GATE_SP: each group's fixed coordinates, once per tile.
+        int gfx[4] = {0, 0, 0, 0}, ggx[4] = {0, 0, 0, 0}, gfy[4] = {0, 0, 0, 0}, ggy[4] = {0, 0, 0, 0};
+        if (MODE == MODE_GATE_SP) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) gate_sp_group(p, a0 + g, gfx[g], ggx[g], gfy[g], ggy[g]);
+        }
+        // (tap, channel block) of k-block kb, stepped without division.
+        int tap = 0, cb = 0, ky = 0, kx = 0;
         for (int kb = 0; kb < KB; ++kb, ++it) {
+          if (kb > 0 && ++cb == p.kb_per_tap) {
+            cb = 0;
+            ++tap;
+            if (++kx == (MODE == MODE_CONV4 ? 4 : 3)) kx = 0, ++ky;
+          }
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, vabort)) {
@@ -183,40 +278,46 @@ __global__ void __launch_bounds__(320, 1)
             break;
           }
           uint8_t* st = base + s * C::STAGE_BYTES;
-          const int tap = kb / p.kb_per_tap, cb = kb % p.kb_per_tap;
           int a_bytes = C::A_BYTES;
-          if (MODE == MODE_GATE_GRID) a_bytes = 4096 * min(4, p.groups - a0);
+          if (PER_GROUP) a_bytes = 4096 * min(4, p.groups - a0);
           mbar_arrive_expect_tx(&full[s], a_bytes + 2 * C::B_BYTES);
           if (MODE == MODE_CONV1) {
             tma_load_2d(st, &tmA, &full[s], cb * 32, a0);
           } else if (MODE == MODE_CONV3) {
-            const int ky = tap / 3, kx = tap % 3;
             tma_load_3d(st, &tmA, &full[s], cb * 32, a0 + kx - 1, a1 + ky - 1);
           } else if (MODE == MODE_CONV4) {
             // Output pixel (oy, ox) reads input (2oy + ky - pt, 2ox + kx - pl):
             // the tensor map steps 2 input pixels per box element.
-            const int ky = tap >> 2, kx = tap & 3;
             tma_load_3d(st, &tmA, &full[s], cb * 32, 2 * a0 + kx - p.pad_l, 2 * a1 + ky - p.pad_t);
           } else if (MODE == MODE_GATE) {
             tma_load_3d(st, &tmA, &full[s], a1, kb * 32, a0);
           } else {
-            // A box past the last position would read nothing; its rows
-            // only feed accumulator rows that are never stored, so it is
-            // skipped and the expected byte count below counts only real boxes.
+            // A box past the last group would read nothing; its rows only
+            // feed accumulator rows that are never stored, so it is skipped
+            // and the expected byte count above counts only real boxes.
 #pragma unroll
             for (int g = 0; g < 4; ++g)
-              if (a0 + g < p.groups) tma_load_3d(st + g * 4096, &tmA, &full[s], a1, a0 + g, kb * 32);
+              if (a0 + g < p.groups) {
+                if (MODE == MODE_GATE_GRID) {
+                  tma_load_3d(st + g * 4096, &tmA, &full[s], a1, a0 + g, kb * 32);
+                } else {
+                  const int r = (kb * 32) >> p.sp_shift;
+                  // (fx, gx, fy, gy): the contracted index runs along gy
+                  // (grid gating) or fy (block gating).
+                  tma_load_5d(st + g * 4096, &tmA, &full[s], a1, gfx[g], ggx[g], p.sp_mode == 0 ? gfy[g] : r,
+                              p.sp_mode == 0 ? r : ggy[g]);
+                }
+              }
           }
           const int kcol = tap * p.c_in + cb * 32;
-          tma_load_2d(st + 2 * C::A_BYTES, &tmB, &full[s], kcol, 0);
-          tma_load_2d(st + 2 * C::A_BYTES + C::B_BYTES, &tmBlo, &full[s], kcol, 0);
+          tma_load_2d(st + 2 * C::A_BYTES, &tmB, &full[s], kcol, n0);
+          tma_load_2d(st + 2 * C::A_BYTES + C::B_BYTES, &tmBlo, &full[s], kcol, n0);
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr bool GATE = MODE == MODE_GATE || MODE == MODE_GATE_GRID;
       constexpr uint32_t idesc = idesc_tf32(128, N, GATE ? 1 : 0, 0);
       uint32_t it = 0, tc = 0;
       for (int t = blockIdx.x; t < p.tiles && !*vabort; t += gridDim.x, ++tc) {
@@ -306,74 +407,166 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int et = threadIdx.x - 192;  // 0..127
-    const int q = warp & 3;            // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;     // accumulator row this thread owns
-    uint32_t tc = 0;
-    int chunk = 0;
-    for (int t = blockIdx.x; t < p.tiles && !*vabort; t += gridDim.x, ++tc) {
-      const uint32_t acc = tc % C::ACC_SETS, aph = (tc / C::ACC_SETS) & 1;
-      if (!mbar_wait(&acc_full[acc], aph, vabort)) {
-        fail(kErrEpilogue);
-        break;
+    // Two sets of four warps; set `set` drains accumulator `set`, i.e. every
+    // other tile, so two tiles drain at once. A warp owns the 32 accumulator
+    // rows of its TMEM lane quarter and stages and stores them itself (one
+    // 4 KB staging buffer per warp), so no barrier joins the epilogue warps.
+    const int ew = warp - 6;        // 0..7
+    const int set = ew >> 2;
+    const int q = warp & 3;         // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;  // accumulator row this thread owns
+    const bool has_e = p.epi >= UEPI_ADD;
+    uint8_t* sb = staging + ew * 4096;
+
+    // The second operand's values for this thread in chunk j of tile t: for
+    // row layouts its output pixel's 32 channels, for gating layouts its
+    // channel at the chunk's 32 output positions of its group.
+    auto load_e = [&](int t, int j, float(&e)[32]) {
+      int a0, a1, n0;
+      decode(t, a0, a1, n0);
+      const int col = n0 + j * 32;
+      if (!GATE) {
+        int pix;
+        bool ok;
+        if (MODE == MODE_CONV1) {
+          pix = a0 + row;
+          ok = pix < p.e_npix;
+        } else {
+          const int y = a1 + (row >> 4), x = a0 + (row & 15);
+          ok = y < p.e_h && x < p.e_w;
+          pix = y * p.e_w + x;
+        }
+        const float4* src = reinterpret_cast<const float4*>(p.eptr + size_t(ok ? pix : 0) * p.estride + col);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 v = ok ? src[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          e[4 * i] = v.x, e[4 * i + 1] = v.y, e[4 * i + 2] = v.z, e[4 * i + 3] = v.w;
+        }
+      } else {
+        const int G = a0 + q;
+        const bool ok = G < p.groups;
+        const float* src = p.eptr + a1 + lane;
+        int fx = 0, fy = 0, gx = 0, gy = 0;
+        if (MODE == MODE_GATE_SP) {
+          if (p.sp_mode == 0) fx = G % p.fw, fy = G / p.fw;
+          else gx = G % p.gw, gy = G / p.gw;
+        }
+        const int msk = (1 << p.sp_shift) - 1, rows0 = col >> p.sp_shift;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int a = col + i;
+          int pix;
+          if (MODE == MODE_GATE) {
+            pix = G * p.e_pp + a;
+          } else if (MODE == MODE_GATE_GRID) {
+            pix = a * p.e_pp + G;
+          } else if (p.sp_mode == 0) {
+            pix = ((rows0 + (i >> p.sp_shift)) * p.fh + fy) * p.e_w + (i & msk) * p.fw + fx;
+          } else {
+            pix = (gy * p.fh + rows0 + (i >> p.sp_shift)) * p.e_w + gx * p.fw + (i & msk);
+          }
+          e[i] = ok ? src[size_t(pix) * p.estride] : 0.0f;
+        }
       }
-      tc_fence_after();
-      int a0, a1;
-      decode(t, a0, a1);
-#pragma unroll 1
-      for (int j = 0; j < N / 32; ++j, ++chunk) {
-        float v[32], x[32];
-        const uint32_t col = tmem + (uint32_t(q * 32) << 16) + acc * 2 * N + j * 32;
-        tmem_ld32(col, v);
-        tmem_ld32(col + N, x);
+    };
+
+    const int tstep = 2 * gridDim.x;
+    int t = blockIdx.x + set * gridDim.x, j = 0, a0 = 0, a1 = 0, n0 = 0;
+    uint32_t use = 0;  // how many tiles this set has taken from its accumulator
+    // One chunk (32 columns), in two 16-column halves: drain from TMEM, add
+    // the bias, apply the tail (operand values in `ecur`, loaded while the
+    // previous chunk was finishing), stage and store, then start loading the
+    // next chunk's operand values into `ecur`. Returns false when the
+    // pipeline failed.
+    auto step = [&](float(&ecur)[32]) -> bool {
+      if (j == 0) {
+        bool ok = mbar_wait(&acc_full[set], use & 1, vabort);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) {
+          if (lane == 0) fail(kErrEpilogue);
+          return false;
+        }
+        tc_fence_after();
+        decode(t, a0, a1, n0);
+      }
+      if (lane == 0) bulk_wait_read<0>();  // this warp's previous store has read the buffer
+      __syncwarp();
+      const uint32_t tcol = tmem + (uint32_t(q * 32) << 16) + set * 2 * N + j * 32;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] += x[i];
+      for (int h = 0; h < 2; ++h) {
+        float v[16], x[16], e[16];
+        tmem_ld16x2(tcol + h * 16, tcol + N + h * 16, v, x);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] += x[i];
         if (p.bias) {
-          const float4* b4 = reinterpret_cast<const float4*>(p.bias + j * 32);
+          const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0 + j * 32 + h * 16);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float4 b = __ldg(b4 + i);
+          for (int i = 0; i < 4; ++i) {
+            const float4 b = __ldg(b4 + i);
             v[4 * i] += b.x;
             v[4 * i + 1] += b.y;
             v[4 * i + 2] += b.z;
             v[4 * i + 3] += b.w;
           }
         }
-        uint8_t* sb = staging + (chunk & 1) * (128 * 128);
-        named_bar(1, 128);  // the buffer's previous store has been read (see below)
-        if (MODE == MODE_GATE || MODE == MODE_GATE_GRID) {
-          // Staging is [group][a][channel]: this thread (group q, channel
-          // lane) writes one float into each of its group's 32 rows.
-          float* g = reinterpret_cast<float*>(sb + q * 4096);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int r = q * 32 + i;  // row within the 128-row staging tile
-            g[i * 32 + (((lane >> 2) ^ (r & 7)) << 2) + (lane & 3)] = v[i];
+        for (int i = 0; i < 16; ++i) e[i] = ecur[h * 16 + i];
+        epi_apply(p.epi, v, e, p.slope);
+        if (GATE) {
+          // Staging is [a][channel] for this warp's group: this thread
+          // (channel lane) owns one float in each of the 32 rows.
+          float* g = reinterpret_cast<float*>(sb);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int r = h * 16 + i;
+            g[r * 32 + (((lane >> 2) ^ (r & 7)) << 2) + (lane & 3)] = v[i];
           }
         } else {
-          float4* rowp = reinterpret_cast<float4*>(sb + row * 128);
+          float4* rowp = reinterpret_cast<float4*>(sb + lane * 128);
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            rowp[i ^ (row & 7)] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        }
-        fence_proxy_async_smem();
-        named_bar(1, 128);
-        if (et == 0) {
-          if (MODE == MODE_CONV1) tma_store_2d(&tmD, sb, j * 32, a0);
-          else if (SPATIAL) tma_store_3d(&tmD, sb, j * 32, a0, a1);
-          else if (MODE == MODE_GATE) tma_store_3d(&tmD, sb, a1, j * 32, a0);
-          else
-#pragma unroll
-            for (int g = 0; g < 4; ++g)
-              if (a0 + g < p.groups) tma_store_3d(&tmD, sb + g * 4096, a1, a0 + g, j * 32);
-          bulk_commit();
-          bulk_wait_read<1>();
+          for (int i = 0; i < 4; ++i)
+            rowp[(h * 4 + i) ^ (lane & 7)] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
         }
       }
-      tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
+      if (j == N / 32 - 1) {
+        // Everything this tile needs from TMEM has been read.
+        tc_fence_before();
+        mbar_arrive(&acc_empty[set]);
+        ++use;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int col = n0 + j * 32;
+        if (MODE == MODE_CONV1) {
+          tma_store_2d(&tmD, sb, col, a0 + 32 * q);
+        } else if (SPATIAL) {
+          tma_store_3d(&tmD, sb, col, a0, a1 + 2 * q);
+        } else if (a0 + q < p.groups) {
+          if (MODE == MODE_GATE) {
+            tma_store_3d(&tmD, sb, a1, col, a0 + q);
+          } else if (MODE == MODE_GATE_GRID) {
+            tma_store_3d(&tmD, sb, a1, a0 + q, col);
+          } else {
+            int fx, gx, fy, gy;
+            gate_sp_coords(p, a0 + q, col, fx, gx, fy, gy);
+            tma_store_5d(&tmD, sb, a1, fx, gx, fy, gy);
+          }
+        }
+        bulk_commit();
+      }
+      if (++j == N / 32) j = 0, t += tstep;
+      if (has_e && t < p.tiles) load_e(t, j, ecur);
+      return true;
+    };
+
+    float e[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) e[i] = 0.0f;
+    if (has_e && t < p.tiles) load_e(t, 0, e);
+    while (t < p.tiles && step(e)) {
     }
-    if (et == 0) bulk_wait<0>();
+    if (lane == 0) bulk_wait<0>();
   }
 
   tc_fence_before();

@@ -1,0 +1,412 @@
+// The executor's schedule: fusion, block-permutation removal and arena packing
+// over a plan's op list. The plan's semantics are src/model.rs:66-112 (ops) and
+// src/model.rs:1237-1272 (buffers, views, offsets); the reference packs the
+// arena for its own op list (src/model.rs, Builder::finish), which is the
+// layout the executor keeps for op-by-op stepping. This file packs afresh for
+// the rewritten list with the same rule: first fit over live ranges.
+#include "schedule.h"
+
+#include <algorithm>
+#include <climits>
+#include <cstdint>
+
+#include "common.h"
+
+namespace mx {
+namespace {
+
+constexpr int32_t kNative = -1;  // data stored in the order the plan says
+
+// Buffer geometry: every buffer is a channel range [lo, hi) of a root.
+struct Geo {
+  std::vector<int32_t> root;
+  std::vector<int64_t> lo, hi;
+
+  explicit Geo(const mx_plan& p) : root(size_t(p.n_bufs)), lo(size_t(p.n_bufs)), hi(size_t(p.n_bufs)) {
+    for (int32_t b = 0; b < p.n_bufs; ++b) {
+      int32_t r = b, guard_steps = 0;
+      while (p.alias_parent[r] >= 0) {
+        r = p.alias_parent[r];
+        if (++guard_steps > p.n_bufs) throw Error("plan: the buffer views form a cycle");
+      }
+      root[size_t(b)] = r;
+      const mx_buf& rb = p.bufs[r];
+      const mx_buf& bb = p.bufs[b];
+      const int64_t hw = rb.h * rb.w, delta = p.offs[b] - p.offs[r];
+      if (bb.h * bb.w != hw || (hw > 0 && delta % hw != 0) || delta < 0)
+        throw Error(fmt("plan: buffer %d is a view of %d that is not a channel range", b, r));
+      lo[size_t(b)] = hw > 0 ? delta / hw : 0;
+      hi[size_t(b)] = lo[size_t(b)] + bb.c;
+      if (hi[size_t(b)] > rb.c) throw Error(fmt("plan: view %d runs past the channels of %d", b, r));
+    }
+  }
+  bool overlap(int32_t a, int32_t b) const {
+    if (a < 0 || b < 0) return false;
+    return root[size_t(a)] == root[size_t(b)] && lo[size_t(a)] < hi[size_t(b)] && lo[size_t(b)] < hi[size_t(a)];
+  }
+  bool covers(int32_t a, int32_t t) const {
+    return root[size_t(a)] == root[size_t(t)] && lo[size_t(a)] <= lo[size_t(t)] && hi[size_t(t)] <= hi[size_t(a)];
+  }
+  bool whole(int32_t a) const { return lo[size_t(a)] == 0 && hi[size_t(a)] == hi[size_t(root[size_t(a)])]; }
+};
+
+bool per_pixel_unary(int k) {
+  return k == MX_OP_COPY || k == MX_OP_GELU || k == MX_OP_LRELU || k == MX_OP_SIGMOID || k == MX_OP_CHAN_LN ||
+         k == MX_OP_CONV1X1;
+}
+bool per_pixel_binary(int k) { return k == MX_OP_ADD || k == MX_OP_MUL || k == MX_OP_GATE_APPLY; }
+bool elementwise(int k) { return k <= MX_OP_SIGMOID; }
+
+int writes_of(const mx_op& o, int32_t* w) {
+  int n = 0;
+  w[n++] = o.dst;
+  if (o.kind == MX_OP_RESIZE && o.tmp >= 0) w[n++] = o.tmp;
+  return n;
+}
+int reads_of(const mx_op& o, int32_t extra, int32_t* r) {
+  int n = 0;
+  if (o.src >= 0) r[n++] = o.src;
+  if (o.src2 >= 0) r[n++] = o.src2;
+  if (extra >= 0) r[n++] = extra;
+  return n;
+}
+
+// The outcome of dropping a set of forward block permutations.
+struct PermSim {
+  std::vector<int32_t> src, src2;  // per op: inputs with dropped permutations' outputs resolved
+  std::vector<int32_t> gate_perm;  // per op
+  std::vector<char> to_copy;       // per op: a backward permutation that became a Copy
+};
+
+// Walk the plan with the forward permutations in `drop` removed: the removed
+// permutation's output is read from its (spatial) input instead, and every
+// buffer carries the pixel order it is really stored in. Succeeds when every
+// op sees inputs in an order it can handle: per-pixel ops any order (all
+// inputs alike), gating matmuls a blocked order they can read through a
+// tensor map, backward permutations the order they undo (they become
+// Copies), everything else the plan's own order.
+bool simulate(const mx_plan& p, const Geo& G, const ScheduleHooks& H, const std::vector<char>& drop, PermSim& out) {
+  const int n = p.n_ops;
+  std::vector<int32_t> subst(size_t(p.n_bufs), -1), sub_ord(size_t(p.n_bufs), kNative);
+  std::vector<int32_t> rord(size_t(p.n_bufs), kNative);
+  std::vector<char> written(size_t(p.n_bufs), 0);
+  out.src.assign(size_t(n), -1);
+  out.src2.assign(size_t(n), -1);
+  out.gate_perm.assign(size_t(n), -1);
+  out.to_copy.assign(size_t(n), 0);
+  struct Active {
+    int32_t y, x;
+    int last;
+  };
+  std::vector<Active> active;
+  for (int k = 0; k < n; ++k) {
+    const mx_op& o = p.ops[k];
+    for (size_t a = 0; a < active.size();) {
+      if (active[a].last < k) {
+        subst[size_t(active[a].y)] = -1;
+        active.erase(active.begin() + long(a));
+      } else {
+        ++a;
+      }
+    }
+    const int32_t in[2] = {o.src, o.src2};
+    for (int32_t b : in)
+      for (const Active& a : active)
+        if (b >= 0 && G.overlap(b, a.y) && b != a.y) return false;  // a partial read of a dropped output
+    auto ord = [&](int32_t b) { return subst[size_t(b)] >= 0 ? sub_ord[size_t(b)] : rord[size_t(G.root[size_t(b)])]; };
+    auto res = [&](int32_t b) { return b >= 0 && subst[size_t(b)] >= 0 ? subst[size_t(b)] : b; };
+    out.src[size_t(k)] = res(o.src);
+    out.src2[size_t(k)] = res(o.src2);
+
+    if (o.kind == MX_OP_BLOCK_PERM && o.forward && drop[size_t(k)]) {
+      const int32_t x = o.src, y = o.dst;
+      if (o.swap != 0 || subst[size_t(x)] >= 0 || ord(x) != kNative) return false;
+      if (G.root[size_t(y)] != y || G.overlap(y, p.output) || G.overlap(y, p.input)) return false;
+      int last = -1;
+      for (int m = k + 1; m < n; ++m) {
+        const mx_op& q = p.ops[m];
+        int32_t r[3], w[2];
+        const int nr = reads_of(q, -1, r), nw = writes_of(q, w);
+        for (int i = 0; i < nr; ++i)
+          if (G.overlap(r[i], y)) last = m;
+        bool rewritten = false;
+        for (int i = 0; i < nw; ++i) rewritten |= G.overlap(w[i], y);
+        if (rewritten) break;
+      }
+      subst[size_t(y)] = x;
+      sub_ord[size_t(y)] = k;
+      active.push_back({y, x, last});
+      continue;
+    }
+
+    int32_t out_ord = kNative;
+    if (per_pixel_unary(o.kind)) {
+      out_ord = ord(o.src);
+    } else if (per_pixel_binary(o.kind)) {
+      out_ord = ord(o.src);
+      if (ord(o.src2) != out_ord) return false;
+    } else if (o.kind == MX_OP_CHAN_SCALE) {
+      out_ord = ord(o.src);
+      if (ord(o.src2) != kNative) return false;  // the per-channel scale vector
+    } else if (o.kind == MX_OP_GATE_MM) {
+      out_ord = ord(o.src);
+      if (out_ord != kNative) {
+        const mx_op& P = p.ops[out_ord];
+        if (o.c != P.c || int64_t(o.outer) != int64_t(P.gh) * P.gw || int64_t(o.inner) != int64_t(P.fh) * P.fw ||
+            !H.gate_spatial(o, P))
+          return false;
+        out.gate_perm[size_t(k)] = out_ord;
+      }
+    } else if (o.kind == MX_OP_BLOCK_PERM && !o.forward) {
+      const int32_t q = ord(o.src);
+      if (q != kNative) {
+        const mx_op& P = p.ops[q];
+        if (P.gh != o.gh || P.gw != o.gw || P.fh != o.fh || P.fw != o.fw || P.swap != o.swap || P.h != o.h ||
+            P.wd != o.wd || P.c != o.c)
+          return false;
+        out.to_copy[size_t(k)] = 1;
+      }
+    } else {
+      for (int32_t b : in)
+        if (b >= 0 && ord(b) != kNative) return false;
+    }
+
+    int32_t w[2];
+    const int nw = writes_of(o, w);
+    for (int i = 0; i < nw; ++i) {
+      for (const Active& a : active)
+        if (G.overlap(w[i], a.x) || G.overlap(w[i], a.y)) return false;
+      const int32_t r = G.root[size_t(w[i])];
+      const int32_t wo = i == 0 ? out_ord : kNative;
+      if (G.whole(w[i]) || !written[size_t(r)]) rord[size_t(r)] = wo;
+      else if (rord[size_t(r)] != wo) return false;
+      written[size_t(r)] = 1;
+    }
+  }
+  return rord[size_t(G.root[size_t(p.output)])] == kNative;
+}
+
+// The channel count of a tensor-core step's output tile rows.
+int out_channels(const mx_op& o) { return o.kind == MX_OP_GATE_MM ? o.c : o.c_out; }
+
+}  // namespace
+
+Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
+  const Geo G(p);
+  const int n = p.n_ops;
+  Schedule S;
+
+  // 1. Block permutations.
+  std::vector<char> drop(size_t(n), 0);
+  PermSim sim;
+  if (fuse) {
+    std::vector<int> cand;
+    for (int k = 0; k < n; ++k)
+      if (p.ops[k].kind == MX_OP_BLOCK_PERM && p.ops[k].forward && p.ops[k].swap == 0) cand.push_back(k);
+    for (int k : cand) drop[size_t(k)] = 1;
+    if (!simulate(p, G, H, drop, sim)) {
+      for (int k : cand) drop[size_t(k)] = 0;
+      for (int k : cand) {
+        drop[size_t(k)] = 1;
+        if (!simulate(p, G, H, drop, sim)) drop[size_t(k)] = 0;
+      }
+    }
+  }
+  if (!simulate(p, G, H, drop, sim)) throw Error("schedule: the plan's own op order failed the pixel-order check");
+
+  std::vector<SchedStep> W;
+  W.reserve(size_t(n));
+  for (int k = 0; k < n; ++k) {
+    if (drop[size_t(k)]) {
+      ++S.perms_dropped;
+      continue;
+    }
+    SchedStep s;
+    s.o = p.ops[k];
+    s.o.src = sim.src[size_t(k)];
+    s.o.src2 = sim.src2[size_t(k)];
+    if (sim.to_copy[size_t(k)]) {
+      s.o.kind = MX_OP_COPY;
+      s.o.n = int64_t(s.o.c) * s.o.h * s.o.wd;
+    }
+    s.op = k;
+    s.covers.push_back(k);
+    s.gate_perm = sim.gate_perm[size_t(k)];
+    W.push_back(std::move(s));
+  }
+
+  // 2. Fold single consumers into their producers.
+  std::vector<char> dead(W.size(), 0);
+  for (size_t i = 0; fuse && i < W.size(); ++i) {
+    if (dead[i]) continue;
+    for (;;) {
+      SchedStep& A = W[i];
+      const int32_t T = A.o.dst;
+      if (G.overlap(T, p.output) || A.o.kind == MX_OP_CHAN_MEAN) break;
+      size_t j = SIZE_MAX;
+      bool ok = true;
+      for (size_t s = i + 1; s < W.size() && ok; ++s) {
+        if (dead[s]) continue;
+        int32_t r[3], w[2];
+        const int nr = reads_of(W[s].o, W[s].epi_src, r), nw = writes_of(W[s].o, w);
+        for (int a = 0; a < nr; ++a)
+          if (G.overlap(r[a], T)) {
+            if (j != SIZE_MAX || r[a] != T) ok = false;
+            else j = s;
+          }
+        bool gone = false;
+        for (int a = 0; a < nw; ++a)
+          if (G.overlap(w[a], T)) {
+            if (G.covers(w[a], T)) gone = true;
+            else ok = false;
+          }
+        if (gone) break;
+      }
+      if (!ok || j == SIZE_MAX) break;
+      const SchedStep& B = W[j];
+      int epi = -1;
+      int32_t operand = -1;
+      switch (B.o.kind) {
+        case MX_OP_COPY:
+          if (B.o.src == T) epi = EPI_NONE;
+          break;
+        case MX_OP_GELU:
+          if (B.o.src == T && B.o.src2 < 0) epi = EPI_GELU;
+          break;
+        case MX_OP_LRELU:
+          if (B.o.src == T && B.o.src2 < 0) epi = EPI_LRELU;
+          break;
+        case MX_OP_SIGMOID:
+          if (B.o.src == T && B.o.src2 < 0) epi = EPI_SIGMOID;
+          break;
+        case MX_OP_ADD:
+        case MX_OP_MUL:
+          if ((B.o.src == T) != (B.o.src2 == T)) {
+            epi = B.o.kind == MX_OP_ADD ? EPI_ADD : EPI_MUL;
+            operand = B.o.src == T ? B.o.src2 : B.o.src;
+          }
+          break;
+        case MX_OP_GATE_APPLY:  // dst = u * (v + 1) with src = u, src2 = v
+          if (B.o.src2 == T && B.o.src != T) {
+            epi = EPI_GATE;
+            operand = B.o.src;
+          }
+          break;
+        default:
+          break;
+      }
+      if (epi < 0) break;
+      const int32_t D = B.o.dst;
+      const bool identity = epi == EPI_NONE;
+      const bool umma = H.umma(A.o);
+      if (identity) {
+        if (umma && !H.tma_view(D, out_channels(A.o))) break;
+      } else {
+        if (!umma || A.epi != EPI_NONE) break;
+        if (!H.tma_view(D, out_channels(A.o))) break;
+        if (operand >= 0 && !H.tma_view(operand, out_channels(A.o))) break;
+      }
+      // Dependences between the producer and the consumer's own position.
+      int32_t br[3];
+      const int nbr = reads_of(B.o, -1, br);
+      for (size_t s = i + 1; s < j && ok; ++s) {
+        if (dead[s]) continue;
+        int32_t r[3], w[2];
+        const int nr = reads_of(W[s].o, W[s].epi_src, r), nw = writes_of(W[s].o, w);
+        for (int a = 0; a < nw; ++a) {
+          for (int b = 0; b < nbr; ++b)
+            if (br[b] != T && G.overlap(w[a], br[b])) ok = false;
+          if (G.overlap(w[a], D)) ok = false;
+        }
+        for (int a = 0; a < nr; ++a)
+          if (G.overlap(r[a], D)) ok = false;
+      }
+      if (!ok) break;
+      // The destination against what the producer itself reads: an exact
+      // match is an in-place elementwise update (each value is read before
+      // the same thread writes it), anything else is refused.
+      int32_t ar[3];
+      const int nar = reads_of(A.o, A.epi_src, ar);
+      for (int a = 0; a < nar; ++a)
+        if (G.overlap(ar[a], D) && !(ar[a] == D && (elementwise(A.o.kind) || ar[a] == A.epi_src))) ok = false;
+      if (operand >= 0 && G.overlap(operand, D) && operand != D) ok = false;
+      if (operand >= 0 && operand == D && !umma) ok = false;
+      if (G.overlap(D, T) && D != T) ok = false;
+      if (!ok) break;
+      A.o.dst = D;
+      if (!identity) {
+        A.epi = epi;
+        A.epi_src = operand;
+        A.epi_slope = B.o.slope;
+      }
+      A.covers.insert(A.covers.end(), B.covers.begin(), B.covers.end());
+      dead[j] = 1;
+      S.ops_fused += int(B.covers.size());
+    }
+  }
+  for (size_t i = 0; i < W.size(); ++i)
+    if (!dead[i]) S.steps.push_back(std::move(W[i]));
+
+  // 3. Pack the roots the steps touch, by first fit over live ranges.
+  const int m = int(S.steps.size());
+  std::vector<int> first(size_t(p.n_bufs), INT_MAX), last(size_t(p.n_bufs), INT_MIN);
+  auto touch = [&](int32_t b, int t) {
+    if (b < 0) return;
+    const size_t r = size_t(G.root[size_t(b)]);
+    first[r] = std::min(first[r], t);
+    last[r] = std::max(last[r], t);
+  };
+  touch(p.input, -1);
+  touch(p.output, m);
+  for (int t = 0; t < m; ++t) {
+    int32_t r[3], w[2];
+    const int nr = reads_of(S.steps[size_t(t)].o, S.steps[size_t(t)].epi_src, r);
+    const int nw = writes_of(S.steps[size_t(t)].o, w);
+    for (int a = 0; a < nr; ++a) touch(r[a], t);
+    for (int a = 0; a < nw; ++a) touch(w[a], t);
+  }
+  struct Slot {
+    int32_t root;
+    int64_t size, off;
+  };
+  std::vector<Slot> order;
+  for (int32_t b = 0; b < p.n_bufs; ++b)
+    if (G.root[size_t(b)] == b && first[size_t(b)] <= last[size_t(b)]) {
+      const mx_buf& bb = p.bufs[b];
+      const int64_t len = bb.c * bb.h * bb.w;
+      order.push_back({b, (len + 63) / 64 * 64, 0});
+    }
+  std::stable_sort(order.begin(), order.end(), [&](const Slot& a, const Slot& b) {
+    if (a.size != b.size) return a.size > b.size;
+    return first[size_t(a.root)] < first[size_t(b.root)];
+  });
+  std::vector<int64_t> root_off(size_t(p.n_bufs), 0);
+  std::vector<std::pair<int64_t, int64_t>> busy;
+  for (size_t i = 0; i < order.size(); ++i) {
+    Slot& s = order[i];
+    busy.clear();
+    for (size_t k = 0; k < i; ++k) {
+      const Slot& q = order[k];
+      if (first[size_t(q.root)] <= last[size_t(s.root)] && first[size_t(s.root)] <= last[size_t(q.root)])
+        busy.push_back({q.off, q.off + q.size});
+    }
+    std::sort(busy.begin(), busy.end());
+    int64_t off = 0;
+    for (const auto& iv : busy) {
+      if (off + s.size <= iv.first) break;
+      off = std::max(off, iv.second);
+    }
+    s.off = off;
+    root_off[size_t(s.root)] = off;
+    S.arena_len = std::max(S.arena_len, off + s.size);
+  }
+  S.offs.resize(size_t(p.n_bufs));
+  for (int32_t b = 0; b < p.n_bufs; ++b) {
+    const int32_t r = G.root[size_t(b)];
+    S.offs[size_t(b)] = root_off[size_t(r)] + (p.offs[b] - p.offs[r]);
+  }
+  S.arena_len = std::max<int64_t>(S.arena_len, 64);
+  return S;
+}
+
+}  // namespace mx

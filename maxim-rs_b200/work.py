@@ -52,6 +52,38 @@ def op_work(plan, op):
     return 0, 0
 
 
+# Ops a tensor-core step can apply in its epilogue (the step's family names them).
+TAILS = ("gelu", "lrelu", "sigmoid", "add", "mul", "gate_apply")
+
+
+def schedule_steps(primary):
+    """{primary op: [ops it carries out, primary first]} from the executor's
+    schedule (`Gpu.schedule()` / `plan_schedule`); dropped ops are left out."""
+    out = collections.OrderedDict()
+    for i, p in enumerate(primary):
+        if p >= 0:
+            out.setdefault(int(p), []).append(i)
+    return out
+
+
+def step_work(plan, ops, members):
+    """(family, flops, bytes) of one scheduled step. The members' own work,
+    less what fusion removes: each absorbed op (an epilogue or a forwarded
+    Copy) consumed a tensor its producer no longer writes and it no longer
+    reads, the size of its own output."""
+    p = members[0]
+    f, b = op_work(plan, ops[p])
+    fam = [KINDS[ops[p].kind]]
+    for j in members[1:]:
+        fj, bj = op_work(plan, ops[j])
+        c, h, w = plan.buf(ops[j].dst)
+        f += fj
+        b += bj - 8 * c * h * w
+        if KINDS[ops[j].kind] in TAILS:
+            fam.append(KINDS[ops[j].kind])
+    return "+".join(fam), f, b
+
+
 def census(plan):
     """{kind: [ops, flops, bytes]} over the whole plan."""
     out = collections.OrderedDict()

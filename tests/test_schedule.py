@@ -1,0 +1,69 @@
+"""The executor's schedule of a plan, worked out on the host (no device):
+which ops fuse into which, which block permutations go, and the re-packed
+arena. The GPU tests check the fused pass computes the same values; these
+check the schedule's shape and its liveness-safe packing rules on CPU."""
+import os
+
+import numpy as np
+import pytest
+
+BLOCK_PERM, GATE_MM, CONV1X1, CONV3X3, GELU, ADD, COPY, GATE_APPLY = 15, 14, 10, 11, 4, 1, 0, 3
+
+
+def _sched(mx, plan, fuse=True):
+    if fuse:
+        return mx.plan_schedule(plan)
+    os.environ["MAXIM_NO_FUSE"] = "1"
+    try:
+        return mx.plan_schedule(plan)
+    finally:
+        del os.environ["MAXIM_NO_FUSE"]
+
+
+@pytest.mark.parametrize("variant,h,w", [("S-2", 64, 64), ("S-3", 256, 320), ("S-3", 896, 1280)])
+def test_schedule_shape(variant, h, w, mx):
+    plan = mx.Plan(None, h, w, variant=variant)
+    ops = plan.ops()
+    st, primary = _sched(mx, plan)
+    kinds = np.array([o.kind for o in ops])
+    forward = np.array([o.kind == BLOCK_PERM and o.forward for o in ops])
+    # Every forward block permutation goes (the gating reads the blocks in
+    # place); nothing else is removed outright.
+    assert st["perms_dropped"] == forward.sum()
+    assert ((primary < 0) == forward).all()
+    # An absorbed op runs in the step of an earlier op.
+    idx = np.arange(len(ops))
+    assert (primary[primary >= 0] <= idx[primary >= 0]).all()
+    assert st["steps"] == (primary == idx).sum()
+    assert st["ops_fused"] == ((primary >= 0) & (primary != idx)).sum()
+    # Every GELU after a tensor-core 1x1 conv is that conv's epilogue, and
+    # every backward permutation (now a Copy) is forwarded into its producer.
+    for i in np.nonzero(kinds == GELU)[0]:
+        assert kinds[primary[i]] == CONV1X1
+    for i in np.nonzero((kinds == BLOCK_PERM) & ~forward)[0]:
+        assert primary[i] != i
+    # The re-packed arena is no larger than the plan's.
+    assert st["pass_arena_bytes"] <= st["arena_bytes"]
+
+
+def test_schedule_off_keeps_every_op(mx):
+    plan = mx.Plan(None, 128, 192, variant="S-2")
+    st, primary = _sched(mx, plan, fuse=False)
+    assert st["ops_fused"] == 0 and st["perms_dropped"] == 0
+    assert (primary == np.arange(plan.n_ops)).all()
+    assert st["steps"] == plan.n_ops
+
+
+def test_schedule_without_tensor_cores_fuses_only_copies(mx):
+    """With the tensor-core kernel off nothing has an epilogue: only Copies are
+    forwarded, and block permutations stay (the SIMT gating reads blocks)."""
+    plan = mx.Plan(None, 64, 64, variant="S-2")
+    os.environ["MAXIM_NO_UMMA"] = "1"
+    try:
+        st, primary = mx.plan_schedule(plan)
+    finally:
+        del os.environ["MAXIM_NO_UMMA"]
+    kinds = np.array([o.kind for o in plan.ops()])
+    assert st["perms_dropped"] == 0
+    moved = (primary >= 0) & (primary != np.arange(plan.n_ops))
+    assert moved.any() and (kinds[moved] == COPY).all()
