@@ -222,9 +222,10 @@ def run_timeline(args):
     ops = plan.ops()
     fam = collections.defaultdict(lambda: [0, 0.0, 0, 0])
     shp = collections.defaultdict(lambda: [0, 0.0, 0, 0])
-    for p, members in work.schedule_steps(gpu.schedule()).items():
+    prim, flags = gpu.schedule(flags=True)
+    for p, members in work.schedule_steps(prim).items():
         o = ops[p]
-        k, f, b = work.step_work(plan, ops, members)
+        k, f, b = work.step_work(plan, ops, members, flags)
         kind = work.KINDS[o.kind]
         if kind in ("conv1x1", "conv3x3", "conv4x4s2", "convt2x2"):
             d = "%s %d->%d @%dx%d" % (k, o.c_in, o.c_out, o.h, o.wd)
@@ -345,8 +346,9 @@ def run_native(args):
     gpu.set_timeline(False)
     fam = {}
     ops = plan.ops()
-    for p, members in work.schedule_steps(gpu.schedule()).items():
-        k, f, b = work.step_work(plan, ops, members)
+    prim, flags = gpu.schedule(flags=True)
+    for p, members in work.schedule_steps(prim).items():
+        k, f, b = work.step_work(plan, ops, members, flags)
         e = fam.setdefault(k, [0, 0.0, 0, 0])
         e[0] += 1
         e[1] += float(per[p])

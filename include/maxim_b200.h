@@ -200,14 +200,20 @@ int mx_gpu_get_stats(mx_gpu* g, mx_gpu_stats* s);
 
 /* Which scheduled step carries out each plan op: primary[i] is the plan op
  * whose step runs op i (i itself when it is not fused), -1 for an op the
- * schedule removed. n_ops must be the plan's op count. No counterpart in the
- * reference (its executor runs every op as its own launch). */
-int mx_gpu_schedule(mx_gpu* g, int32_t* primary, int32_t n_ops);
+ * schedule removed. flags[i] (may be null): MX_SCHED_STATS_ONLY when op i, a
+ * channel LayerNorm, only computes its per-pixel statistics;
+ * MX_SCHED_LN_ON_LOAD when op i, a conv, normalises its input with such
+ * statistics as it loads it. n_ops must be the plan's op count. No
+ * counterpart in the reference (its executor runs every op as its own
+ * launch). */
+enum { MX_SCHED_STATS_ONLY = 1, MX_SCHED_LN_ON_LOAD = 2 };
+int mx_gpu_schedule(mx_gpu* g, int32_t* primary, int32_t* flags, int32_t n_ops);
 
 /* The same schedule worked out on the host alone, without a device: for
  * tests and tools. `stats` receives steps / ops_fused / perms_dropped /
- * pass_arena_bytes (other fields zero); `primary` as above (may be null). */
-int mx_plan_schedule(const mx_plan* plan, mx_gpu_stats* stats, int32_t* primary, int32_t n_ops);
+ * pass_arena_bytes (other fields zero); `primary` and `flags` as above (may
+ * be null). */
+int mx_plan_schedule(const mx_plan* plan, mx_gpu_stats* stats, int32_t* primary, int32_t* flags, int32_t n_ops);
 
 /* The per-channel mean (the CALayer squeeze) of an NHWC tensor in device
  * memory, computed without allocating anything. This entry point has no

@@ -88,9 +88,9 @@ _SIGS = {
     "mx_gpu_timeline": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                        ctypes.POINTER(ctypes.c_float)]),
     "mx_gpu_get_stats": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(mx_gpu_stats)]),
-    "mx_gpu_schedule": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32]),
+    "mx_gpu_schedule": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32]),
     "mx_plan_schedule": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(mx_gpu_stats), ctypes.c_void_p,
-                                        ctypes.c_int32]),
+                                        ctypes.c_void_p, ctypes.c_int32]),
     "mx_channel_mean_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int64,
                                                ctypes.c_void_p, ctypes.c_void_p]),
     "mx_weights_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
@@ -350,11 +350,13 @@ class Gpu:
         check(lib().mx_gpu_get_stats(self._h, ctypes.byref(s)))
         return _stats_dict(s)
 
-    def schedule(self):
-        """Per plan op, the op whose scheduled step carries it out (-1: removed)."""
+    def schedule(self, flags=False):
+        """Per plan op, the op whose scheduled step carries it out (-1: removed);
+        with flags=True also the per-op SCHED_* flags."""
         out = np.zeros(self.plan.n_ops, np.int32)
-        check(lib().mx_gpu_schedule(self._h, _ptr(out), self.plan.n_ops), "schedule")
-        return out
+        fl = np.zeros(self.plan.n_ops, np.int32)
+        check(lib().mx_gpu_schedule(self._h, _ptr(out), _ptr(fl), self.plan.n_ops), "schedule")
+        return (out, fl) if flags else out
 
 
 def _stats_dict(s):
@@ -363,14 +365,18 @@ def _stats_dict(s):
             "ops_fused": s.ops_fused, "perms_dropped": s.perms_dropped, "pass_arena_bytes": s.pass_arena_bytes}
 
 
-def plan_schedule(plan):
+SCHED_STATS_ONLY, SCHED_LN_ON_LOAD = 1, 2
+
+
+def plan_schedule(plan, flags=False):
     """`mx_plan_schedule`: the executor's schedule of a plan, worked out on the
-    host: (stats dict, per-op primary op array)."""
+    host: (stats dict, per-op primary op array[, per-op SCHED_* flags])."""
     s = mx_gpu_stats()
     out = np.zeros(plan.n_ops, np.int32)
-    check(lib().mx_plan_schedule(ctypes.cast(plan.view, ctypes.c_void_p), ctypes.byref(s), _ptr(out), plan.n_ops),
-          "plan schedule")
-    return _stats_dict(s), out
+    fl = np.zeros(plan.n_ops, np.int32)
+    check(lib().mx_plan_schedule(ctypes.cast(plan.view, ctypes.c_void_p), ctypes.byref(s), _ptr(out), _ptr(fl),
+                                 plan.n_ops), "plan schedule")
+    return (_stats_dict(s), out, fl) if flags else (_stats_dict(s), out)
 
 
 def channel_mean_noalloc(x_ptr, npix, c, pixel_stride, out_ptr, stream=0):

@@ -204,6 +204,7 @@ struct mx_gpu {
   std::vector<int64_t> foffs;   // the scheduled pass's offsets
   std::vector<mx::Step> fsteps; // the scheduled pass: [in-transpose, steps..., out-transpose]
   std::vector<int32_t> primary_of;  // plan op -> the op whose step carries it out (-1: dropped)
+  std::vector<int32_t> sched_flags; // plan op -> MX_SCHED_* flags
   int64_t farena_len = 0;
   int perms_dropped = 0, ops_fused = 0;
   std::map<std::pair<int32_t, int>, int64_t> wcache;  // (weight id, layout tag) -> pool offset
@@ -348,16 +349,17 @@ void umma_attrs_once() {
   if (done) return;
 #define MX_UMMA_ATTR(NN, MM)                                                                       \
   MX_CUDA(cudaFuncSetAttribute(umma_conv_kernel<NN, MM>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                               UmmaCfg<NN>::SMEM_BYTES));
+                               UmmaCfg<NN, umma_tmem_a(NN, MM)>::SMEM_BYTES));
   MX_UMMA_INSTANCES(MX_UMMA_ATTR)
 #undef MX_UMMA_ATTR
   done = true;
 }
-int umma_smem(int n) {
+int umma_smem(int n, int mode) {
+  const bool ta = umma_tmem_a(n, mode);
   switch (n) {
-    case 32: return UmmaCfg<32>::SMEM_BYTES;
-    case 64: return UmmaCfg<64>::SMEM_BYTES;
-    default: return UmmaCfg<128>::SMEM_BYTES;
+    case 32: return ta ? UmmaCfg<32, true>::SMEM_BYTES : UmmaCfg<32, false>::SMEM_BYTES;
+    case 64: return ta ? UmmaCfg<64, true>::SMEM_BYTES : UmmaCfg<64, false>::SMEM_BYTES;
+    default: return UmmaCfg<128, false>::SMEM_BYTES;
   }
 }
 
@@ -400,6 +402,8 @@ struct UmmaEpi {
   float slope = 0.0f;
   bool spatial = false;
   mx_op perm{};
+  int32_t ln_stats = -1;                 // LayerNorm on load: statistics buffer
+  int64_t ln_scale = -1, ln_bias = -1;  // and the pool offsets of its weights
 };
 
 // The tensor-core step of a gating matmul. Over a blocked buffer (pixels in
@@ -498,7 +502,7 @@ Step umma_gate_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
     u->n = tn;
     u->taps = 1;
     u->grid = std::min(u->p.tiles, G->sms);
-    u->smem = umma_smem(tn);
+    u->smem = umma_smem(tn, u->mode);
   };
   st.run = [u](cudaStream_t s) { launch_umma(s, *u); };
   return st;
@@ -531,6 +535,13 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
     }
     u->p.eptr = E.epi >= EPI_ADD ? e.ptr : nullptr;
     u->p.estride = int(e.stride);
+    if (E.ln_stats >= 0) {
+      u->p.ln_stats = reinterpret_cast<const float2*>(view_of(*G, *L, E.ln_stats).ptr);
+      u->p.ln_scale = reinterpret_cast<const float*>(G->pool.dev + E.ln_scale);
+      u->p.ln_bias = reinterpret_cast<const float*>(G->pool.dev + E.ln_bias);
+      u->p.in_w = taps == 1 ? int(x.npix) : W;
+      u->p.in_h = H;
+    }
     if (taps == 1) {
       uint64_t da[2] = {uint64_t(ci), uint64_t(x.npix)}, sa[1] = {uint64_t(x.stride) * 4};
       uint32_t ba[2] = {32, 128};
@@ -579,7 +590,7 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
     u->taps = taps;
     u->mode = taps == 9 ? MODE_CONV3 : (taps == 16 ? MODE_CONV4 : MODE_CONV1);
     u->grid = std::min(u->p.tiles, G->sms);
-    u->smem = umma_smem(tn);
+    u->smem = umma_smem(tn, u->mode);
   };
   st.run = [u](cudaStream_t s) { launch_umma(s, *u); };
   return st;
@@ -620,8 +631,13 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
       E.spatial = true;
       E.perm = plan.ops[fs->gate_perm];
     }
+    if (fs->ln_stats >= 0) {
+      E.ln_stats = fs->ln_stats;
+      E.ln_scale = raw(fs->ln_scale);
+      E.ln_bias = raw(fs->ln_bias);
+    }
   }
-  const bool needs_umma = E.epi != EPI_NONE || E.spatial;
+  const bool needs_umma = E.epi != EPI_NONE || E.spatial || E.ln_stats >= 0;
   bool on_umma = false;
   mx_gpu* G = &g;
   auto P = [G](int64_t off) -> const float* {
@@ -660,6 +676,23 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
       break;
     }
     case MX_OP_CHAN_LN: {
+      if (fs && fs->stats_only) {
+        // The statistics half only (its consumer normalises on load).
+        st.run = [G, L, dst, src](cudaStream_t s) {
+          View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
+          const int c = int(x.c), np = int(x.npix);
+          const int pb = c <= 64 ? 128 : (c == 128 ? 64 : 32);
+          const unsigned grid = unsigned((np + pb - 1) / pb);
+          const size_t smem = size_t(pb) * (c + 1) * sizeof(float);
+          float2* sp = reinterpret_cast<float2*>(d.ptr);
+          const int sx = int(x.stride);
+          if (c == 32) chan_stats_tile_kernel<32><<<grid, 128, smem, s>>>(np, x.ptr, sx, sp, kLnEps);
+          else if (c == 64) chan_stats_tile_kernel<64><<<grid, 128, smem, s>>>(np, x.ptr, sx, sp, kLnEps);
+          else if (c == 128) chan_stats_tile_kernel<128><<<grid, 128, smem, s>>>(np, x.ptr, sx, sp, kLnEps);
+          else chan_stats_tile_kernel<256><<<grid, 128, smem, s>>>(np, x.ptr, sx, sp, kLnEps);
+        };
+        break;
+      }
       int64_t ws = raw(o.scale), wb = raw(o.bias);
       st.run = [G, L, P, dst, src, ws, wb](cudaStream_t s) {
         View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
@@ -947,6 +980,15 @@ ScheduleHooks schedule_hooks(const mx_gpu& g) {
     return umma_gate_spatial_ok(*G, G->roffs, gate, perm) && tma_view(*G, G->roffs, gate.dst, gate.c);
   };
   h.tma_view = [G](int32_t b, int n) { return tma_view(*G, G->roffs, b, n); };
+  // The split stage normalises A for 1x1 convs whose input has a channel
+  // count the statistics kernel takes (32..256, aligned rows). A 3x3 conv
+  // could too, but it would normalise every input pixel once per tap (nine
+  // times), which measured slower than the separate LayerNorm.
+  h.ln_on_load = [G](const mx_op& o) {
+    if (o.kind != MX_OP_CONV1X1) return false;
+    const int c = o.c_in;
+    return (c == 32 || c == 64 || c == 128 || c == 256) && tma_view(*G, G->roffs, o.src, c);
+  };
   return h;
 }
 
@@ -1086,15 +1128,24 @@ int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) {
     }
     add_boundary_steps(*g, g->steps, &g->offs);
 
-    // The scheduled pass, at its own offsets.
+    // The scheduled pass, at its own offsets, over the plan's buffers and the
+    // ones the schedule adds (LayerNorm statistics).
+    for (const mx_buf& b : S.extra) {
+      g->bufs.push_back(b);
+      g->alias_parent.push_back(-1);
+      g->roffs.push_back(0);
+    }
     g->foffs = S.offs;
     g->farena_len = S.arena_len;
     g->perms_dropped = S.perms_dropped;
     g->ops_fused = S.ops_fused;
     g->primary_of.assign(size_t(plan->n_ops), -1);
+    g->sched_flags.assign(size_t(plan->n_ops), 0);
     for (const SchedStep& ss : S.steps) {
       g->fsteps.push_back(make_step(*g, *plan, ss.o, ss.op, &g->foffs, &ss));
       for (int32_t c : ss.covers) g->primary_of[size_t(c)] = ss.op;
+      g->sched_flags[size_t(ss.op)] = (ss.stats_only ? MX_SCHED_STATS_ONLY : 0) |
+                                      (ss.ln_stats >= 0 ? MX_SCHED_LN_ON_LOAD : 0);
     }
     add_boundary_steps(*g, g->fsteps, &g->foffs);
     for (auto& st : g->fsteps) g->kernels += st.kernels;
@@ -1296,7 +1347,7 @@ int mx_gpu_step_op(mx_gpu* g, int32_t i) {
 
 int mx_gpu_read_buf(mx_gpu* g, int32_t id, float* out, int64_t len) {
   return guard([&] {
-    if (!g || !out || id < 0 || size_t(id) >= g->bufs.size()) throw Error("mx_gpu_read_buf: bad argument");
+    if (!g || !out || id < 0 || size_t(id) >= g->offs.size()) throw Error("mx_gpu_read_buf: bad argument");
     if (len != len_of(g->bufs[size_t(id)])) throw Error("mx_gpu_read_buf: length does not match the buffer");
     DevicePin pin(g->device);
     View v = view_of(*g, g->offs, id);
@@ -1356,18 +1407,19 @@ int mx_gpu_get_stats(mx_gpu* g, mx_gpu_stats* s) {
   });
 }
 
-int mx_gpu_schedule(mx_gpu* g, int32_t* primary, int32_t n_ops) {
+int mx_gpu_schedule(mx_gpu* g, int32_t* primary, int32_t* flags, int32_t n_ops) {
   return guard([&] {
     if (!g || !primary) throw Error("mx_gpu_schedule: null argument");
     if (size_t(n_ops) != g->ops.size()) throw Error("mx_gpu_schedule: n_ops does not match the plan");
     memcpy(primary, g->primary_of.data(), g->primary_of.size() * sizeof(int32_t));
+    if (flags) memcpy(flags, g->sched_flags.data(), g->sched_flags.size() * sizeof(int32_t));
   });
 }
 
-int mx_plan_schedule(const mx_plan* plan, mx_gpu_stats* stats, int32_t* primary, int32_t n_ops) {
+int mx_plan_schedule(const mx_plan* plan, mx_gpu_stats* stats, int32_t* primary, int32_t* flags, int32_t n_ops) {
   return guard([&] {
     if (!plan || !stats) throw Error("mx_plan_schedule: null argument");
-    if (primary && n_ops != plan->n_ops) throw Error("mx_plan_schedule: n_ops does not match the plan");
+    if ((primary || flags) && n_ops != plan->n_ops) throw Error("mx_plan_schedule: n_ops does not match the plan");
     mx_gpu g;
     g.use_umma = std::getenv("MAXIM_NO_UMMA") == nullptr;
     const Schedule S = plan_schedule(g, *plan);
@@ -1382,6 +1434,11 @@ int mx_plan_schedule(const mx_plan* plan, mx_gpu_stats* stats, int32_t* primary,
       for (int32_t i = 0; i < n_ops; ++i) primary[i] = -1;
       for (const SchedStep& ss : S.steps)
         for (int32_t c : ss.covers) primary[c] = ss.op;
+    }
+    if (flags) {
+      for (int32_t i = 0; i < n_ops; ++i) flags[i] = 0;
+      for (const SchedStep& ss : S.steps)
+        flags[ss.op] = (ss.stats_only ? MX_SCHED_STATS_ONLY : 0) | (ss.ln_stats >= 0 ? MX_SCHED_LN_ON_LOAD : 0);
     }
   });
 }

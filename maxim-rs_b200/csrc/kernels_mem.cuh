@@ -90,6 +90,44 @@ __global__ void __launch_bounds__(128) chan_ln_tile_kernel(int npix, const float
   }
 }
 
+// The statistics half of the same LayerNorm, for a consumer that normalises
+// on load: per pixel (mean, 1 / sqrt(max(var, 0) + eps)) as two floats,
+// computed exactly as chan_ln_tile_kernel computes them.
+template <int C>
+__global__ void __launch_bounds__(128) chan_stats_tile_kernel(int npix, const float* __restrict__ x, int sx,
+                                                              float2* __restrict__ stats, float eps) {
+  constexpr int P = C <= 64 ? 128 : (C == 128 ? 64 : 32);
+  constexpr int C4 = C / 4, R = C + 1;
+  extern __shared__ float tile[];  // P * R
+  const int p0 = blockIdx.x * P;
+  const int np = min(P, npix - p0);
+  for (int idx = threadIdx.x; idx < np * C4; idx += 128) {
+    int r = idx / C4, c = (idx - r * C4) * 4;
+    float4 v = *reinterpret_cast<const float4*>(x + size_t(p0 + r) * sx + c);
+    float* t = tile + r * R + c;
+    t[0] = v.x;
+    t[1] = v.y;
+    t[2] = v.z;
+    t[3] = v.w;
+  }
+  __syncthreads();
+  if (threadIdx.x < np) {
+    const float* t = tile + threadIdx.x * R;
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll 8
+    for (int i = 0; i < C; ++i) {
+      float v = t[i];
+      s1 = __fadd_rn(s1, v);
+      s2 = __fadd_rn(s2, __fmul_rn(v, v));
+    }
+    const float nf = float(C);
+    float m = __fdiv_rn(s1, nf);
+    float var = __fsub_rn(__fdiv_rn(s2, nf), __fmul_rn(m, m));
+    float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(fmaxf(var, 0.0f), eps)));
+    stats[p0 + threadIdx.x] = make_float2(m, rstd);
+  }
+}
+
 // Per-channel mean over the pixels (the CALayer squeeze) in two deterministic
 // phases: block b sums its own pixel range per channel into part[b][c];
 // then one thread per channel adds the blocks' partials in block order.

@@ -88,6 +88,12 @@ struct UmmaConvParams {
   int e_npix;         // CONV1: output pixels
   int e_w, e_h;       // CONV3 / CONV4: output width, height; GATE_SP: image width
   int e_pp;           // GATE / GATE_GRID: pixels per block of the blocked buffer
+  // LayerNorm on load (CONV1 / CONV3): A = LN(x) with per-input-pixel
+  // (mean, rstd) and per-channel scale / bias; ln_stats null when off.
+  const float2* ln_stats;
+  const float* ln_scale;
+  const float* ln_bias;
+  int in_w, in_h;     // CONV1: input pixels in in_w; CONV3: input width, height
   const float* bias;  // per output column, or null
   int* status;        // device status word (0 = ok)
 };
@@ -137,20 +143,31 @@ __device__ __forceinline__ void epi_apply(int kind, float (&v)[16], const float 
   }
 }
 
-template <int N>
+// Whether a kernel instance keeps its A operand (the split hi / lo halves)
+// in TMEM rather than shared memory: the convolutions with N <= 64, where
+// the tensor core's reads of A (twice hi, once lo per k-step) would
+// otherwise dominate shared-memory bandwidth. TMEM then holds the two
+// accumulator sets (4N columns) and one 64-column A slot per stage.
+__host__ __device__ constexpr bool umma_tmem_a(int n, int mode) {
+  return n <= 64 && (mode == MODE_CONV1 || mode == MODE_CONV3 || mode == MODE_CONV4);
+}
+
+template <int N, bool TMEM_A>
 struct UmmaCfg {
-  static constexpr int STAGES = N <= 64 ? 4 : (N <= 128 ? 3 : 2);
   static constexpr int A_BYTES = 128 * 128;  // 128 rows x 32 fp32
   static constexpr int B_BYTES = N * 128;    // N rows x 32 fp32
-  static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+  // A stage holds A (and A_lo unless it lives in TMEM), B and B_lo.
+  static constexpr int STAGE_BYTES = (TMEM_A ? 1 : 2) * A_BYTES + 2 * B_BYTES;
+  static constexpr int STAGES = TMEM_A ? (N <= 32 ? 6 : 4) : (N <= 64 ? 4 : 3);
   static constexpr int STAGING_BYTES = 8 * 4096;  // one 32-row x 32-column buffer per epilogue warp
   // An accumulator set is two N-column fp32 regions: the hi*hi products and
-  // the two cross terms, summed once in the epilogue. Sets are double
-  // buffered (the epilogue drains one tile while the next accumulates) where
-  // two fit in the 512 TMEM columns.
-  static constexpr int ACC_SETS = 4 * N <= 512 ? 2 : 1;
-  static constexpr int TMEM_COLS = ACC_SETS * 2 * N;
+  // the two cross terms, summed once in the epilogue. Two sets: the epilogue
+  // drains one tile while the next accumulates.
+  static constexpr int ACC_SETS = 2;
+  static constexpr int A_COL0 = ACC_SETS * 2 * N;  // first TMEM column of the A slots
+  static constexpr int TMEM_COLS = TMEM_A ? 512 : ACC_SETS * 2 * N;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 8 * (3 * STAGES + 4) + 16;
+  static_assert(!TMEM_A || A_COL0 + STAGES * 64 <= 512, "TMEM holds the accumulators and the A slots");
 };
 
 enum : int {
@@ -161,14 +178,15 @@ enum : int {
   kErrEpilogue = 0x105,
 };
 
-// Round an fp32 value to the nearest TF32 value (ties to even), returned as
-// fp32 with the low 13 mantissa bits clear, so the tensor core reads it
-// exactly whatever it does with those bits. Finite inputs here are far below
-// the overflow threshold, so the carry never reaches the exponent's top.
-__device__ __forceinline__ float tf32_rne(float v) {
-  uint32_t b = __float_as_uint(v);
-  b = (b + 0xFFFu + ((b >> 13) & 1u)) & 0xFFFFE000u;
-  return __uint_as_float(b);
+// Round an fp32 value to the nearest TF32 value (ties away from zero) with
+// the conversion instruction, returned as fp32 with the low 13 mantissa bits
+// clear, so the tensor core reads it exactly whatever it does with those
+// bits. One instruction: the split of every A element costs three (hi, the
+// difference, lo), which keeps the split warps off the critical path.
+__device__ __forceinline__ float tf32_round(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
 }
 
 constexpr int kUmmaThreads = 448;
@@ -178,7 +196,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     umma_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmD,
                      UmmaConvParams p) {
-  using C = UmmaCfg<N>;
+  constexpr bool TMEM_A = umma_tmem_a(N, MODE);
+  using C = UmmaCfg<N, TMEM_A>;
   using namespace sm100;
   constexpr int TAPS = MODE == MODE_CONV3 ? 9 : (MODE == MODE_CONV4 ? 16 : 1);
   constexpr bool SPATIAL = MODE == MODE_CONV3 || MODE == MODE_CONV4;  // 8x16-pixel output tiles
@@ -186,7 +205,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   constexpr bool PER_GROUP = MODE == MODE_GATE_GRID || MODE == MODE_GATE_SP;  // one box per group
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* staging = base + C::STAGES * C::STAGE_BYTES;
+  uint8_t* staging = base + C::STAGES * C::STAGE_BYTES;  // 1024-byte aligned (stage sizes are multiples of 1 KB)
   uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES);
   uint64_t* lo_ready = full + C::STAGES;
   uint64_t* empty = lo_ready + C::STAGES;
@@ -310,8 +329,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
               }
           }
           const int kcol = tap * p.c_in + cb * 32;
-          tma_load_2d(st + 2 * C::A_BYTES, &tmB, &full[s], kcol, n0);
-          tma_load_2d(st + 2 * C::A_BYTES + C::B_BYTES, &tmBlo, &full[s], kcol, n0);
+          uint8_t* sbw = st + (TMEM_A ? 1 : 2) * C::A_BYTES;  // B follows A (and A_lo unless it lives in TMEM)
+          tma_load_2d(sbw, &tmB, &full[s], kcol, n0);
+          tma_load_2d(sbw + C::B_BYTES, &tmBlo, &full[s], kcol, n0);
         }
       }
     }
@@ -339,7 +359,23 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           }
           tc_fence_after();
           const uint32_t a = smem_u32(base + s * C::STAGE_BYTES);
-          const uint32_t alo = a + C::A_BYTES, b = a + 2 * C::A_BYTES, blo = b + C::B_BYTES;
+          const uint32_t b = a + (TMEM_A ? 1 : 2) * C::A_BYTES, blo = b + C::B_BYTES;
+          if (TMEM_A) {
+            // A_hi / A_lo of this stage sit in TMEM columns [slot, slot + 32)
+            // and [slot + 32, slot + 64); k-step k reads 8 of them.
+            const uint32_t slot = tmem + C::A_COL0 + s * 64;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t db = desc_kmajor_sw128(b + 32 * k), dblo = desc_kmajor_sw128(blo + 32 * k);
+              const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+              mma_tf32_ts(d, slot + 8 * k, db, idesc, accum);
+              mma_tf32_ts(dx, slot + 32 + 8 * k, db, idesc, accum);
+              mma_tf32_ts(dx, slot + 8 * k, dblo, idesc, 1u);
+            }
+            mma_commit(&empty[s]);
+            continue;
+          }
+          const uint32_t alo = a + C::A_BYTES;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             uint64_t da, dalo;
@@ -371,15 +407,93 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     // ------------------------------------------------------------ split
     const int tid = threadIdx.x - 64;  // 0..127
     uint32_t it = 0;
+    // LayerNorm on load: the statistics of the input pixel behind A row r of
+    // the current k-block, if that pixel is inside the image (rows outside
+    // it are zero padding, which stays zero).
+    int a0 = 0, a1 = 0, n0 = 0, cb = 0, ky = 0, kx = 0;
+    auto ln_row = [&](int r, float& m, float& rs) -> bool {
+      int pix = -1;
+      if (MODE == MODE_CONV1) {
+        if (a0 + r < p.in_w) pix = a0 + r;
+      } else if (MODE == MODE_CONV3) {
+        const int y = a1 + (r >> 4) + ky - 1, x = a0 + (r & 15) + kx - 1;
+        if (y >= 0 && y < p.in_h && x >= 0 && x < p.in_w) pix = y * p.in_w + x;
+      }
+      if (pix < 0) return false;
+      const float2 st = p.ln_stats[pix];
+      m = st.x, rs = st.y;
+      return true;
+    };
+    // (x - m) * rstd * scale + bias, in the LayerNorm kernel's exact order,
+    // over 4 channels from ch (a multiple of 4; every thread reads the same
+    // scale and bias, so the read-only cache serves them).
+    auto ln_apply4 = [&](float4 v, float m, float rs, int ch) {
+      const float4 w = __ldg(reinterpret_cast<const float4*>(p.ln_scale + ch));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(p.ln_bias + ch));
+      v.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, m), rs), w.x), b.x);
+      v.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, m), rs), w.y), b.y);
+      v.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, m), rs), w.z), b.z);
+      v.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, m), rs), w.w), b.w);
+      return v;
+    };
     for (int t = blockIdx.x; t < p.tiles && !*vabort; t += gridDim.x) {
       bool ok = true;
+      decode(t, a0, a1, n0);
+      cb = 0, ky = 0, kx = 0;
       for (int kb = 0; kb < KB; ++kb, ++it) {
+        if (kb > 0 && ++cb == p.kb_per_tap) {
+          cb = 0;
+          if (++kx == 3) kx = 0, ++ky;
+        }
         const int s = it % C::STAGES;
         const uint32_t ph = (it / C::STAGES) & 1;
+        // LayerNorm on load: the statistics this k-block needs depend only
+        // on the tile and the tap, so their loads go out before the wait for
+        // the A tile and overlap it. TMEM_A: one row per thread; otherwise
+        // the 8 rows of this thread's float4s (rows tid / 8 + 16 i).
+        const int q = warp & 3, rq = q * 32 + lane;
+        float lm = 0.0f, lr = 0.0f;
+        bool ln = false;
+        float lms[8], lrs[8];
+        bool lns[8];
+        if (p.ln_stats) {
+          if (TMEM_A) {
+            ln = ln_row(rq, lm, lr);
+          } else if (!GATE) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) lns[i] = ln_row((tid >> 3) + 16 * i, lms[i], lrs[i]);
+          }
+        }
         if (!mbar_wait(&full[s], ph, vabort)) {
           fail(kErrSplit);
           ok = false;
           break;
+        }
+        if (TMEM_A) {
+          // This warp's TMEM lane quarter: rows q*32 .. q*32+31 of A. Each
+          // thread reads its row (32 K values, 128-byte swizzled) and writes
+          // the hi / lo halves into the stage's TMEM slot.
+          const int r = rq;
+          const uint8_t* arow = base + s * C::STAGE_BYTES + r * 128;
+          float hi[32], lo[32];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            float4 v = *reinterpret_cast<const float4*>(arow + ((c ^ (r & 7)) << 4));
+            if (ln) v = ln_apply4(v, lm, lr, cb * 32 + 4 * c);
+            const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              hi[4 * c + e] = tf32_round(x[e]);
+              lo[4 * c + e] = tf32_round(x[e] - hi[4 * c + e]);
+            }
+          }
+          const uint32_t slot = tmem + (uint32_t(q * 32) << 16) + C::A_COL0 + s * 64;
+          tmem_st32(slot, hi);
+          tmem_st32(slot + 32, lo);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&lo_ready[s]);
+          continue;
         }
         // Elementwise, so the layout does not matter; a warp touches 32
         // consecutive float4 (512 contiguous bytes) per access, which keeps
@@ -389,14 +503,19 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 #pragma unroll
         for (int i = 0; i < 8 * 128; i += 128) {
           float4 v = a[i], h, l;
-          h.x = tf32_rne(v.x);
-          h.y = tf32_rne(v.y);
-          h.z = tf32_rne(v.z);
-          h.w = tf32_rne(v.w);
-          l.x = tf32_rne(v.x - h.x);
-          l.y = tf32_rne(v.y - h.y);
-          l.z = tf32_rne(v.z - h.z);
-          l.w = tf32_rne(v.w - h.w);
+          if (!GATE && p.ln_stats && lns[i >> 7]) {
+            // float4 (tid + i) of the swizzled tile: row f / 8, chunk (f % 8) ^ (row % 8).
+            const int f = tid + i, r = f >> 3, ch = cb * 32 + (((f & 7) ^ (r & 7)) << 2);
+            v = ln_apply4(v, lms[i >> 7], lrs[i >> 7], ch);
+          }
+          h.x = tf32_round(v.x);
+          h.y = tf32_round(v.y);
+          h.z = tf32_round(v.z);
+          h.w = tf32_round(v.w);
+          l.x = tf32_round(v.x - h.x);
+          l.y = tf32_round(v.y - h.y);
+          l.z = tf32_round(v.z - h.z);
+          l.w = tf32_round(v.w - h.w);
           a[i] = h;
           alo[i] = l;
         }

@@ -48,6 +48,14 @@ struct Geo {
     return root[size_t(a)] == root[size_t(t)] && lo[size_t(a)] <= lo[size_t(t)] && hi[size_t(t)] <= hi[size_t(a)];
   }
   bool whole(int32_t a) const { return lo[size_t(a)] == 0 && hi[size_t(a)] == hi[size_t(root[size_t(a)])]; }
+  // A buffer the schedule adds: a root of c channels. Returns its id.
+  int32_t add(int64_t c) {
+    const int32_t id = int32_t(root.size());
+    root.push_back(id);
+    lo.push_back(0);
+    hi.push_back(c);
+    return id;
+  }
 };
 
 bool per_pixel_unary(int k) {
@@ -68,6 +76,13 @@ int reads_of(const mx_op& o, int32_t extra, int32_t* r) {
   if (o.src >= 0) r[n++] = o.src;
   if (o.src2 >= 0) r[n++] = o.src2;
   if (extra >= 0) r[n++] = extra;
+  return n;
+}
+// Everything a scheduled step reads: its op's inputs, the epilogue operand
+// and the LayerNorm statistics it normalises with. r holds 4.
+int step_reads(const SchedStep& st, int32_t* r) {
+  int n = reads_of(st.o, st.epi_src, r);
+  if (st.ln_stats >= 0) r[n++] = st.ln_stats;
   return n;
 }
 
@@ -192,7 +207,7 @@ int out_channels(const mx_op& o) { return o.kind == MX_OP_GATE_MM ? o.c : o.c_ou
 }  // namespace
 
 Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
-  const Geo G(p);
+  Geo G(p);
   const int n = p.n_ops;
   Schedule S;
 
@@ -247,8 +262,8 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
       bool ok = true;
       for (size_t s = i + 1; s < W.size() && ok; ++s) {
         if (dead[s]) continue;
-        int32_t r[3], w[2];
-        const int nr = reads_of(W[s].o, W[s].epi_src, r), nw = writes_of(W[s].o, w);
+        int32_t r[4], w[2];
+        const int nr = step_reads(W[s], r), nw = writes_of(W[s].o, w);
         for (int a = 0; a < nr; ++a)
           if (G.overlap(r[a], T)) {
             if (j != SIZE_MAX || r[a] != T) ok = false;
@@ -311,8 +326,8 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
       const int nbr = reads_of(B.o, -1, br);
       for (size_t s = i + 1; s < j && ok; ++s) {
         if (dead[s]) continue;
-        int32_t r[3], w[2];
-        const int nr = reads_of(W[s].o, W[s].epi_src, r), nw = writes_of(W[s].o, w);
+        int32_t r[4], w[2];
+        const int nr = step_reads(W[s], r), nw = writes_of(W[s].o, w);
         for (int a = 0; a < nw; ++a) {
           for (int b = 0; b < nbr; ++b)
             if (br[b] != T && G.overlap(w[a], br[b])) ok = false;
@@ -325,8 +340,8 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
       // The destination against what the producer itself reads: an exact
       // match is an in-place elementwise update (each value is read before
       // the same thread writes it), anything else is refused.
-      int32_t ar[3];
-      const int nar = reads_of(A.o, A.epi_src, ar);
+      int32_t ar[4];
+      const int nar = step_reads(A, ar);
       for (int a = 0; a < nar; ++a)
         if (G.overlap(ar[a], D) && !(ar[a] == D && (elementwise(A.o.kind) || ar[a] == A.epi_src))) ok = false;
       if (operand >= 0 && G.overlap(operand, D) && operand != D) ok = false;
@@ -344,12 +359,68 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
       S.ops_fused += int(B.covers.size());
     }
   }
+  // 3. LayerNorm on load: a LayerNorm whose only reader is a conv that can
+  // normalise its A operand becomes a statistics step, and the conv reads
+  // the LayerNorm's input instead of its output.
+  for (size_t j = 0; fuse && j < W.size(); ++j) {
+    if (dead[j] || W[j].o.kind != MX_OP_CHAN_LN || W[j].stats_only) continue;
+    const mx_op L = W[j].o;
+    const int32_t x = L.src, y = L.dst;
+    if (G.overlap(y, p.output) || G.overlap(x, y)) continue;
+    size_t k = SIZE_MAX;
+    bool ok = true;
+    for (size_t s = j + 1; s < W.size() && ok; ++s) {
+      if (dead[s]) continue;
+      int32_t r[4], w[2];
+      const int nr = step_reads(W[s], r), nw = writes_of(W[s].o, w);
+      for (int a = 0; a < nr; ++a)
+        if (G.overlap(r[a], y)) {
+          if (k != SIZE_MAX || r[a] != y) ok = false;
+          else k = s;
+        }
+      bool gone = false;
+      for (int a = 0; a < nw; ++a)
+        if (G.overlap(w[a], y)) {
+          if (G.covers(w[a], y)) gone = true;
+          else ok = false;
+        }
+      if (gone) break;
+    }
+    if (!ok || k == SIZE_MAX) continue;
+    SchedStep& C = W[k];
+    if (C.o.src != y || C.o.src2 == y || C.epi_src == y || C.ln_stats >= 0) continue;
+    mx_op as_read = C.o;
+    as_read.src = x;
+    if (!H.umma(as_read) || !H.ln_on_load(as_read)) continue;
+    // x must still hold the LayerNorm's input when the conv runs, and the
+    // conv must not write over it.
+    for (size_t s = j + 1; s < k && ok; ++s) {
+      if (dead[s]) continue;
+      int32_t w[2];
+      const int nw = writes_of(W[s].o, w);
+      for (int a = 0; a < nw; ++a)
+        if (G.overlap(w[a], x)) ok = false;
+    }
+    if (!ok || G.overlap(C.o.dst, x)) continue;
+    const mx_buf& yb = p.bufs[y];
+    const int32_t sb = G.add(2);
+    S.extra.push_back(mx_buf{2, yb.h, yb.w});
+    W[j].stats_only = true;
+    W[j].o.dst = sb;
+    C.o.src = x;
+    C.ln_stats = sb;
+    C.ln_scale = L.scale;
+    C.ln_bias = L.bias;
+    ++S.ln_on_load;
+  }
+
   for (size_t i = 0; i < W.size(); ++i)
     if (!dead[i]) S.steps.push_back(std::move(W[i]));
 
-  // 3. Pack the roots the steps touch, by first fit over live ranges.
+  // 4. Pack the roots the steps touch, by first fit over live ranges.
   const int m = int(S.steps.size());
-  std::vector<int> first(size_t(p.n_bufs), INT_MAX), last(size_t(p.n_bufs), INT_MIN);
+  const int32_t nb = p.n_bufs + int32_t(S.extra.size());
+  std::vector<int> first(size_t(nb), INT_MAX), last(size_t(nb), INT_MIN);
   auto touch = [&](int32_t b, int t) {
     if (b < 0) return;
     const size_t r = size_t(G.root[size_t(b)]);
@@ -359,8 +430,8 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
   touch(p.input, -1);
   touch(p.output, m);
   for (int t = 0; t < m; ++t) {
-    int32_t r[3], w[2];
-    const int nr = reads_of(S.steps[size_t(t)].o, S.steps[size_t(t)].epi_src, r);
+    int32_t r[4], w[2];
+    const int nr = step_reads(S.steps[size_t(t)], r);
     const int nw = writes_of(S.steps[size_t(t)].o, w);
     for (int a = 0; a < nr; ++a) touch(r[a], t);
     for (int a = 0; a < nw; ++a) touch(w[a], t);
@@ -370,9 +441,9 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     int64_t size, off;
   };
   std::vector<Slot> order;
-  for (int32_t b = 0; b < p.n_bufs; ++b)
+  for (int32_t b = 0; b < nb; ++b)
     if (G.root[size_t(b)] == b && first[size_t(b)] <= last[size_t(b)]) {
-      const mx_buf& bb = p.bufs[b];
+      const mx_buf& bb = b < p.n_bufs ? p.bufs[b] : S.extra[size_t(b - p.n_bufs)];
       const int64_t len = bb.c * bb.h * bb.w;
       order.push_back({b, (len + 63) / 64 * 64, 0});
     }
@@ -380,7 +451,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     if (a.size != b.size) return a.size > b.size;
     return first[size_t(a.root)] < first[size_t(b.root)];
   });
-  std::vector<int64_t> root_off(size_t(p.n_bufs), 0);
+  std::vector<int64_t> root_off(size_t(nb), 0);
   std::vector<std::pair<int64_t, int64_t>> busy;
   for (size_t i = 0; i < order.size(); ++i) {
     Slot& s = order[i];
@@ -400,10 +471,10 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     root_off[size_t(s.root)] = off;
     S.arena_len = std::max(S.arena_len, off + s.size);
   }
-  S.offs.resize(size_t(p.n_bufs));
-  for (int32_t b = 0; b < p.n_bufs; ++b) {
+  S.offs.resize(size_t(nb));
+  for (int32_t b = 0; b < nb; ++b) {
     const int32_t r = G.root[size_t(b)];
-    S.offs[size_t(b)] = root_off[size_t(r)] + (p.offs[b] - p.offs[r]);
+    S.offs[size_t(b)] = root_off[size_t(r)] + (b < p.n_bufs ? p.offs[b] - p.offs[r] : 0);
   }
   S.arena_len = std::max<int64_t>(S.arena_len, 64);
   return S;

@@ -20,6 +20,11 @@
 //     about pixel order) and the gating matmul reads the blocks through a
 //     5-D tensor map instead. The matching backward permutation becomes a
 //     Copy, which copy forwarding then removes.
+//   * LayerNorm on load: a channel LayerNorm whose only reader is a
+//     tensor-core conv becomes a statistics step (per-pixel mean and
+//     reciprocal standard deviation, in the reference's serial order) and
+//     the conv normalises its A operand as it splits it, so the normalised
+//     tensor is never written or read back.
 //   * Packing: every buffer the rewritten list still touches gets an arena
 //     range by first fit over the rewritten list's live ranges (largest
 //     buffers first), 256-byte aligned.
@@ -61,14 +66,22 @@ struct SchedStep {
   // permutation, since dropped) whose blocking it reads through; -1 if it
   // reads a blocked buffer.
   int32_t gate_perm = -1;
+  // A channel LayerNorm turned into its statistics: o.dst is the statistics
+  // buffer (2 floats per pixel: mean, 1 / sqrt(var + eps)).
+  bool stats_only = false;
+  // A conv whose A operand is LayerNorm'd on load: the statistics buffer and
+  // the LayerNorm's scale and bias weights (-1 when not).
+  int32_t ln_stats = -1, ln_scale = -1, ln_bias = -1;
 };
 
 struct Schedule {
   std::vector<SchedStep> steps;
-  std::vector<int64_t> offs;  // per buffer, in floats: the root's offset + the plan's view delta
+  std::vector<mx_buf> extra;  // buffers the schedule adds (ids n_bufs, n_bufs + 1, ...), each its own root
+  std::vector<int64_t> offs;  // per buffer (plan's, then extra), in floats: the root's offset + the plan's view delta
   int64_t arena_len = 0;      // floats
   int perms_dropped = 0;
   int ops_fused = 0;          // plan ops carried out inside another op's step
+  int ln_on_load = 0;         // LayerNorms applied by their consumer
 };
 
 struct ScheduleHooks {
@@ -78,6 +91,8 @@ struct ScheduleHooks {
   std::function<bool(const mx_op& gate, const mx_op& perm)> gate_spatial;
   // Whether buffer b can be a tensor-core operand or output of n channels.
   std::function<bool(int32_t b, int n)> tma_view;
+  // Whether the op's kernel can LayerNorm its A operand on load.
+  std::function<bool(const mx_op&)> ln_on_load;
 };
 
 // fuse = false gives the plan's op list unchanged (one step per op), packed

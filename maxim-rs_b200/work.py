@@ -66,14 +66,25 @@ def schedule_steps(primary):
     return out
 
 
-def step_work(plan, ops, members):
+SCHED_STATS_ONLY, SCHED_LN_ON_LOAD = 1, 2
+
+
+def step_work(plan, ops, members, flags=None):
     """(family, flops, bytes) of one scheduled step. The members' own work,
     less what fusion removes: each absorbed op (an epilogue or a forwarded
     Copy) consumed a tensor its producer no longer writes and it no longer
-    reads, the size of its own output."""
+    reads, the size of its own output. A LayerNorm reduced to its statistics
+    reads its input and writes 8 bytes per pixel."""
     p = members[0]
     f, b = op_work(plan, ops[p])
     fam = [KINDS[ops[p].kind]]
+    fl = 0 if flags is None else int(flags[p])
+    if fl & SCHED_STATS_ONLY:
+        o = ops[p]
+        f, b = 3 * o.c * o.hw, 4 * o.c * o.hw + 8 * o.hw
+        fam = ["ln_stats"]
+    elif fl & SCHED_LN_ON_LOAD:
+        fam = [fam[0] + "(ln)"]
     for j in members[1:]:
         fj, bj = op_work(plan, ops[j])
         c, h, w = plan.buf(ops[j].dst)

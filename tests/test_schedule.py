@@ -44,6 +44,13 @@ def test_schedule_shape(variant, h, w, mx):
         assert primary[i] != i
     # The re-packed arena is no larger than the plan's.
     assert st["pass_arena_bytes"] <= st["arena_bytes"]
+    # Every LayerNorm read by a 1x1 conv alone is normalised on load: it
+    # runs as a statistics step, paired with exactly one conv.
+    _, _, flags = mx.plan_schedule(plan, flags=True)
+    stats_only = (flags & mx._native.SCHED_STATS_ONLY) > 0
+    on_load = (flags & mx._native.SCHED_LN_ON_LOAD) > 0
+    assert stats_only.sum() == on_load.sum() > 0
+    assert (kinds[stats_only] == 7).all() and (kinds[on_load] == CONV1X1).all()
 
 
 def test_schedule_off_keeps_every_op(mx):
