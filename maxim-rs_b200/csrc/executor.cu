@@ -315,6 +315,19 @@ bool umma_eligible(const mx_gpu& g, const Layout& L, const mx_op& o) {
   return true;
 }
 
+// Whether a 2x2 transposed conv runs on the tensor-core kernel: the GEMM's
+// N = 4 c_out comes in 128-column slices, and each epilogue warp's 32 input
+// pixels must be one row segment (width a multiple of 32).
+bool umma_convt_eligible(const mx_gpu& g, const Layout& L, const mx_op& o) {
+  if (!g.use_umma || o.kind != MX_OP_CONVT2X2) return false;
+  if (o.c_in % 32 != 0 || (o.c_out != 32 && o.c_out != 64 && o.c_out != 128)) return false;
+  if (o.wd % 32 != 0) return false;
+  ViewMeta x = meta_of(g, L, o.src), d = meta_of(g, L, o.dst);
+  if (x.off % 4 || x.stride % 4 || d.off % 4 || d.stride % 4) return false;
+  if (x.c != o.c_in || d.c != o.c_out || x.npix != int64_t(o.h) * o.wd || d.npix != 4 * x.npix) return false;
+  return true;
+}
+
 // Whether a gating matmul runs on the tensor-core kernel.
 bool umma_gate_eligible(const mx_gpu& g, const Layout& L, const mx_op& o) {
   if (!g.use_umma || o.kind != MX_OP_GATE_MM) return false;
@@ -342,7 +355,7 @@ bool umma_gate_spatial_ok(const mx_gpu& g, const Layout& L, const mx_op& gate, c
 // 128-column slices) x MODE.
 #define MX_UMMA_INSTANCES(X)                                                                        \
   X(32, 0) X(64, 0) X(128, 0) X(32, 1) X(64, 1) X(128, 1) X(32, 2) X(64, 2) X(128, 2) X(32, 3) X(64, 3) \
-  X(128, 3) X(32, 4) X(64, 4) X(128, 4) X(32, 5) X(64, 5) X(128, 5)
+  X(128, 3) X(32, 4) X(64, 4) X(128, 4) X(32, 5) X(64, 5) X(128, 5) X(128, 6)
 
 void umma_attrs_once() {
   static bool done = false;
@@ -378,7 +391,18 @@ void launch_umma(cudaStream_t s, const UmmaOp& u) {
 
 // Weights in a kernel's layout, uploaded once per (weight, layout) however
 // many steps use them; -1 for an absent weight.
-enum WeightTag : int { WT_RAW = 0, WT_KTAP = 1, WT_HI = 2, WT_LO = 3, WT_KTAP_HI = 4, WT_KTAP_LO = 5, WT_CONVT = 6 };
+enum WeightTag : int {
+  WT_RAW = 0,
+  WT_KTAP = 1,
+  WT_HI = 2,
+  WT_LO = 3,
+  WT_KTAP_HI = 4,
+  WT_KTAP_LO = 5,
+  WT_CONVT = 6,
+  WT_CONVT_HI = 7,
+  WT_CONVT_LO = 8,
+  WT_BIAS4 = 9,  // a bias repeated once per transposed-conv tap
+};
 int64_t cached(mx_gpu& g, int32_t id, int tag, const std::function<std::vector<float>()>& make) {
   if (id < 0) return -1;
   const auto key = std::make_pair(id, tag);
@@ -611,6 +635,57 @@ std::pair<int64_t, int64_t> cached_split(mx_gpu& g, int32_t id, int tag_hi, int 
   return {oh, ol};
 }
 
+// The tensor-core step of a 2x2 stride-2 transposed conv: a 1x1 GEMM over the
+// input pixels with N = 4 c_out columns (tap major), stored through a 5-D
+// map onto the output pixels (2y + dy, 2x + dx).
+Step umma_convt_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int64_t ho, int64_t lo_off, int64_t bo) {
+  auto u = std::make_shared<UmmaOp>();
+  mx_gpu* G = &g;
+  const mx_op op = o;
+  ++g.umma_ops;
+  Step st{oi, 1, nullptr, nullptr};
+  st.prepare = [G, L, u, op, ho, lo_off, bo]() {
+    View x = view_of(*G, *L, op.src), d = view_of(*G, *L, op.dst);
+    const int co = op.c_out, ci = op.c_in, n = 4 * co, tn = 128, W = op.wd, H = op.h;
+    const float* whi = reinterpret_cast<const float*>(G->pool.dev + ho);
+    const float* wlo = reinterpret_cast<const float*>(G->pool.dev + lo_off);
+    {
+      uint64_t dims[2] = {uint64_t(ci), uint64_t(n)}, str[1] = {uint64_t(ci) * 4};
+      uint32_t box[2] = {32, uint32_t(tn)};
+      u->b = make_tensor_map(whi, 2, dims, str, box);
+      u->blo = make_tensor_map(wlo, 2, dims, str, box);
+    }
+    uint64_t da[2] = {uint64_t(ci), uint64_t(x.npix)}, sa[1] = {uint64_t(x.stride) * 4};
+    uint32_t ba[2] = {32, 128};
+    u->a = make_tensor_map(x.ptr, 2, da, sa, ba);
+    // Output pixel (2y + dy, 2x + dx) of a 2W-wide image: dims (c, dx, x, dy, y).
+    const uint64_t px = uint64_t(d.stride) * 4;
+    uint64_t dd[5] = {uint64_t(co), 2, uint64_t(W), 2, uint64_t(H)};
+    uint64_t sd[4] = {px, 2 * px, 2 * uint64_t(W) * px, 4 * uint64_t(W) * px};
+    uint32_t bd[5] = {32, 1, 32, 1, 1};
+    u->d = make_tensor_map(d.ptr, 5, dd, sd, bd);
+    u->p.tiles = int((x.npix + 127) / 128);
+    u->p.tiles_x = 0;
+    u->p.e_npix = int(x.npix);
+    u->p.e_w = W;
+    u->p.co = co;
+    u->p.n_slices = n / tn;
+    u->p.tiles *= u->p.n_slices;
+    u->p.kb_per_tap = ci / 32;
+    u->p.c_in = ci;
+    u->p.epi = EPI_NONE;
+    u->p.bias = bo < 0 ? nullptr : reinterpret_cast<const float*>(G->pool.dev + bo);
+    u->p.status = G->status;
+    u->n = tn;
+    u->taps = 1;
+    u->mode = MODE_CONVT;
+    u->grid = std::min(u->p.tiles, G->sms);
+    u->smem = umma_smem(tn, u->mode);
+  };
+  st.run = [u](cudaStream_t s) { launch_umma(s, *u); };
+  return st;
+}
+
 // Build the step that runs op `o` (plan op oi, as the plan has it or as the
 // schedule rewrote it, `fs` non-null) over layout L. Weight layouts are
 // converted here and recorded in the pool (once per weight and layout);
@@ -637,7 +712,7 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
       E.ln_bias = raw(fs->ln_bias);
     }
   }
-  const bool needs_umma = E.epi != EPI_NONE || E.spatial || E.ln_stats >= 0;
+  bool needs_umma = (E.epi != EPI_NONE && o.kind != MX_OP_CHAN_SCALE) || E.spatial || E.ln_stats >= 0;
   bool on_umma = false;
   mx_gpu* G = &g;
   auto P = [G](int64_t off) -> const float* {
@@ -737,6 +812,20 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
       break;
     }
     case MX_OP_CHAN_SCALE: {
+      if (E.epi == EPI_ADD) {
+        // x * s + residual in one pass (the schedule checked the views are
+        // 4-channel aligned).
+        const int32_t res = E.src;
+        st.run = [G, L, dst, src, src2, res](cudaStream_t s) {
+          View d = view_of(*G, *L, dst), x = view_of(*G, *L, src), sc = view_of(*G, *L, src2),
+               r = view_of(*G, *L, res);
+          const int c4 = int(x.c / 4), total4 = int(x.npix) * c4;
+          chan_scale_add4_kernel<<<blocks_for(total4, TPB), TPB, 0, s>>>(total4, c4, x.ptr, int(x.stride), sc.ptr,
+                                                                         r.ptr, int(r.stride), d.ptr, int(d.stride));
+        };
+        on_umma = needs_umma = false;
+        break;
+      }
       st.run = [G, L, dst, src, src2](cudaStream_t s) {
         View d = view_of(*G, *L, dst), x = view_of(*G, *L, src), sc = view_of(*G, *L, src2);
         if (aligned4(d) && aligned4(x) && aligned4(sc)) {
@@ -819,14 +908,27 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
     case MX_OP_CONVT2X2: {
       int ci = o.c_in, co = o.c_out;
       // [ci][co][2][2] (flipped) -> [tap*co + o][ci]
-      int64_t wo = cached(g, o.w, WT_CONVT, [&] {
+      auto tapmajor = [&] {
         auto w = W(o.w);
         std::vector<float> wt(w.size());
         for (int ic = 0; ic < ci; ++ic)
           for (int oc = 0; oc < co; ++oc)
             for (int t = 0; t < 4; ++t) wt[(size_t(t) * co + oc) * ci + ic] = w[(size_t(ic) * co + oc) * 4 + t];
         return wt;
-      });
+      };
+      if (umma_convt_eligible(g, *L, o)) {
+        const auto hl = cached_split(g, o.w, WT_CONVT_HI, WT_CONVT_LO, tapmajor);
+        const int64_t b4 = cached(g, o.bias, WT_BIAS4, [&] {
+          auto b = W(o.bias);
+          std::vector<float> r(4 * b.size());
+          for (size_t t = 0; t < 4; ++t) std::copy(b.begin(), b.end(), r.begin() + long(t * b.size()));
+          return r;
+        });
+        st = umma_convt_step(g, oi, o, L, hl.first, hl.second, b4);
+        on_umma = true;
+        break;
+      }
+      int64_t wo = cached(g, o.w, WT_CONVT, tapmajor);
       int64_t bo = raw(o.bias);
       int wd = o.wd;
       st.run = [G, L, P, dst, src, wo, bo, ci, co, wd](cudaStream_t s) {
@@ -974,6 +1076,7 @@ ScheduleHooks schedule_hooks(const mx_gpu& g) {
   const mx_gpu* G = &g;
   ScheduleHooks h;
   h.umma = [G](const mx_op& o) {
+    if (o.kind == MX_OP_CONVT2X2) return umma_convt_eligible(*G, G->roffs, o);
     return o.kind == MX_OP_GATE_MM ? umma_gate_eligible(*G, G->roffs, o) : umma_eligible(*G, G->roffs, o);
   };
   h.gate_spatial = [G](const mx_op& gate, const mx_op& perm) {

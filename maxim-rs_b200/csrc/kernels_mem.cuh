@@ -183,6 +183,22 @@ __global__ void chan_scale4_kernel(int total4, int c4, const float* __restrict__
   *reinterpret_cast<float4*>(d + size_t(p) * sd + c) = make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w);
 }
 
+// x * s + r (channel scale, then the residual add) in one pass, with the two
+// roundings of the separate ops: no fused multiply-add.
+__global__ void chan_scale_add4_kernel(int total4, int c4, const float* __restrict__ x, int sx,
+                                       const float* __restrict__ s, const float* __restrict__ r, int sr,
+                                       float* __restrict__ d, int sd) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total4) return;
+  int p = i / c4, c = (i - p * c4) * 4;
+  float4 v = *reinterpret_cast<const float4*>(x + size_t(p) * sx + c);
+  float4 g = *reinterpret_cast<const float4*>(s + c);
+  float4 e = *reinterpret_cast<const float4*>(r + size_t(p) * sr + c);
+  *reinterpret_cast<float4*>(d + size_t(p) * sd + c) =
+      make_float4(__fadd_rn(__fmul_rn(v.x, g.x), e.x), __fadd_rn(__fmul_rn(v.y, g.y), e.y),
+                  __fadd_rn(__fmul_rn(v.z, g.z), e.z), __fadd_rn(__fmul_rn(v.w, g.w), e.w));
+}
+
 // Resize passes, 4 channels per thread, same tap tables and the same
 // per-channel arithmetic as the scalar kernels (acc over taps ascending with
 // non-contracting ops, then acc / wsum if wsum > 0).

@@ -62,7 +62,19 @@ namespace mx {
 // t = cell (gy, gx), group = (fy, fx)) takes 32 / gw rows of gw cells, block
 // gating (sp_mode 1, t = (fy, fx), group = block (gy, gx)) 32 / fw rows of fw
 // positions.
-enum : int { MODE_CONV1 = 0, MODE_CONV3 = 1, MODE_GATE = 2, MODE_GATE_GRID = 3, MODE_CONV4 = 4, MODE_GATE_SP = 5 };
+// MODE_CONVT: the 2x2 stride-2 transposed conv (Conv_up) as a 1x1 GEMM with
+// N = 4 c_out columns (tap t = 2 dy + dx major, then output channel); each
+// epilogue warp's 32 input pixels (one image-row segment) are stored to
+// output pixels (2y + dy, 2x + dx) through a 5-D map over (c, dx, x, dy, y).
+enum : int {
+  MODE_CONV1 = 0,
+  MODE_CONV3 = 1,
+  MODE_GATE = 2,
+  MODE_GATE_GRID = 3,
+  MODE_CONV4 = 4,
+  MODE_GATE_SP = 5,
+  MODE_CONVT = 6
+};
 
 // The elementwise tail applied to each output value v before the store, with
 // e the same element of a second operand (same shape as the output), which
@@ -94,6 +106,7 @@ struct UmmaConvParams {
   const float* ln_scale;
   const float* ln_bias;
   int in_w, in_h;     // CONV1: input pixels in in_w; CONV3: input width, height
+  int co;             // CONVT: output channels (columns per tap)
   const float* bias;  // per output column, or null
   int* status;        // device status word (0 = ok)
 };
@@ -226,7 +239,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   auto decode = [&](int t, int& a0, int& a1, int& n0) {
     n0 = (t % p.n_slices) * N;
     t /= p.n_slices;
-    if (MODE == MODE_CONV1) {
+    if (MODE == MODE_CONV1 || MODE == MODE_CONVT) {
       a0 = t * 128;
       a1 = 0;
     } else if (SPATIAL) {
@@ -300,7 +313,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           int a_bytes = C::A_BYTES;
           if (PER_GROUP) a_bytes = 4096 * min(4, p.groups - a0);
           mbar_arrive_expect_tx(&full[s], a_bytes + 2 * C::B_BYTES);
-          if (MODE == MODE_CONV1) {
+          if (MODE == MODE_CONV1 || MODE == MODE_CONVT) {
             tma_load_2d(st, &tmA, &full[s], cb * 32, a0);
           } else if (MODE == MODE_CONV3) {
             tma_load_3d(st, &tmA, &full[s], cb * 32, a0 + kx - 1, a1 + ky - 1);
@@ -659,6 +672,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         const int col = n0 + j * 32;
         if (MODE == MODE_CONV1) {
           tma_store_2d(&tmD, sb, col, a0 + 32 * q);
+        } else if (MODE == MODE_CONVT) {
+          // Rows a0 + 32q .. +31 are one row segment of the input image.
+          const int pix = a0 + 32 * q;
+          if (pix < p.e_npix) {
+            const int tap = col / p.co, y = pix / p.e_w;
+            tma_store_5d(&tmD, sb, col - tap * p.co, tap & 1, pix - y * p.e_w, tap >> 1, y);
+          }
         } else if (SPATIAL) {
           tma_store_3d(&tmD, sb, col, a0, a1 + 2 * q);
         } else if (a0 + q < p.groups) {

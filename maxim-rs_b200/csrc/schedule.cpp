@@ -316,8 +316,14 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
       const bool umma = H.umma(A.o);
       if (identity) {
         if (umma && !H.tma_view(D, out_channels(A.o))) break;
+      } else if (A.o.kind == MX_OP_CHAN_SCALE) {
+        // The channel-attention tail x * s + residual: one pass over x and
+        // the residual (all views 4-channel aligned for the vector kernel).
+        if (epi != EPI_ADD || A.epi != EPI_NONE) break;
+        if (!H.tma_view(D, A.o.c) || !H.tma_view(operand, A.o.c) || !H.tma_view(A.o.src, A.o.c)) break;
       } else {
-        if (!umma || A.epi != EPI_NONE) break;
+        // (A transposed conv's epilogue only forwards copies.)
+        if (!umma || A.epi != EPI_NONE || A.o.kind == MX_OP_CONVT2X2) break;
         if (!H.tma_view(D, out_channels(A.o))) break;
         if (operand >= 0 && !H.tma_view(operand, out_channels(A.o))) break;
       }
@@ -345,7 +351,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
       for (int a = 0; a < nar; ++a)
         if (G.overlap(ar[a], D) && !(ar[a] == D && (elementwise(A.o.kind) || ar[a] == A.epi_src))) ok = false;
       if (operand >= 0 && G.overlap(operand, D) && operand != D) ok = false;
-      if (operand >= 0 && operand == D && !umma) ok = false;
+      if (operand >= 0 && operand == D && !umma && A.o.kind != MX_OP_CHAN_SCALE) ok = false;
       if (G.overlap(D, T) && D != T) ok = false;
       if (!ok) break;
       A.o.dst = D;

@@ -62,8 +62,9 @@ def test_schedule_off_keeps_every_op(mx):
 
 
 def test_schedule_without_tensor_cores_fuses_only_copies(mx):
-    """With the tensor-core kernel off nothing has an epilogue: only Copies are
-    forwarded, and block permutations stay (the SIMT gating reads blocks)."""
+    """With the tensor-core kernel off no GEMM has an epilogue: only Copies are
+    forwarded and the channel-attention residual add joins its channel scale;
+    block permutations stay (the SIMT gating reads blocks)."""
     plan = mx.Plan(None, 64, 64, variant="S-2")
     os.environ["MAXIM_NO_UMMA"] = "1"
     try:
@@ -73,4 +74,5 @@ def test_schedule_without_tensor_cores_fuses_only_copies(mx):
     kinds = np.array([o.kind for o in plan.ops()])
     assert st["perms_dropped"] == 0
     moved = (primary >= 0) & (primary != np.arange(plan.n_ops))
-    assert moved.any() and (kinds[moved] == COPY).all()
+    assert moved.any() and np.isin(kinds[moved], [COPY, ADD]).all()
+    assert (kinds[primary[moved & (kinds == ADD)]] == 9).all()  # an add only ever joins a channel scale
