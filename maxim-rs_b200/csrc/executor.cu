@@ -804,7 +804,7 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
           const int c4 = int(x.c / 4);
           chan_mean_partial_kernel<<<unsigned(nb), 256, 0, s>>>(int(x.npix), c4, per, x.ptr, int(x.stride),
                                                                 G->scratch);
-          chan_mean_final_kernel<<<blocks_for(x.c, 128), 128, 0, s>>>(nb, int(x.c), int(x.npix), G->scratch, d.ptr);
+          chan_mean_final_tree_kernel<<<unsigned(x.c), 256, 0, s>>>(nb, int(x.c), int(x.npix), G->scratch, d.ptr);
         } else {
           chan_mean_kernel<<<unsigned(x.c), 512, 0, s>>>(x.npix, x.ptr, x.stride, d.ptr);
         }

@@ -172,6 +172,26 @@ __global__ void chan_mean_final_kernel(int nblocks, int c, int npix, const float
   out[ch] = s / float(npix);
 }
 
+// The same second phase with one block per channel: each of 256 threads sums
+// a fixed stride of the partials, then a fixed shared-memory tree adds the
+// threads' sums, so the result is deterministic and the serial chain is
+// nblocks / 256 adds instead of nblocks.
+__global__ void __launch_bounds__(256) chan_mean_final_tree_kernel(int nblocks, int c, int npix,
+                                                                   const float* __restrict__ part,
+                                                                   float* __restrict__ out) {
+  __shared__ float red[256];
+  const int ch = blockIdx.x;
+  float s = 0.0f;
+  for (int b = threadIdx.x; b < nblocks; b += 256) s += part[size_t(b) * c + ch];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[ch] = red[0] / float(npix);
+}
+
 // out[p][c] = x[p][c] * s[c], 4 channels per thread.
 __global__ void chan_scale4_kernel(int total4, int c4, const float* __restrict__ x, int sx,
                                    const float* __restrict__ s, float* __restrict__ d, int sd) {
