@@ -428,6 +428,9 @@ struct UmmaEpi {
   mx_op perm{};
   int32_t ln_stats = -1;                 // LayerNorm on load: statistics buffer
   int64_t ln_scale = -1, ln_bias = -1;  // and the pool offsets of its weights
+  int32_t st_out[2] = {-1, -1};          // LayerNorm statistics the epilogue writes
+  int32_t st_c0[2] = {0, 0};
+  int32_t st_c = 0;
 };
 
 // The tensor-core step of a gating matmul. Over a blocked buffer (pixels in
@@ -559,6 +562,13 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
     }
     u->p.eptr = E.epi >= EPI_ADD ? e.ptr : nullptr;
     u->p.estride = int(e.stride);
+    for (int g2 = 0; g2 < 2; ++g2)
+      if (E.st_out[g2] >= 0) {
+        u->p.st_out[g2] = reinterpret_cast<float2*>(view_of(*G, *L, E.st_out[g2]).ptr);
+        u->p.st_c0[g2] = E.st_c0[g2];
+      }
+    u->p.st_c = E.st_c;
+    u->p.st_eps = kLnEps;
     if (E.ln_stats >= 0) {
       u->p.ln_stats = reinterpret_cast<const float2*>(view_of(*G, *L, E.ln_stats).ptr);
       u->p.ln_scale = reinterpret_cast<const float*>(G->pool.dev + E.ln_scale);
@@ -711,8 +721,14 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
       E.ln_scale = raw(fs->ln_scale);
       E.ln_bias = raw(fs->ln_bias);
     }
+    for (int g2 = 0; g2 < 2; ++g2) {
+      E.st_out[g2] = fs->stats_out[g2];
+      E.st_c0[g2] = fs->stats_c0[g2];
+    }
+    E.st_c = fs->stats_c;
   }
-  bool needs_umma = (E.epi != EPI_NONE && o.kind != MX_OP_CHAN_SCALE) || E.spatial || E.ln_stats >= 0;
+  bool needs_umma = (E.epi != EPI_NONE && o.kind != MX_OP_CHAN_SCALE) || E.spatial || E.ln_stats >= 0 ||
+                    E.st_out[0] >= 0;
   bool on_umma = false;
   mx_gpu* G = &g;
   auto P = [G](int64_t off) -> const float* {
@@ -1091,6 +1107,12 @@ ScheduleHooks schedule_hooks(const mx_gpu& g) {
     if (o.kind != MX_OP_CONV1X1) return false;
     const int c = o.c_in;
     return (c == 32 || c == 64 || c == 128 || c == 256) && tma_view(*G, G->roffs, o.src, c);
+  };
+  // A 1x1 / 3x3 / 4x4 conv on the tensor-core kernel writes whole pixel rows
+  // per epilogue thread, one output slice at a time.
+  h.stats_slice = [G](const mx_op& o) {
+    if (o.kind != MX_OP_CONV1X1 && o.kind != MX_OP_CONV3X3 && o.kind != MX_OP_CONV4X4S2) return 0;
+    return umma_eligible(*G, G->roffs, o) ? umma_tile_n(o.c_out) : 0;
   };
   return h;
 }

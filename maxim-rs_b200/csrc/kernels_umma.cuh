@@ -107,6 +107,13 @@ struct UmmaConvParams {
   const float* ln_bias;
   int in_w, in_h;     // CONV1: input pixels in in_w; CONV3: input width, height
   int co;             // CONVT: output channels (columns per tap)
+  // LayerNorm statistics written by the epilogue (row layouts): for group g,
+  // output channels [st_c0[g], st_c0[g] + st_c) of every output pixel give
+  // (mean, 1 / sqrt(max(var, 0) + st_eps)) at st_out[g][pixel]; null if off.
+  float2* st_out[2];
+  int st_c0[2];
+  int st_c;
+  float st_eps;
   const float* bias;  // per output column, or null
   int* status;        // device status word (0 = ok)
 };
@@ -604,6 +611,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 
     const int tstep = 2 * gridDim.x;
     int t = blockIdx.x + set * gridDim.x, j = 0, a0 = 0, a1 = 0, n0 = 0;
+    // LayerNorm statistics of this thread's output pixel, one serial pair of
+    // sums per group, in channel order (the statistics kernel's order).
+    float ss1[2] = {0.0f, 0.0f}, ss2[2] = {0.0f, 0.0f};
     uint32_t use = 0;  // how many tiles this set has taken from its accumulator
     // One chunk (32 columns), in two 16-column halves: drain from TMEM, add
     // the bias, apply the tail (operand values in `ecur`, loaded while the
@@ -644,6 +654,36 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) e[i] = ecur[h * 16 + i];
         epi_apply(p.epi, v, e, p.slope);
+        if (!GATE && MODE != MODE_CONVT && p.st_out[0]) {
+          const int colh = n0 + j * 32 + h * 16;
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            if (!p.st_out[g] || colh < p.st_c0[g] || colh >= p.st_c0[g] + p.st_c) continue;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              ss1[g] = __fadd_rn(ss1[g], v[i]);
+              ss2[g] = __fadd_rn(ss2[g], __fmul_rn(v[i], v[i]));
+            }
+            if (colh + 16 == p.st_c0[g] + p.st_c) {
+              int pix;
+              bool in;
+              if (MODE == MODE_CONV1) {
+                pix = a0 + row;
+                in = pix < p.e_npix;
+              } else {
+                const int y = a1 + (row >> 4), x = a0 + (row & 15);
+                in = y < p.e_h && x < p.e_w;
+                pix = y * p.e_w + x;
+              }
+              const float nf = float(p.st_c);
+              const float m = __fdiv_rn(ss1[g], nf);
+              const float var = __fsub_rn(__fdiv_rn(ss2[g], nf), __fmul_rn(m, m));
+              const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(fmaxf(var, 0.0f), p.st_eps)));
+              if (in) p.st_out[g][pix] = make_float2(m, rs);
+              ss1[g] = 0.0f, ss2[g] = 0.0f;
+            }
+          }
+        }
         if (GATE) {
           // Staging is [a][channel] for this warp's group: this thread
           // (channel lane) owns one float in each of the 32 rows.

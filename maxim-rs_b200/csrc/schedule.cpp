@@ -85,6 +85,14 @@ int step_reads(const SchedStep& st, int32_t* r) {
   if (st.ln_stats >= 0) r[n++] = st.ln_stats;
   return n;
 }
+// Everything a scheduled step writes, the statistics of its epilogue
+// included. w holds 4.
+int step_writes(const SchedStep& st, int32_t* w) {
+  int n = writes_of(st.o, w);
+  for (int g = 0; g < 2; ++g)
+    if (st.stats_out[g] >= 0) w[n++] = st.stats_out[g];
+  return n;
+}
 
 // The outcome of dropping a set of forward block permutations.
 struct PermSim {
@@ -420,6 +428,44 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     ++S.ln_on_load;
   }
 
+  // 3b. Statistics from the producer: a statistics step whose input was
+  // last written by a tensor-core conv's epilogue, as a 32-aligned channel
+  // group inside one output slice of it, is computed by that epilogue (each
+  // of its threads holds whole pixel rows, in channel order) and disappears.
+  for (size_t j = 0; fuse && j < W.size(); ++j) {
+    if (dead[j] || !W[j].stats_only) continue;
+    const int32_t x = W[j].o.src, sb = W[j].o.dst;
+    size_t i = SIZE_MAX;
+    bool ok = true;
+    for (size_t s = j; s-- > 0;) {
+      if (dead[s]) continue;
+      int32_t w[4];
+      const int nw = step_writes(W[s], w);
+      bool hit = false;
+      for (int a = 0; a < nw; ++a) hit |= G.overlap(w[a], x);
+      if (!hit) continue;
+      if (G.covers(W[s].o.dst, x)) i = s;
+      else ok = false;
+      break;
+    }
+    if (!ok || i == SIZE_MAX) continue;
+    SchedStep& P = W[i];
+    const int slice = H.stats_slice(P.o);
+    if (slice <= 0) continue;
+    const int64_t c0 = G.lo[size_t(x)] - G.lo[size_t(P.o.dst)], c = G.hi[size_t(x)] - G.lo[size_t(x)];
+    if (c0 % 32 != 0 || (c != 32 && c != 64 && c != 128) || c0 / slice != (c0 + c - 1) / slice) continue;
+    if (P.stats_c != 0 && P.stats_c != c) continue;
+    const int g = P.stats_out[0] < 0 ? 0 : (P.stats_out[1] < 0 ? 1 : -1);
+    if (g < 0) continue;
+    P.stats_out[g] = sb;
+    P.stats_c0[g] = int32_t(c0);
+    P.stats_c = int32_t(c);
+    P.covers.insert(P.covers.end(), W[j].covers.begin(), W[j].covers.end());
+    dead[j] = 1;
+    ++S.stats_in_epilogue;
+    ++S.ops_fused;
+  }
+
   for (size_t i = 0; i < W.size(); ++i)
     if (!dead[i]) S.steps.push_back(std::move(W[i]));
 
@@ -436,9 +482,9 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
   touch(p.input, -1);
   touch(p.output, m);
   for (int t = 0; t < m; ++t) {
-    int32_t r[4], w[2];
+    int32_t r[4], w[4];
     const int nr = step_reads(S.steps[size_t(t)], r);
-    const int nw = writes_of(S.steps[size_t(t)].o, w);
+    const int nw = step_writes(S.steps[size_t(t)], w);
     for (int a = 0; a < nr; ++a) touch(r[a], t);
     for (int a = 0; a < nw; ++a) touch(w[a], t);
   }

@@ -72,6 +72,13 @@ struct SchedStep {
   // A conv whose A operand is LayerNorm'd on load: the statistics buffer and
   // the LayerNorm's scale and bias weights (-1 when not).
   int32_t ln_stats = -1, ln_scale = -1, ln_bias = -1;
+  // A tensor-core step whose epilogue also writes LayerNorm statistics of
+  // (up to two) channel groups of its output: group g is output channels
+  // [stats_c0[g], stats_c0[g] + stats_c), its statistics go to buffer
+  // stats_out[g] (-1: unused).
+  int32_t stats_out[2] = {-1, -1};
+  int32_t stats_c0[2] = {0, 0};
+  int32_t stats_c = 0;
 };
 
 struct Schedule {
@@ -82,6 +89,7 @@ struct Schedule {
   int perms_dropped = 0;
   int ops_fused = 0;          // plan ops carried out inside another op's step
   int ln_on_load = 0;         // LayerNorms applied by their consumer
+  int stats_in_epilogue = 0;  // of those, statistics written by the producer's epilogue
 };
 
 struct ScheduleHooks {
@@ -93,6 +101,9 @@ struct ScheduleHooks {
   std::function<bool(int32_t b, int n)> tma_view;
   // Whether the op's kernel can LayerNorm its A operand on load.
   std::function<bool(const mx_op&)> ln_on_load;
+  // The output-column slice width of a tensor-core op whose epilogue can
+  // write LayerNorm statistics (whole pixel rows per thread), 0 if it cannot.
+  std::function<int(const mx_op&)> stats_slice;
 };
 
 // fuse = false gives the plan's op list unchanged (one step per op), packed

@@ -7,7 +7,7 @@ import os
 import numpy as np
 import pytest
 
-BLOCK_PERM, GATE_MM, CONV1X1, CONV3X3, GELU, ADD, COPY, GATE_APPLY = 15, 14, 10, 11, 4, 1, 0, 3
+BLOCK_PERM, GATE_MM, CONV1X1, CONV3X3, GELU, ADD, COPY, GATE_APPLY, LN = 15, 14, 10, 11, 4, 1, 0, 3, 7
 
 
 def _sched(mx, plan, fuse=True):
@@ -44,13 +44,18 @@ def test_schedule_shape(variant, h, w, mx):
         assert primary[i] != i
     # The re-packed arena is no larger than the plan's.
     assert st["pass_arena_bytes"] <= st["arena_bytes"]
-    # Every LayerNorm read by a 1x1 conv alone is normalised on load: it
-    # runs as a statistics step, paired with exactly one conv.
+    # Every LayerNorm read by a 1x1 conv alone is normalised on load, paired
+    # with exactly one conv: its statistics come from a statistics step or,
+    # where a tensor-core conv produced its input, from that conv's epilogue.
     _, _, flags = mx.plan_schedule(plan, flags=True)
     stats_only = (flags & mx._native.SCHED_STATS_ONLY) > 0
     on_load = (flags & mx._native.SCHED_LN_ON_LOAD) > 0
-    assert stats_only.sum() == on_load.sum() > 0
-    assert (kinds[stats_only] == 7).all() and (kinds[on_load] == CONV1X1).all()
+    ln = kinds == LN
+    in_epilogue = ln & (primary >= 0) & (primary != idx)
+    assert on_load.sum() > 0 and stats_only.sum() + in_epilogue.sum() == on_load.sum()
+    assert (kinds[stats_only] == LN).all() and (kinds[on_load] == CONV1X1).all()
+    assert np.isin(kinds[primary[in_epilogue]], [CONV1X1, CONV3X3, 12]).all()
+    assert in_epilogue.sum() > stats_only.sum()
 
 
 def test_schedule_off_keeps_every_op(mx):
