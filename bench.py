@@ -101,19 +101,41 @@ class Clocks:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
+def shard(n, rank, world):
+    """The stream indices of this rank's n images: image i of the one seeded
+    stream goes to rank i % world (replicas, no image is split)."""
+    return [rank + world * k for k in range(n)]
+
+
+def max_over_ranks(x, world, device=None):
+    """The largest of x over all ranks (every rank passes its own x); the
+    job's time is its slowest rank's."""
+    if world <= 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_mpx_per_s(images_per_rank, world, seconds):
+    """Whole-job throughput: every rank's images, over the slowest rank's time."""
+    return images_per_rank * world * OUT_MPX / seconds
+
+
 def make_images(n, rank, world):
-    """This rank's share of one seeded image stream (image i -> rank i % N)."""
+    """This rank's share of one seeded image stream (see shard)."""
     synth = importlib.import_module("maxim-rs_b200.synth")
     mx = importlib.import_module("maxim-rs_b200")
     rng = synth.input_rng(IN_SEED)
+    want = set(shard(n, rank, world))
     out = []
-    i = 0
-    while len(out) < n:
+    for i in range(max(want) + 1):
         img = synth.image_uniform(rng, IMG_H, IMG_W)
-        if i % world == rank:
+        if i in want:
             padded, _ = mx.preprocess(img, 64)
             out.append(padded)
-        i += 1
     return out
 
 
@@ -311,12 +333,8 @@ def run_native(args):
         torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
     barrier()
-    if world > 1:
-        t = torch.tensor([ms], device="cuda:%d" % local, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    images = args.steps * B * world
-    value = images * OUT_MPX / (ms / 1000.0)
+    ms = max_over_ranks(ms, world, "cuda:%d" % local)
+    value = job_mpx_per_s(args.steps * B, world, ms / 1000.0)
 
     # e2e: the public API from pinned host memory, H2D + pass + D2H per image.
     pin_in = [torch.from_numpy(im).pin_memory() for im in imgs]
@@ -330,11 +348,8 @@ def run_native(args):
             gpu.run(pin_in[b].numpy(), pin_out[b].numpy())
     e2e_s = time.perf_counter() - t0
     barrier()
-    if world > 1:
-        t = torch.tensor([e2e_s], device="cuda:%d" % local, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e = images * OUT_MPX / e2e_s
+    e2e_s = max_over_ranks(e2e_s, world, "cuda:%d" % local)
+    e2e = job_mpx_per_s(args.steps * B, world, e2e_s)
 
     # Roofline of the dominant kernel family, from per-op CUDA events on the
     # executor's stream over one pass of the same workload.
