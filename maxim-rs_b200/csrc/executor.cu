@@ -57,6 +57,7 @@ constexpr int TPB = 256;
 struct HostTaps {
   std::vector<int> j0, w0, cnt;
   std::vector<float> w, wsum;
+  std::vector<float> wrcp;  // 1 / wsum where wsum is an exact power of two, else 0
 };
 HostTaps make_taps(int n_in, int n_out, int max_taps) {
   HostTaps t;
@@ -85,6 +86,10 @@ HostTaps make_taps(int n_in, int n_out, int max_taps) {
   for (int o = 0; o < n_out; ++o) {
     int end = o + 1 < n_out ? t.w0[o + 1] : int(t.w.size());
     t.cnt.push_back(std::min(end - t.w0[o], max_taps));
+    int e = 0;
+    const float m = std::frexp(t.wsum[size_t(o)], &e);
+    const float ws = t.wsum[size_t(o)];
+    t.wrcp.push_back(std::isnormal(ws) && ws > 0.0f && m == 0.5f && e > -120 && e < 120 ? 1.0f / ws : 0.0f);
   }
   return t;
 }
@@ -1013,24 +1018,28 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
       HostTaps tx = make_taps(o.win, o.wout, 1 << 30), ty = make_taps(o.hin, o.hout, 64);
       int64_t tx_j0 = int64_t(g.pool.put(tx.j0)), tx_w0 = int64_t(g.pool.put(tx.w0)),
               tx_c = int64_t(g.pool.put(tx.cnt)), tx_w = int64_t(g.pool.put(tx.w)),
-              tx_s = int64_t(g.pool.put(tx.wsum));
+              tx_s = int64_t(g.pool.put(tx.wsum)), tx_r = int64_t(g.pool.put(tx.wrcp));
       int64_t ty_j0 = int64_t(g.pool.put(ty.j0)), ty_w0 = int64_t(g.pool.put(ty.w0)),
               ty_c = int64_t(g.pool.put(ty.cnt)), ty_w = int64_t(g.pool.put(ty.w)),
-              ty_s = int64_t(g.pool.put(ty.wsum));
+              ty_s = int64_t(g.pool.put(ty.wsum)), ty_r = int64_t(g.pool.put(ty.wrcp));
       st.kernels = 2;
-      st.run = [G, L, op, tx_j0, tx_w0, tx_c, tx_w, tx_s, ty_j0, ty_w0, ty_c, ty_w, ty_s](cudaStream_t s) {
+      st.run = [G, L, op, tx_j0, tx_w0, tx_c, tx_w, tx_s, tx_r, ty_j0, ty_w0, ty_c, ty_w, ty_s,
+                ty_r](cudaStream_t s) {
         auto I = [G](int64_t off) { return reinterpret_cast<const int*>(G->pool.dev + off); };
         auto F = [G](int64_t off) { return reinterpret_cast<const float*>(G->pool.dev + off); };
         View d = view_of(*G, *L, op.dst), x = view_of(*G, *L, op.src), t = view_of(*G, *L, op.tmp);
-        if (aligned4(d) && aligned4(x) && aligned4(t)) {
-          TapTable4 TX{I(tx_j0), I(tx_w0), I(tx_c), F(tx_w), F(tx_s)};
-          TapTable4 TY{I(ty_j0), I(ty_w0), I(ty_c), F(ty_w), F(ty_s)};
-          const int c4 = op.c / 4;
-          const int t1 = op.hin * op.wout * c4, t2 = op.hout * op.wout * c4;
-          resize_h4_kernel<<<blocks_for(t1, TPB), TPB, 0, s>>>(t1, c4, op.win, op.wout, TX, x.ptr, int(x.stride),
-                                                               t.ptr, int(t.stride));
-          resize_v4_kernel<<<blocks_for(t2, TPB), TPB, 0, s>>>(t2, c4, op.wout, TY, t.ptr, int(t.stride), d.ptr,
-                                                               int(d.stride));
+        const int c4 = op.c / 4;
+        if (aligned4(d) && aligned4(x) && aligned4(t) && op.c % 4 == 0 && (c4 & (c4 - 1)) == 0 && op.hin < 65536 &&
+            op.hout < 65536) {
+          TapTable4 TX{I(tx_j0), I(tx_w0), I(tx_c), F(tx_w), F(tx_s), F(tx_r)};
+          TapTable4 TY{I(ty_j0), I(ty_w0), I(ty_c), F(ty_w), F(ty_s), F(ty_r)};
+          int lg4 = 0;
+          while ((1 << lg4) < c4) ++lg4;
+          const int row = op.wout * c4;
+          const dim3 g1(unsigned(blocks_for(row, TPB)), unsigned(op.hin)), g2(unsigned(blocks_for(row, TPB)),
+                                                                              unsigned(op.hout));
+          resize_h4_kernel<<<g1, TPB, 0, s>>>(lg4, op.win, op.wout, TX, x.ptr, int(x.stride), t.ptr, int(t.stride));
+          resize_v4_kernel<<<g2, TPB, 0, s>>>(lg4, op.wout, TY, t.ptr, int(t.stride), d.ptr, int(d.stride));
           return;
         }
         TapTable TX{I(tx_j0), I(tx_w0), I(tx_c), F(tx_w), F(tx_s)};

@@ -221,13 +221,19 @@ __global__ void chan_scale_add4_kernel(int total4, int c4, const float* __restri
 
 // Resize passes, 4 channels per thread, same tap tables and the same
 // per-channel arithmetic as the scalar kernels (acc over taps ascending with
-// non-contracting ops, then acc / wsum if wsum > 0).
+// non-contracting ops, then acc / wsum if wsum > 0). One block row of threads
+// per output row (blockIdx.y), channels in groups of 4 along x; c4 (channels
+// / 4) is a power of two, 1 << lg4.
 struct TapTable4 {
   const int* j0;
   const int* w0;
   const int* cnt;
   const float* w;
   const float* wsum;
+  // 1 / wsum where wsum is an exact power of two (then acc * wrcp is acc /
+  // wsum bit for bit), else 0: the division is only paid where the taps were
+  // clipped at the border.
+  const float* wrcp;
 };
 
 __device__ __forceinline__ void tap_acc(float4& acc, float w, float4 v) {
@@ -236,37 +242,41 @@ __device__ __forceinline__ void tap_acc(float4& acc, float w, float4 v) {
   acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
   acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
 }
-__device__ __forceinline__ float4 tap_norm(float4 acc, float sm) {
+__device__ __forceinline__ float4 tap_norm(float4 acc, float sm, float rcp) {
+  if (rcp != 0.0f)
+    return make_float4(__fmul_rn(acc.x, rcp), __fmul_rn(acc.y, rcp), __fmul_rn(acc.z, rcp), __fmul_rn(acc.w, rcp));
   if (sm > 0.0f)
     return make_float4(__fdiv_rn(acc.x, sm), __fdiv_rn(acc.y, sm), __fdiv_rn(acc.z, sm), __fdiv_rn(acc.w, sm));
   return acc;
 }
 
-__global__ void resize_h4_kernel(int total4, int c4, int win, int wout, TapTable4 t, const float* __restrict__ src,
-                                 int ss, float* __restrict__ dst, int sd) {
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= total4) return;  // total4 = rows * wout * c4
-  int p = i / c4, c = (i - p * c4) * 4;
-  int row = p / wout, xo = p - row * wout;
-  int j0 = __ldg(t.j0 + xo), w0 = __ldg(t.w0 + xo), n = __ldg(t.cnt + xo);
+// Horizontal pass: dst row r (of hin), column xo, from src row r.
+__global__ void resize_h4_kernel(int lg4, int win, int wout, TapTable4 t, const float* __restrict__ src, int ss,
+                                 float* __restrict__ dst, int sd) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (wout << lg4)) return;
+  const int row = blockIdx.y, xo = i >> lg4, c = (i & ((1 << lg4) - 1)) * 4;
+  const int j0 = __ldg(t.j0 + xo), w0 = __ldg(t.w0 + xo), n = __ldg(t.cnt + xo);
   const float* s = src + (size_t(row) * win + j0) * ss + c;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k = 0; k < n; ++k) tap_acc(acc, __ldg(t.w + w0 + k), *reinterpret_cast<const float4*>(s + size_t(k) * ss));
-  *reinterpret_cast<float4*>(dst + size_t(p) * sd + c) = tap_norm(acc, __ldg(t.wsum + xo));
+  *reinterpret_cast<float4*>(dst + (size_t(row) * wout + xo) * sd + c) =
+      tap_norm(acc, __ldg(t.wsum + xo), __ldg(t.wrcp + xo));
 }
 
-__global__ void resize_v4_kernel(int total4, int c4, int wout, TapTable4 t, const float* __restrict__ src, int ss,
+// Vertical pass: dst row yo (of hout) from rows j0.. of the horizontal result.
+__global__ void resize_v4_kernel(int lg4, int wout, TapTable4 t, const float* __restrict__ src, int ss,
                                  float* __restrict__ dst, int sd) {
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= total4) return;  // total4 = hout * wout * c4
-  int p = i / c4, c = (i - p * c4) * 4;
-  int yo = p / wout, x = p - yo * wout;
-  int j0 = __ldg(t.j0 + yo), w0 = __ldg(t.w0 + yo), n = __ldg(t.cnt + yo);
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (wout << lg4)) return;
+  const int yo = blockIdx.y, x = i >> lg4, c = (i & ((1 << lg4) - 1)) * 4;
+  const int j0 = __ldg(t.j0 + yo), w0 = __ldg(t.w0 + yo), n = __ldg(t.cnt + yo);
   const float* s = src + (size_t(j0) * wout + x) * ss + c;
   const size_t step = size_t(wout) * ss;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k = 0; k < n; ++k) tap_acc(acc, __ldg(t.w + w0 + k), *reinterpret_cast<const float4*>(s + k * step));
-  *reinterpret_cast<float4*>(dst + size_t(p) * sd + c) = tap_norm(acc, __ldg(t.wsum + yo));
+  *reinterpret_cast<float4*>(dst + (size_t(yo) * wout + x) * sd + c) =
+      tap_norm(acc, __ldg(t.wsum + yo), __ldg(t.wrcp + yo));
 }
 
 }  // namespace
