@@ -163,11 +163,11 @@ __device__ __forceinline__ void epi_apply(int kind, float (&v)[16], const float 
   }
 }
 
-// Whether a kernel instance keeps its A operand (the split hi / lo halves)
-// in TMEM rather than shared memory: the convolutions with N <= 64, where
-// the tensor core's reads of A (twice hi, once lo per k-step) would
-// otherwise dominate shared-memory bandwidth. TMEM then holds the two
-// accumulator sets (4N columns) and one 64-column A slot per stage.
+// Whether a kernel instance keeps A_lo (the residual half of the split A
+// operand) in TMEM rather than shared memory: the convolutions with N <= 64.
+// A_hi is always the fp32 tile in shared memory, which the tensor core reads
+// as TF32 by dropping the 13 low mantissa bits. TMEM then holds the two
+// accumulator sets (4N columns) and one 32-column A_lo slot per stage.
 __host__ __device__ constexpr bool umma_tmem_a(int n, int mode) {
   return n <= 64 && (mode == MODE_CONV1 || mode == MODE_CONV3 || mode == MODE_CONV4);
 }
@@ -184,10 +184,11 @@ struct UmmaCfg {
   // the two cross terms, summed once in the epilogue. Two sets: the epilogue
   // drains one tile while the next accumulates.
   static constexpr int ACC_SETS = 2;
-  static constexpr int A_COL0 = ACC_SETS * 2 * N;  // first TMEM column of the A slots
+  static constexpr int A_COL0 = ACC_SETS * 2 * N;  // first TMEM column of the A_lo slots
   static constexpr int TMEM_COLS = TMEM_A ? 512 : ACC_SETS * 2 * N;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 8 * (3 * STAGES + 4) + 16;
-  static_assert(!TMEM_A || A_COL0 + STAGES * 64 <= 512, "TMEM holds the accumulators and the A slots");
+  static_assert(!TMEM_A || A_COL0 + STAGES * 32 <= 512, "TMEM holds the accumulators and the A_lo slots");
+  static_assert(2 * N <= 256, "one instruction covers B_hi and B_lo");
 };
 
 enum : int {
@@ -198,15 +199,22 @@ enum : int {
   kErrEpilogue = 0x105,
 };
 
-// Round an fp32 value to the nearest TF32 value (ties away from zero) with
-// the conversion instruction, returned as fp32 with the low 13 mantissa bits
-// clear, so the tensor core reads it exactly whatever it does with those
-// bits. One instruction: the split of every A element costs three (hi, the
-// difference, lo), which keeps the split warps off the critical path.
-__device__ __forceinline__ float tf32_round(float v) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
-  return __uint_as_float(r);
+// The A split. The tensor core reads an fp32 operand as TF32 by dropping
+// its 13 low mantissa bits (checked on B200 with an exact 0/1 selector as B:
+// every value, ties included, came back truncated), so the fp32 tile in
+// shared memory is A_hi = trunc(v) as it stands and only the residual
+// A_lo = v - trunc(v) is computed and stored. The subtraction is exact; the
+// residual is then rounded to the nearest TF32 value, ties away from zero:
+// adding half a TF32 ulp (bit 12) to the sign-magnitude bits and clearing
+// the 13 low bits does that and carries into the exponent where it should.
+// All on the integer and fp32 ALUs at the full issue rate (the TF32
+// conversion instruction runs on a slower pipe). A NaN residual would wrap
+// to zero, but it only comes with a NaN or infinite A_hi, which the product
+// carries.
+__device__ __forceinline__ float tf32_residual(float v) {
+  const float hi = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+  const float r = __fsub_rn(v, hi);
+  return __uint_as_float((__float_as_uint(r) + 0x1000u) & 0xFFFFE000u);
 }
 
 constexpr int kUmmaThreads = 448;
@@ -359,6 +367,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_tf32(128, N, GATE ? 1 : 0, 0);
+      // B_lo sits right after B_hi in the stage (N rows each, whole 8-row
+      // swizzle atoms), and the cross-term region right after the hi*hi one
+      // in TMEM, so one N' = 2N instruction computes A_hi*B_hi and A_hi*B_lo
+      // together. An MMA costs about the same below N = 128 whatever its
+      // width, so the k-step takes two instructions instead of three.
+      constexpr uint32_t idesc2 = idesc_tf32(128, 2 * N, GATE ? 1 : 0, 0);
       uint32_t it = 0, tc = 0;
       for (int t = blockIdx.x; t < p.tiles && !*vabort; t += gridDim.x, ++tc) {
         const uint32_t acc = tc % C::ACC_SETS, aph = (tc / C::ACC_SETS) & 1;
@@ -379,43 +393,33 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           }
           tc_fence_after();
           const uint32_t a = smem_u32(base + s * C::STAGE_BYTES);
-          const uint32_t b = a + (TMEM_A ? 1 : 2) * C::A_BYTES, blo = b + C::B_BYTES;
-          if (TMEM_A) {
-            // A_hi / A_lo of this stage sit in TMEM columns [slot, slot + 32)
-            // and [slot + 32, slot + 64); k-step k reads 8 of them.
-            const uint32_t slot = tmem + C::A_COL0 + s * 64;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint64_t db = desc_kmajor_sw128(b + 32 * k), dblo = desc_kmajor_sw128(blo + 32 * k);
-              const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-              mma_tf32_ts(d, slot + 8 * k, db, idesc, accum);
-              mma_tf32_ts(dx, slot + 32 + 8 * k, db, idesc, accum);
-              mma_tf32_ts(dx, slot + 8 * k, dblo, idesc, 1u);
-            }
-            mma_commit(&empty[s]);
-            continue;
-          }
-          const uint32_t alo = a + C::A_BYTES;
+          const uint32_t b = a + (TMEM_A ? 1 : 2) * C::A_BYTES, alo = a + C::A_BYTES;
+          // TMEM_A: this stage's A_lo sits in TMEM columns [slot, slot + 32);
+          // k-step k reads 8 of them.
+          const uint32_t slot = tmem + C::A_COL0 + s * 32;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            uint64_t da, dalo;
+            uint64_t da, dalo = 0;
             if (GATE) {
               // MN-major: k-step k covers K rows 8k..8k+7 of each 4 KB group block.
               da = desc_mnmajor_sw128_32b(a + 1024 * k, 4096);
               dalo = desc_mnmajor_sw128_32b(alo + 1024 * k, 4096);
             } else {
               da = desc_kmajor_sw128(a + 32 * k);
-              dalo = desc_kmajor_sw128(alo + 32 * k);
+              if (!TMEM_A) dalo = desc_kmajor_sw128(alo + 32 * k);
             }
-            const uint64_t db = desc_kmajor_sw128(b + 32 * k), dblo = desc_kmajor_sw128(blo + 32 * k);
+            const uint64_t db = desc_kmajor_sw128(b + 32 * k);
             // The running sum of the hi*hi products takes one accumulator
-            // update per k-step; the cross terms, about 2^-12 of its size,
+            // update per k-step; the cross terms, 2^-10 of its size or less,
             // go to their own region, so the accumulator's rounding at each
-            // update is paid once per k-step at full magnitude, not three times.
+            // update is paid once per k-step at full magnitude.
             const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-            mma_tf32(d, da, db, idesc, accum);
-            mma_tf32(dx, dalo, db, idesc, accum);
-            mma_tf32(dx, da, dblo, idesc, 1u);
+            mma_tf32(d, da, db, idesc2, accum);
+            if (TMEM_A) {
+              mma_tf32_ts(dx, slot + 8 * k, db, idesc, 1u);
+            } else {
+              mma_tf32(dx, dalo, db, idesc, 1u);
+            }
           }
           mma_commit(&empty[s]);
         }
@@ -492,25 +496,27 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         if (TMEM_A) {
           // This warp's TMEM lane quarter: rows q*32 .. q*32+31 of A. Each
           // thread reads its row (32 K values, 128-byte swizzled) and writes
-          // the hi / lo halves into the stage's TMEM slot.
+          // the row's A_lo into the stage's TMEM slot; with LayerNorm on
+          // load the normalised row also goes back into the tile (A_hi).
           const int r = rq;
-          const uint8_t* arow = base + s * C::STAGE_BYTES + r * 128;
-          float hi[32], lo[32];
+          uint8_t* arow = base + s * C::STAGE_BYTES + r * 128;
+          float lo[32];
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
-            float4 v = *reinterpret_cast<const float4*>(arow + ((c ^ (r & 7)) << 4));
-            if (ln) v = ln_apply4(v, lm, lr, cb * 32 + 4 * c);
-            const float x[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              hi[4 * c + e] = tf32_round(x[e]);
-              lo[4 * c + e] = tf32_round(x[e] - hi[4 * c + e]);
+            float4* p4 = reinterpret_cast<float4*>(arow + ((c ^ (r & 7)) << 4));
+            float4 v = *p4;
+            if (ln) {
+              v = ln_apply4(v, lm, lr, cb * 32 + 4 * c);
+              *p4 = v;
             }
+            lo[4 * c] = tf32_residual(v.x);
+            lo[4 * c + 1] = tf32_residual(v.y);
+            lo[4 * c + 2] = tf32_residual(v.z);
+            lo[4 * c + 3] = tf32_residual(v.w);
           }
-          const uint32_t slot = tmem + (uint32_t(q * 32) << 16) + C::A_COL0 + s * 64;
-          tmem_st32(slot, hi);
-          tmem_st32(slot + 32, lo);
+          tmem_st32(tmem + (uint32_t(q * 32) << 16) + C::A_COL0 + s * 32, lo);
           tmem_wait_st();
+          if (p.ln_stats) fence_proxy_async_smem();
           tc_fence_before();
           mbar_arrive(&lo_ready[s]);
           continue;
@@ -522,21 +528,17 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         float4* alo = reinterpret_cast<float4*>(base + s * C::STAGE_BYTES + C::A_BYTES) + tid;
 #pragma unroll
         for (int i = 0; i < 8 * 128; i += 128) {
-          float4 v = a[i], h, l;
+          float4 v = a[i], l;
           if (!GATE && p.ln_stats && lns[i >> 7]) {
             // float4 (tid + i) of the swizzled tile: row f / 8, chunk (f % 8) ^ (row % 8).
             const int f = tid + i, r = f >> 3, ch = cb * 32 + (((f & 7) ^ (r & 7)) << 2);
             v = ln_apply4(v, lms[i >> 7], lrs[i >> 7], ch);
+            a[i] = v;
           }
-          h.x = tf32_round(v.x);
-          h.y = tf32_round(v.y);
-          h.z = tf32_round(v.z);
-          h.w = tf32_round(v.w);
-          l.x = tf32_round(v.x - h.x);
-          l.y = tf32_round(v.y - h.y);
-          l.z = tf32_round(v.z - h.z);
-          l.w = tf32_round(v.w - h.w);
-          a[i] = h;
+          l.x = tf32_residual(v.x);
+          l.y = tf32_residual(v.y);
+          l.z = tf32_residual(v.z);
+          l.w = tf32_residual(v.w);
           alo[i] = l;
         }
         fence_proxy_async_smem();
