@@ -386,7 +386,8 @@ int umma_tile_n(int n) { return n > 128 ? 128 : n; }
 void launch_umma(cudaStream_t s, const UmmaOp& u) {
 #define MX_UMMA_CASE(NN, MM)                                                                      \
   if (u.n == NN && u.mode == MM) {                                                                \
-    umma_conv_kernel<NN, MM><<<unsigned(u.grid), kUmmaThreads, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.p); \
+    umma_conv_kernel<NN, MM>                                                                      \
+        <<<unsigned(u.grid), UmmaCfg<NN, umma_tmem_a(NN, MM)>::THREADS, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.p); \
     return;                                                                                       \
   }
   MX_UMMA_INSTANCES(MX_UMMA_CASE)

@@ -1,15 +1,16 @@
 // Tensor-core contractions for sm_100a: tcgen05.mma kind::tf32 with FP32
 // accumulators in TMEM, operands staged by TMA (no multicast).
 //
-// One persistent kernel, three problem shapes (MODE):
+// One persistent kernel; the problem shapes (MODE):
 //   MODE_CONV1  1x1 conv / Dense:  D[pix][co] = b[co] + sum_ci X[pix][ci] W[co][ci]
 //               M = 128 pixels of the flat pixel axis, K = c_in
 //   MODE_CONV3  3x3 pad-1 conv:    K = (tap, ci); each tap's A block is a
 //               shifted 3-D TMA box (8 rows x 16 columns x 32 channels) whose
 //               out-of-image part TMA fills with zeros - the padding is free
+//   MODE_CONV4  4x4 stride-2 conv, the same with a stride-2 box
 //   MODE_GATE   gMLP gating Dense over a spatial axis of a blocked buffer:
 //               D[(grp, c)][a] = b[a] + sum_t X[grp, t][c] W[a][t]
-//               (MODE_GATE / MODE_GATE_GRID)
+//               (MODE_GATE / MODE_GATE_GRID / MODE_GATE_SP)
 //               M = 4 groups x 32 channels, N = a, K = t. The activation is
 //               the MN-major operand: for each t, 32 channels are contiguous
 //               in NHWC, which is one 128-byte row of the canonical SW128
@@ -17,27 +18,30 @@
 //               exactly in that layout. Block gating (t = position inside a
 //               block) and grid gating (t = the cell) differ only in the
 //               tensor map's strides.
+//   MODE_CONVT  2x2 stride-2 transposed conv: a 1x1 product with N = 4 co
+//               whose four column groups are stored to the four output taps
 //
 // Precision: every product is a 3-pass TF32 split,
 //   a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi,
-// with a_hi = a rounded to the nearest TF32 value and a_lo = a - a_hi rounded
-// to TF32 again, so each product carries ~22 significant bits (plain TF32
-// measured 46-48 dB against the fp32 CPU path under the He-normal init, below
-// the 50 dB bar). Weights are split on the host, activations in the kernel.
-// The hi*hi products and the two cross terms accumulate in separate TMEM
-// regions, added in fp32 by the epilogue: the tensor core rounds its fp32
-// accumulator at every MMA, and with one region the full-size running sum
-// took three such roundings per k-step instead of one.
+// about 21 significant bits per product (plain TF32 measured 46-48 dB against
+// the fp32 CPU path under the He-normal init, below the 50 dB bar). Weights
+// are split on the host; for activations a_hi is the fp32 tile itself, which
+// the tensor core reads truncated to TF32, and the split stage computes a_lo
+// (tf32_residual). The hi*hi products and the cross terms accumulate in
+// separate TMEM regions, added in fp32 by the epilogue: the tensor core
+// rounds its fp32 accumulator at every MMA, and with one region the full-size
+// running sum took more such roundings per k-step at full magnitude.
 //
-// Warp roles (320 threads, one CTA per SM, persistent over output tiles):
+// Warp roles (one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: A block (16 KB), B and B_lo blocks per k-block
 //   warp 1      TMEM owner and MMA issuer (one thread)
-//   warps 2-5   split: A -> (A_hi in place, A_lo beside it) per k-block
-//   warps 6-9   epilogue: TMEM -> registers -> +bias -> [elementwise tail, with a
-//               second operand TMA-loaded into the staging tile] -> swizzled
-//               smem -> TMA store
-// Two accumulator sets (N <= 128) let the epilogue of tile i overlap the MMAs
-// of tile i+1; N = 256 has room for one set only.
+//   warps 2-5   split: A_lo per k-block (into TMEM for N <= 64 convolutions,
+//               beside A in shared memory otherwise), LayerNorm on load
+//   warps 6-    epilogue, four warps per accumulator set: TMEM -> registers
+//               -> +bias -> [elementwise tail, second operand prefetched into
+//               registers] -> swizzled smem -> TMA store
+// Three accumulator sets (N <= 64) or two (N = 128) let the epilogue of
+// earlier tiles overlap the MMAs of the next one.
 // Every mbarrier wait is bounded in time; a wait that runs out records a code
 // in the status word, the kernel unwinds and frees its TMEM.
 #pragma once
@@ -179,14 +183,21 @@ struct UmmaCfg {
   // A stage holds A (and A_lo unless it lives in TMEM), B and B_lo.
   static constexpr int STAGE_BYTES = (TMEM_A ? 1 : 2) * A_BYTES + 2 * B_BYTES;
   static constexpr int STAGES = TMEM_A ? (N <= 32 ? 6 : 4) : (N <= 64 ? 4 : 3);
-  static constexpr int STAGING_BYTES = 8 * 4096;  // one 32-row x 32-column buffer per epilogue warp
   // An accumulator set is two N-column fp32 regions: the hi*hi products and
-  // the two cross terms, summed once in the epilogue. Two sets: the epilogue
-  // drains one tile while the next accumulates.
-  static constexpr int ACC_SETS = 2;
+  // the two cross terms, summed once in the epilogue. Each set has its own
+  // four epilogue warps, so while the next tile accumulates the epilogue
+  // drains one tile (two sets) or two (three sets, where TMEM has room for
+  // them beside the A_lo slots: N <= 64).
+  static constexpr int ACC_SETS = TMEM_A ? 3 : 2;
+  static constexpr int EPI_WARPS = 4 * ACC_SETS;
+  // Warp 0 producer, warp 1 MMA issuer, warps 2-5 split, then the epilogue.
+  static constexpr int THREADS = 32 * (6 + EPI_WARPS);
+  static constexpr int STAGING_BYTES = EPI_WARPS * 4096;  // one 32-row x 32-column buffer per epilogue warp
   static constexpr int A_COL0 = ACC_SETS * 2 * N;  // first TMEM column of the A_lo slots
   static constexpr int TMEM_COLS = TMEM_A ? 512 : ACC_SETS * 2 * N;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 8 * (3 * STAGES + 4) + 16;
+  static constexpr int SMEM_BYTES =
+      1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 8 * (3 * STAGES + 2 * ACC_SETS) + 16;
+  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
   static_assert(!TMEM_A || A_COL0 + STAGES * 32 <= 512, "TMEM holds the accumulators and the A_lo slots");
   static_assert(2 * N <= 256, "one instruction covers B_hi and B_lo");
 };
@@ -217,10 +228,8 @@ __device__ __forceinline__ float tf32_residual(float v) {
   return __uint_as_float((__float_as_uint(r) + 0x1000u) & 0xFFFFE000u);
 }
 
-constexpr int kUmmaThreads = 448;
-
 template <int N, int MODE>
-__global__ void __launch_bounds__(kUmmaThreads, 1)
+__global__ void __launch_bounds__(UmmaCfg<N, umma_tmem_a(N, MODE)>::THREADS, 1)
     umma_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmD,
                      UmmaConvParams p) {
@@ -238,8 +247,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   uint64_t* lo_ready = full + C::STAGES;
   uint64_t* empty = lo_ready + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;
-  uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* acc_empty = acc_full + C::ACC_SETS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + C::ACC_SETS);
   __shared__ int abort_flag;
   const volatile int* vabort = &abort_flag;
 
@@ -273,7 +282,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       mbar_init(&lo_ready[s], 128);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < C::ACC_SETS; ++a) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 128);
     }
@@ -548,11 +557,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Two sets of four warps; set `set` drains accumulator `set`, i.e. every
-    // other tile, so two tiles drain at once. A warp owns the 32 accumulator
-    // rows of its TMEM lane quarter and stages and stores them itself (one
-    // 4 KB staging buffer per warp), so no barrier joins the epilogue warps.
-    const int ew = warp - 6;        // 0..7
+    // ACC_SETS sets of four warps; set `set` drains accumulator `set`, i.e.
+    // every ACC_SETS-th tile, so that many tiles drain at once. A warp owns
+    // the 32 accumulator rows of its TMEM lane quarter and stages and stores
+    // them itself (one 4 KB staging buffer per warp), so no barrier joins the
+    // epilogue warps.
+    const int ew = warp - 6;        // 0 .. EPI_WARPS - 1
     const int set = ew >> 2;
     const int q = warp & 3;         // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;  // accumulator row this thread owns
@@ -611,7 +621,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       }
     };
 
-    const int tstep = 2 * gridDim.x;
+    const int tstep = C::ACC_SETS * gridDim.x;
     int t = blockIdx.x + set * gridDim.x, j = 0, a0 = 0, a1 = 0, n0 = 0;
     // LayerNorm statistics of this thread's output pixel, one serial pair of
     // sums per group, in channel order (the statistics kernel's order).
