@@ -367,18 +367,17 @@ void umma_attrs_once() {
   if (done) return;
 #define MX_UMMA_ATTR(NN, MM)                                                                       \
   MX_CUDA(cudaFuncSetAttribute(umma_conv_kernel<NN, MM>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                               UmmaCfg<NN, umma_tmem_a(NN, MM)>::SMEM_BYTES));
+                               UmmaCfg<NN, MM>::SMEM_BYTES));
   MX_UMMA_INSTANCES(MX_UMMA_ATTR)
 #undef MX_UMMA_ATTR
   done = true;
 }
 int umma_smem(int n, int mode) {
-  const bool ta = umma_tmem_a(n, mode);
-  switch (n) {
-    case 32: return ta ? UmmaCfg<32, true>::SMEM_BYTES : UmmaCfg<32, false>::SMEM_BYTES;
-    case 64: return ta ? UmmaCfg<64, true>::SMEM_BYTES : UmmaCfg<64, false>::SMEM_BYTES;
-    default: return UmmaCfg<128, false>::SMEM_BYTES;
-  }
+#define MX_UMMA_SMEM(NN, MM) \
+  if (n == NN && mode == MM) return UmmaCfg<NN, MM>::SMEM_BYTES;
+  MX_UMMA_INSTANCES(MX_UMMA_SMEM)
+#undef MX_UMMA_SMEM
+  throw Error(fmt("no tensor-core kernel for N=%d mode=%d", n, mode));
 }
 
 // Columns per tile for an output of n columns (32..256), and the slices.
@@ -387,7 +386,7 @@ void launch_umma(cudaStream_t s, const UmmaOp& u) {
 #define MX_UMMA_CASE(NN, MM)                                                                      \
   if (u.n == NN && u.mode == MM) {                                                                \
     umma_conv_kernel<NN, MM>                                                                      \
-        <<<unsigned(u.grid), UmmaCfg<NN, umma_tmem_a(NN, MM)>::THREADS, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.p); \
+        <<<unsigned(u.grid), UmmaCfg<NN, MM>::THREADS, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.p);           \
     return;                                                                                       \
   }
   MX_UMMA_INSTANCES(MX_UMMA_CASE)

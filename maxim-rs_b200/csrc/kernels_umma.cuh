@@ -36,8 +36,8 @@
 //   warp 0      TMA producer: A block (16 KB), B and B_lo blocks per k-block
 //   warp 1      TMEM owner and MMA issuer (one thread)
 //   warps 2-5   split: A_lo per k-block (into TMEM for N <= 64 convolutions,
-//               beside A in shared memory otherwise), LayerNorm on load
-//   warps 6-    epilogue, four warps per accumulator set: TMEM -> registers
+//   (or 2-9)    beside A in shared memory otherwise), LayerNorm on load
+//   then        epilogue, four warps per accumulator set: TMEM -> registers
 //               -> +bias -> [elementwise tail, second operand prefetched into
 //               registers] -> swizzled smem -> TMA store
 // Three accumulator sets (N <= 64) or two (N = 128) let the epilogue of
@@ -176,22 +176,31 @@ __host__ __device__ constexpr bool umma_tmem_a(int n, int mode) {
   return n <= 64 && (mode == MODE_CONV1 || mode == MODE_CONV3 || mode == MODE_CONV4);
 }
 
-template <int N, bool TMEM_A>
+template <int N, int MODE>
 struct UmmaCfg {
+  static constexpr bool TMEM_A = umma_tmem_a(N, MODE);
   static constexpr int A_BYTES = 128 * 128;  // 128 rows x 32 fp32
   static constexpr int B_BYTES = N * 128;    // N rows x 32 fp32
   // A stage holds A (and A_lo unless it lives in TMEM), B and B_lo.
   static constexpr int STAGE_BYTES = (TMEM_A ? 1 : 2) * A_BYTES + 2 * B_BYTES;
   static constexpr int STAGES = TMEM_A ? (N <= 32 ? 6 : 4) : (N <= 64 ? 4 : 3);
+  // The split stage: four warps, one per TMEM lane quarter, or for the 3x3 and
+  // 4x4 convolutions (TMEM_A) eight, two per quarter, each taking 16 of the
+  // k-block's 32 columns. Those convs split every input pixel once per tap,
+  // and the quarters whose warps share a sub-partition with the producer or
+  // the MMA issuer set the pace; halving their work per warp lets the MMA
+  // issue set it instead.
+  static constexpr int SPLIT = TMEM_A && (MODE == MODE_CONV3 || MODE == MODE_CONV4) ? 8 : 4;
   // An accumulator set is two N-column fp32 regions: the hi*hi products and
   // the two cross terms, summed once in the epilogue. Each set has its own
   // four epilogue warps, so while the next tile accumulates the epilogue
-  // drains one tile (two sets) or two (three sets, where TMEM has room for
-  // them beside the A_lo slots: N <= 64).
-  static constexpr int ACC_SETS = TMEM_A ? 3 : 2;
+  // drains one tile (two sets) or two (three sets, for the 1x1 convs with
+  // N <= 64, where TMEM has room for them beside the A_lo slots).
+  static constexpr int ACC_SETS = TMEM_A && SPLIT == 4 ? 3 : 2;
   static constexpr int EPI_WARPS = 4 * ACC_SETS;
-  // Warp 0 producer, warp 1 MMA issuer, warps 2-5 split, then the epilogue.
-  static constexpr int THREADS = 32 * (6 + EPI_WARPS);
+  // Warp 0 producer, warp 1 MMA issuer, SPLIT split warps, then the epilogue.
+  static constexpr int EPI_WARP0 = 2 + SPLIT;
+  static constexpr int THREADS = 32 * (EPI_WARP0 + EPI_WARPS);
   static constexpr int STAGING_BYTES = EPI_WARPS * 4096;  // one 32-row x 32-column buffer per epilogue warp
   static constexpr int A_COL0 = ACC_SETS * 2 * N;  // first TMEM column of the A_lo slots
   static constexpr int TMEM_COLS = TMEM_A ? 512 : ACC_SETS * 2 * N;
@@ -200,6 +209,7 @@ struct UmmaCfg {
   static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
   static_assert(!TMEM_A || A_COL0 + STAGES * 32 <= 512, "TMEM holds the accumulators and the A_lo slots");
   static_assert(2 * N <= 256, "one instruction covers B_hi and B_lo");
+  static_assert(SPLIT == 4 || TMEM_A, "eight split warps only write A_lo into TMEM");
 };
 
 enum : int {
@@ -229,12 +239,12 @@ __device__ __forceinline__ float tf32_residual(float v) {
 }
 
 template <int N, int MODE>
-__global__ void __launch_bounds__(UmmaCfg<N, umma_tmem_a(N, MODE)>::THREADS, 1)
+__global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
     umma_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmD,
                      UmmaConvParams p) {
-  constexpr bool TMEM_A = umma_tmem_a(N, MODE);
-  using C = UmmaCfg<N, TMEM_A>;
+  using C = UmmaCfg<N, MODE>;
+  constexpr bool TMEM_A = C::TMEM_A;
   using namespace sm100;
   constexpr int TAPS = MODE == MODE_CONV3 ? 9 : (MODE == MODE_CONV4 ? 16 : 1);
   constexpr bool SPATIAL = MODE == MODE_CONV3 || MODE == MODE_CONV4;  // 8x16-pixel output tiles
@@ -279,7 +289,7 @@ __global__ void __launch_bounds__(UmmaCfg<N, umma_tmem_a(N, MODE)>::THREADS, 1)
     abort_flag = 0;
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&lo_ready[s], 128);
+      mbar_init(&lo_ready[s], 32 * C::SPLIT);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < C::ACC_SETS; ++a) {
@@ -436,9 +446,13 @@ __global__ void __launch_bounds__(UmmaCfg<N, umma_tmem_a(N, MODE)>::THREADS, 1)
         mma_commit(&acc_full[acc]);
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < C::EPI_WARP0) {
     // ------------------------------------------------------------ split
-    const int tid = threadIdx.x - 64;  // 0..127
+    const int tid = threadIdx.x - 64;  // 0..127 (the SPLIT = 4 instances)
+    // TMEM_A with SPLIT = 8: warps 2-5 take columns 0-15 of each row, warps
+    // 6-9 columns 16-31; otherwise one warp takes all 32.
+    constexpr int NCH = 32 / 4 / (C::SPLIT / 4);  // float4 chunks of a row per thread
+    const int half = (warp - 2) >> 2;
     uint32_t it = 0;
     // LayerNorm on load: the statistics of the input pixel behind A row r of
     // the current k-block, if that pixel is inside the image (rows outside
@@ -504,18 +518,20 @@ __global__ void __launch_bounds__(UmmaCfg<N, umma_tmem_a(N, MODE)>::THREADS, 1)
         }
         if (TMEM_A) {
           // This warp's TMEM lane quarter: rows q*32 .. q*32+31 of A. Each
-          // thread reads its row (32 K values, 128-byte swizzled) and writes
-          // the row's A_lo into the stage's TMEM slot; with LayerNorm on
-          // load the normalised row also goes back into the tile (A_hi).
+          // thread reads its row's columns (all 32 K values, or its half of
+          // them; 128-byte swizzled) and writes their A_lo into the stage's
+          // TMEM slot; with LayerNorm on load the normalised values also go
+          // back into the tile (A_hi).
           const int r = rq;
           uint8_t* arow = base + s * C::STAGE_BYTES + r * 128;
-          float lo[32];
+          float lo[4 * NCH];
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            float4* p4 = reinterpret_cast<float4*>(arow + ((c ^ (r & 7)) << 4));
+          for (int c = 0; c < NCH; ++c) {
+            const int cc = half * NCH + c;  // float4 chunk of the row
+            float4* p4 = reinterpret_cast<float4*>(arow + ((cc ^ (r & 7)) << 4));
             float4 v = *p4;
             if (ln) {
-              v = ln_apply4(v, lm, lr, cb * 32 + 4 * c);
+              v = ln_apply4(v, lm, lr, cb * 32 + 4 * cc);
               *p4 = v;
             }
             lo[4 * c] = tf32_residual(v.x);
@@ -523,7 +539,12 @@ __global__ void __launch_bounds__(UmmaCfg<N, umma_tmem_a(N, MODE)>::THREADS, 1)
             lo[4 * c + 2] = tf32_residual(v.z);
             lo[4 * c + 3] = tf32_residual(v.w);
           }
-          tmem_st32(tmem + (uint32_t(q * 32) << 16) + C::A_COL0 + s * 32, lo);
+          const uint32_t slot = tmem + (uint32_t(q * 32) << 16) + C::A_COL0 + s * 32;
+          if (NCH == 8) {
+            tmem_st32(slot, lo);
+          } else {
+            tmem_st16(slot + 16 * half, lo);
+          }
           tmem_wait_st();
           if (p.ln_stats) fence_proxy_async_smem();
           tc_fence_before();
@@ -562,7 +583,7 @@ __global__ void __launch_bounds__(UmmaCfg<N, umma_tmem_a(N, MODE)>::THREADS, 1)
     // the 32 accumulator rows of its TMEM lane quarter and stages and stores
     // them itself (one 4 KB staging buffer per warp), so no barrier joins the
     // epilogue warps.
-    const int ew = warp - 6;        // 0 .. EPI_WARPS - 1
+    const int ew = warp - C::EPI_WARP0;  // 0 .. EPI_WARPS - 1
     const int set = ew >> 2;
     const int q = warp & 3;         // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;  // accumulator row this thread owns
