@@ -392,7 +392,16 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
       // together. An MMA costs about the same below N = 128 whatever its
       // width, so the k-step takes two instructions instead of three.
       constexpr uint32_t idesc2 = idesc_tf32(128, 2 * N, GATE ? 1 : 0, 0);
-      uint32_t it = 0, tc = 0;
+      // The issuing thread shares its sub-partition with split and epilogue
+      // warps, so its own instruction count per k-block sets part of the
+      // pace: the stage and phase step without division, and each stage's
+      // descriptors are built once per k-block and stepped by constants
+      // (32 bytes along K = 2 in the address field; 1024 bytes = 64 for the
+      // MN-major layout).
+      const uint32_t base_u = smem_u32(base);
+      constexpr uint32_t kStepK = GATE ? 64u : 2u;
+      int s = 0;
+      uint32_t ph = 0, tc = 0;
       for (int t = blockIdx.x; t < p.tiles && !*vabort; t += gridDim.x, ++tc) {
         const uint32_t acc = tc % C::ACC_SETS, aph = (tc / C::ACC_SETS) & 1;
         if (!mbar_wait(&acc_empty[acc], aph ^ 1, vabort)) {
@@ -402,32 +411,26 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
         tc_fence_after();
         const uint32_t d = tmem + acc * 2 * N, dx = d + N;
         bool ok = true;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const int s = it % C::STAGES;
-          const uint32_t ph = (it / C::STAGES) & 1;
+        for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(&lo_ready[s], ph, vabort)) {
             fail(kErrMmaLo);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a = smem_u32(base + s * C::STAGE_BYTES);
+          const uint32_t a = base_u + s * C::STAGE_BYTES;
           const uint32_t b = a + (TMEM_A ? 1 : 2) * C::A_BYTES, alo = a + C::A_BYTES;
           // TMEM_A: this stage's A_lo sits in TMEM columns [slot, slot + 32);
           // k-step k reads 8 of them.
           const uint32_t slot = tmem + C::A_COL0 + s * 32;
+          const uint64_t da0 = GATE ? desc_mnmajor_sw128_32b(a, 4096) : desc_kmajor_sw128(a);
+          const uint64_t dalo0 = GATE ? desc_mnmajor_sw128_32b(alo, 4096) : desc_kmajor_sw128(alo);
+          const uint64_t db0 = desc_kmajor_sw128(b);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            uint64_t da, dalo = 0;
-            if (GATE) {
-              // MN-major: k-step k covers K rows 8k..8k+7 of each 4 KB group block.
-              da = desc_mnmajor_sw128_32b(a + 1024 * k, 4096);
-              dalo = desc_mnmajor_sw128_32b(alo + 1024 * k, 4096);
-            } else {
-              da = desc_kmajor_sw128(a + 32 * k);
-              if (!TMEM_A) dalo = desc_kmajor_sw128(alo + 32 * k);
-            }
-            const uint64_t db = desc_kmajor_sw128(b + 32 * k);
+            // GATE: MN-major, k-step k covers K rows 8k..8k+7 of each 4 KB
+            // group block; otherwise K-major, 8 fp32 = 32 bytes per k-step.
+            const uint64_t da = da0 + kStepK * k, db = db0 + 2u * k;
             // The running sum of the hi*hi products takes one accumulator
             // update per k-step; the cross terms, 2^-10 of its size or less,
             // go to their own region, so the accumulator's rounding at each
@@ -437,10 +440,11 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
             if (TMEM_A) {
               mma_tf32_ts(dx, slot + 8 * k, db, idesc, 1u);
             } else {
-              mma_tf32(dx, dalo, db, idesc, 1u);
+              mma_tf32(dx, dalo0 + kStepK * k, db, idesc, 1u);
             }
           }
           mma_commit(&empty[s]);
+          if (++s == C::STAGES) s = 0, ph ^= 1;
         }
         if (!ok) break;
         mma_commit(&acc_full[acc]);
