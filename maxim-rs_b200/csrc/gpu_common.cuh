@@ -37,14 +37,14 @@ inline unsigned blocks_for(int64_t n, int threads) { return unsigned((n + thread
 // GELU in its erf form, x * Phi(x), evaluated as
 //   x Phi(x) = max(x, 0) - u Phi(-u),   u = |x|,
 //   Phi(-u)  = exp(-u^2 / 2) * R(u),     R(u) = erfcx(u / sqrt 2) / 2,
-// with R a degree-12 polynomial in u fitted for this kernel set (least squares
+// with R a degree-11 polynomial in u fitted for this kernel set (least squares
 // on [0, 5.6] weighted by exp(-u^2 / 2), reweighted toward minimax) and u
 // clamped to 5.6 inside R, past which the term is below 2^-24 |x|. No
 // subtraction cancels: for x < 0 the result is the product itself. The
 // exponential is one ex2.approx. Including fp32 evaluation, the error over
-// [-12, 12] stays within about 1.2 ulp of |x| and, for x > -0.7, 3 ulp of the
+// [-12, 12] stays within about 1.3 ulp of |x| and, for x > -0.7, 3 ulp of the
 // result (checked against a double-precision erf by tests/test_gelu_poly.py;
-// the erf form loses about as much to the rounding of 1 + erf). It costs 19
+// the erf form loses about as much to the rounding of 1 + erf). It costs 18
 // instructions, where
 // 0.5 x (1 + erff(x / sqrt 2)) costs about 28, and the tensor-core epilogue
 // of a GELU step is bound by its instruction issue.
@@ -54,24 +54,23 @@ __device__ __forceinline__ float ex2_approx(float a) {
   return r;
 }
 __device__ __forceinline__ float gelu_f(float x) {
-  constexpr float kGeluR[13] = {
-      0.5f,
-      -0.3989417850971222f,
-      0.24999110400676727f,
-      -0.1329168826341629f,
-      0.062262363731861115f,
-      -0.02606913261115551f,
-      0.009659754112362862f,
-      -0.0030553194228559732f,
-      0.0007796600693836808f,
-      -0.0001497869088780135f,
-      1.9892220734618604e-05f,
-      -1.6035770613598288e-06f,
-      5.852924900295875e-08f};
+  constexpr float kGeluR[12] = {
+      0.4999999701976776f,
+      -0.3989405930042267f,
+      0.24997256696224213f,
+      -0.13280577957630157f,
+      0.06192392110824585f,
+      -0.025471799075603485f,
+      0.009003829210996628f,
+      -0.0025900795590132475f,
+      0.0005636486457660794f,
+      -8.47700794111006e-05f,
+      7.708666089456528e-06f,
+      -3.155372496621567e-07f};
   const float u = fminf(fabsf(x), 5.6f);
-  float p = kGeluR[12];
+  float p = kGeluR[11];
 #pragma unroll
-  for (int k = 11; k >= 0; --k) p = fmaf(p, u, kGeluR[k]);
+  for (int k = 10; k >= 0; --k) p = fmaf(p, u, kGeluR[k]);
   const float e = ex2_approx(__fmul_rn(__fmul_rn(x, -0.72134752f), x));  // 2^(-x^2 log2(e) / 2)
   return fmaf(-__fmul_rn(u, e), p, fmaxf(x, 0.0f));
 }

@@ -250,8 +250,10 @@ __device__ __forceinline__ float4 tap_norm(float4 acc, float sm, float rcp) {
   return acc;
 }
 
+// Both passes are bound by load latency (each thread's taps wait in turn),
+// so they are held to 32 registers for eight 256-thread blocks per SM.
 // Horizontal pass: dst row r (of hin), column xo, from src row r.
-__global__ void resize_h4_kernel(int lg4, int win, int wout, TapTable4 t, const float* __restrict__ src, int ss,
+__global__ void __launch_bounds__(256, 8) resize_h4_kernel(int lg4, int win, int wout, TapTable4 t, const float* __restrict__ src, int ss,
                                  float* __restrict__ dst, int sd) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (wout << lg4)) return;
@@ -265,7 +267,7 @@ __global__ void resize_h4_kernel(int lg4, int win, int wout, TapTable4 t, const 
 }
 
 // Vertical pass: dst row yo (of hout) from rows j0.. of the horizontal result.
-__global__ void resize_v4_kernel(int lg4, int wout, TapTable4 t, const float* __restrict__ src, int ss,
+__global__ void __launch_bounds__(256, 8) resize_v4_kernel(int lg4, int wout, TapTable4 t, const float* __restrict__ src, int ss,
                                  float* __restrict__ dst, int sd) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (wout << lg4)) return;

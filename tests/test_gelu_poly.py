@@ -1,5 +1,5 @@
 """The GELU the CUDA kernels evaluate (csrc/gpu_common.cuh, gelu_f):
-max(x, 0) - u * 2^(-x^2 log2(e) / 2) * R(u), u = min(|x|, 5.6), R a degree-12
+max(x, 0) - u * 2^(-x^2 log2(e) / 2) * R(u), u = min(|x|, 5.6), R a fitted
 polynomial. This restates that evaluation step by step in numpy fp32 (the
 exponential exactly rounded; the device's ex2.approx adds at most about 2 ulp
 to the one factor it produces) and bounds its error against the erf form of
@@ -18,10 +18,10 @@ SRC = os.path.join(os.path.dirname(__file__), "..", "maxim-rs_b200", "csrc", "gp
 
 def coefficients():
     text = open(SRC).read()
-    m = re.search(r"kGeluR\[13\]\s*=\s*\{([^}]*)\}", text)
+    m = re.search(r"kGeluR\[(\d+)\]\s*=\s*\{([^}]*)\}", text)
     assert m, "kGeluR not found in gpu_common.cuh"
-    vals = [np.float32(v.strip().rstrip("f")) for v in m.group(1).split(",") if v.strip()]
-    assert len(vals) == 13
+    vals = [np.float32(v.strip().rstrip("f")) for v in m.group(2).split(",") if v.strip()]
+    assert len(vals) == int(m.group(1))
     return vals
 
 
@@ -33,8 +33,8 @@ def fma32(a, b, c):
 def gelu_device(x, c):
     x = x.astype(np.float32)
     u = np.minimum(np.abs(x), np.float32(5.6))
-    p = np.full_like(x, c[12])
-    for k in range(11, -1, -1):
+    p = np.full_like(x, c[-1])
+    for k in range(len(c) - 2, -1, -1):
         p = fma32(p, u, np.full_like(x, c[k]))
     with np.errstate(over="ignore"):
         a = (x * np.float32(-0.72134752)).astype(np.float32)
