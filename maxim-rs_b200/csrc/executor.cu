@@ -180,7 +180,7 @@ CUtensorMap make_tensor_map(const void* base, int rank, const uint64_t* dims, co
 // The tensor maps and the launch parameters of one tensor-core conv: A, B
 // (hi, lo) and the output D.
 struct UmmaOp {
-  CUtensorMap a, b, blo, d;
+  CUtensorMap a, b, blo, d, l;  // l: the LayerNorm output of a CONV1 epilogue (else a copy of d)
   UmmaConvParams p{};
   int n = 0, taps = 1, mode = 0, grid = 0, smem = 0;
 };
@@ -386,7 +386,7 @@ void launch_umma(cudaStream_t s, const UmmaOp& u) {
 #define MX_UMMA_CASE(NN, MM)                                                                      \
   if (u.n == NN && u.mode == MM) {                                                                \
     umma_conv_kernel<NN, MM>                                                                      \
-        <<<unsigned(u.grid), UmmaCfg<NN, MM>::THREADS, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.p);           \
+        <<<unsigned(u.grid), UmmaCfg<NN, MM>::THREADS, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.l, u.p);      \
     return;                                                                                       \
   }
   MX_UMMA_INSTANCES(MX_UMMA_CASE)
@@ -433,6 +433,8 @@ struct UmmaEpi {
   mx_op perm{};
   int32_t ln_stats = -1;                 // LayerNorm on load: statistics buffer
   int64_t ln_scale = -1, ln_bias = -1;  // and the pool offsets of its weights
+  int32_t lo_dst = -1, lo_c0 = 0;       // LayerNorm of output columns [lo_c0, +32) written to lo_dst
+  int64_t lo_scale = -1, lo_bias = -1;
   int32_t st_out[2] = {-1, -1};          // LayerNorm statistics the epilogue writes
   int32_t st_c0[2] = {0, 0};
   int32_t st_c = 0;
@@ -491,6 +493,7 @@ Step umma_gate_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
       }
       u->a = make_tensor_map(x.ptr, 5, dims, sa, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
       u->d = make_tensor_map(d.ptr, 5, dims, sd, box);
+      u->l = u->d;
       u->mode = MODE_GATE_SP;
       u->p.sp_mode = op.mode == 0 ? 0 : 1;
       u->p.fw = P.fw;
@@ -521,6 +524,7 @@ Step umma_gate_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
       uint32_t bd[3] = {box[0], box[1], 1};
       if (op.mode == 0) bd[1] = 1, bd[2] = 32;
       u->d = make_tensor_map(d.ptr, 3, dims, sd, bd);
+      u->l = u->d;
     }
     u->p.n_slices = n / tn;
     u->p.tiles_x = (u->p.groups + 3) / 4;
@@ -589,6 +593,17 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
       uint64_t dd[2] = {uint64_t(n), uint64_t(d.npix)}, sd[1] = {uint64_t(d.stride) * 4};
       uint32_t bd[2] = {32, 32};
       u->d = make_tensor_map(d.ptr, 2, dd, sd, bd);
+      u->l = u->d;
+      if (E.lo_dst >= 0) {
+        // The LayerNorm of 32 output channels goes to its own buffer, in
+        // the same 32-pixel boxes.
+        View y = view_of(*G, *L, E.lo_dst);
+        uint64_t dy[2] = {32, uint64_t(y.npix)}, sy[1] = {uint64_t(y.stride) * 4};
+        u->l = make_tensor_map(y.ptr, 2, dy, sy, bd);
+        u->p.lo_col = E.lo_c0;
+        u->p.lo_scale = reinterpret_cast<const float*>(G->pool.dev + E.lo_scale);
+        u->p.lo_bias = reinterpret_cast<const float*>(G->pool.dev + E.lo_bias);
+      }
       u->p.tiles = int((x.npix + 127) / 128);
       u->p.tiles_x = 0;
       u->p.e_npix = int(d.npix);
@@ -610,6 +625,7 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
       uint64_t sd[2] = {uint64_t(d.stride) * 4, uint64_t(OW) * uint64_t(d.stride) * 4};
       uint32_t bd[3] = {32, 16, 2};  // per epilogue warp: two rows of the 8x16 tile
       u->d = make_tensor_map(d.ptr, 3, dd, sd, bd);
+      u->l = u->d;
       u->p.e_w = OW;
       u->p.e_h = OH;
       u->p.tiles_x = (OW + 15) / 16;
@@ -679,6 +695,7 @@ Step umma_convt_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int
     uint64_t sd[4] = {px, 2 * px, 2 * uint64_t(W) * px, 4 * uint64_t(W) * px};
     uint32_t bd[5] = {32, 1, 32, 1, 1};
     u->d = make_tensor_map(d.ptr, 5, dd, sd, bd);
+    u->l = u->d;
     u->p.tiles = int((x.npix + 127) / 128);
     u->p.tiles_x = 0;
     u->p.e_npix = int(x.npix);
@@ -726,6 +743,12 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
       E.ln_scale = raw(fs->ln_scale);
       E.ln_bias = raw(fs->ln_bias);
     }
+    if (fs->ln_out >= 0) {
+      E.lo_dst = fs->ln_out;
+      E.lo_c0 = fs->ln_out_c0;
+      E.lo_scale = raw(fs->ln_out_scale);
+      E.lo_bias = raw(fs->ln_out_bias);
+    }
     for (int g2 = 0; g2 < 2; ++g2) {
       E.st_out[g2] = fs->stats_out[g2];
       E.st_c0[g2] = fs->stats_c0[g2];
@@ -733,7 +756,7 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
     E.st_c = fs->stats_c;
   }
   bool needs_umma = (E.epi != EPI_NONE && o.kind != MX_OP_CHAN_SCALE) || E.spatial || E.ln_stats >= 0 ||
-                    E.st_out[0] >= 0;
+                    E.st_out[0] >= 0 || E.lo_dst >= 0;
   bool on_umma = false;
   mx_gpu* G = &g;
   auto P = [G](int64_t off) -> const float* {
@@ -1280,6 +1303,7 @@ int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) {
       for (int32_t c : ss.covers) g->primary_of[size_t(c)] = ss.op;
       g->sched_flags[size_t(ss.op)] = (ss.stats_only ? MX_SCHED_STATS_ONLY : 0) |
                                       (ss.ln_stats >= 0 ? MX_SCHED_LN_ON_LOAD : 0);
+      if (ss.ln_out_op >= 0) g->sched_flags[size_t(ss.ln_out_op)] |= MX_SCHED_LN_IN_EPILOGUE;
     }
     add_boundary_steps(*g, g->fsteps, &g->foffs);
     for (auto& st : g->fsteps) g->kernels += st.kernels;
@@ -1571,8 +1595,10 @@ int mx_plan_schedule(const mx_plan* plan, mx_gpu_stats* stats, int32_t* primary,
     }
     if (flags) {
       for (int32_t i = 0; i < n_ops; ++i) flags[i] = 0;
-      for (const SchedStep& ss : S.steps)
+      for (const SchedStep& ss : S.steps) {
         flags[ss.op] = (ss.stats_only ? MX_SCHED_STATS_ONLY : 0) | (ss.ln_stats >= 0 ? MX_SCHED_LN_ON_LOAD : 0);
+        if (ss.ln_out_op >= 0) flags[ss.ln_out_op] |= MX_SCHED_LN_IN_EPILOGUE;
+      }
     }
   });
 }

@@ -118,6 +118,11 @@ struct UmmaConvParams {
   int st_c0[2];
   int st_c;
   float st_eps;
+  // CONV1 LayerNorm of output columns [lo_col, lo_col + 32), written through
+  // the fifth tensor map (tmL) beside the plain output; lo_scale null if off.
+  int lo_col;
+  const float* lo_scale;
+  const float* lo_bias;
   const float* bias;  // per output column, or null
   int* status;        // device status word (0 = ok)
 };
@@ -242,7 +247,7 @@ template <int N, int MODE>
 __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
     umma_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmD,
-                     UmmaConvParams p) {
+                     const __grid_constant__ CUtensorMap tmL, UmmaConvParams p) {
   using C = UmmaCfg<N, MODE>;
   constexpr bool TMEM_A = C::TMEM_A;
   using namespace sm100;
@@ -301,6 +306,7 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
     tma_prefetch(&tmB);
     tma_prefetch(&tmBlo);
     tma_prefetch(&tmD);
+    if (MODE == MODE_CONV1 && p.lo_scale) tma_prefetch(&tmL);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -671,6 +677,8 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
       if (lane == 0) bulk_wait_read<0>();  // this warp's previous store has read the buffer
       __syncwarp();
       const uint32_t tcol = tmem + (uint32_t(q * 32) << 16) + set * 2 * N + j * 32;
+      // The chunk whose LayerNorm this step also writes (below).
+      const bool lnc = MODE == MODE_CONV1 && p.lo_scale != nullptr && n0 + j * 32 == p.lo_col;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         float v[16], x[16], e[16];
@@ -770,6 +778,45 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
           }
         }
         bulk_commit();
+      }
+      if (MODE == MODE_CONV1 && lnc) {
+        // The LayerNorm of this pixel's 32 values, read back from the row
+        // this thread just staged (the plain chunk's store only reads it), in
+        // the LayerNorm kernel's order: serial sums over the channels, then
+        // ((v - m) * rstd) * w + b, written over the row once that store has
+        // read it.
+        float4* rowp = reinterpret_cast<float4*>(sb + lane * 128);
+        float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 v = rowp[i ^ (lane & 7)];
+          s1 = __fadd_rn(s1, v.x), s2 = __fadd_rn(s2, __fmul_rn(v.x, v.x));
+          s1 = __fadd_rn(s1, v.y), s2 = __fadd_rn(s2, __fmul_rn(v.y, v.y));
+          s1 = __fadd_rn(s1, v.z), s2 = __fadd_rn(s2, __fmul_rn(v.z, v.z));
+          s1 = __fadd_rn(s1, v.w), s2 = __fadd_rn(s2, __fmul_rn(v.w, v.w));
+        }
+        const float m = __fdiv_rn(s1, 32.0f);
+        const float var = __fsub_rn(__fdiv_rn(s2, 32.0f), __fmul_rn(m, m));
+        const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(fmaxf(var, 0.0f), p.st_eps)));
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float4 v = rowp[i ^ (lane & 7)];
+          const float4 w = __ldg(reinterpret_cast<const float4*>(p.lo_scale) + i);
+          const float4 b = __ldg(reinterpret_cast<const float4*>(p.lo_bias) + i);
+          v.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, m), rs), w.x), b.x);
+          v.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, m), rs), w.y), b.y);
+          v.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, m), rs), w.z), b.z);
+          v.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, m), rs), w.w), b.w);
+          rowp[i ^ (lane & 7)] = v;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmL, sb, 0, a0 + 32 * q);
+          bulk_commit();
+        }
       }
       if (++j == N / 32) j = 0, t += tstep;
       if (has_e && t < p.tiles) load_e(t, j, ecur);

@@ -85,12 +85,13 @@ int step_reads(const SchedStep& st, int32_t* r) {
   if (st.ln_stats >= 0) r[n++] = st.ln_stats;
   return n;
 }
-// Everything a scheduled step writes, the statistics of its epilogue
-// included. w holds 4.
+// Everything a scheduled step writes, the statistics and the LayerNorm of
+// its epilogue included. w holds 5.
 int step_writes(const SchedStep& st, int32_t* w) {
   int n = writes_of(st.o, w);
   for (int g = 0; g < 2; ++g)
     if (st.stats_out[g] >= 0) w[n++] = st.stats_out[g];
+  if (st.ln_out >= 0) w[n++] = st.ln_out;
   return n;
 }
 
@@ -439,7 +440,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     bool ok = true;
     for (size_t s = j; s-- > 0;) {
       if (dead[s]) continue;
-      int32_t w[4];
+      int32_t w[5];
       const int nw = step_writes(W[s], w);
       bool hit = false;
       for (int a = 0; a < nw; ++a) hit |= G.overlap(w[a], x);
@@ -466,6 +467,57 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     ++S.ops_fused;
   }
 
+  // 3c. LayerNorm from the producer: a LayerNorm over exactly one 32-column
+  // chunk of a tensor-core 1x1 conv's output (whose epilogue threads hold
+  // whole pixel rows) is computed by that epilogue, which writes the
+  // normalised chunk to the LayerNorm's output as well as the chunk itself
+  // to its own. The LayerNorm's output is then written at the conv's step,
+  // so nothing between the two may touch it.
+  for (size_t j = 0; fuse && j < W.size(); ++j) {
+    if (dead[j] || W[j].o.kind != MX_OP_CHAN_LN || W[j].stats_only) continue;
+    const mx_op L = W[j].o;
+    const int32_t x = L.src, y = L.dst;
+    size_t i = SIZE_MAX;
+    bool ok = true;
+    for (size_t s = j; s-- > 0;) {
+      if (dead[s]) continue;
+      int32_t w[5];
+      const int nw = step_writes(W[s], w);
+      bool hit = false;
+      for (int a = 0; a < nw; ++a) hit |= G.overlap(w[a], x);
+      if (!hit) continue;
+      if (G.covers(W[s].o.dst, x)) i = s;
+      else ok = false;
+      break;
+    }
+    if (!ok || i == SIZE_MAX) continue;
+    SchedStep& P = W[i];
+    if (P.o.kind != MX_OP_CONV1X1 || P.ln_out >= 0 || H.stats_slice(P.o) <= 0 || !H.tma_view(y, 32)) continue;
+    const int64_t c0 = G.lo[size_t(x)] - G.lo[size_t(P.o.dst)], c = G.hi[size_t(x)] - G.lo[size_t(x)];
+    if (c != 32 || c0 % 32 != 0) continue;
+    if (G.overlap(y, p.output) || G.overlap(y, P.o.dst)) continue;
+    int32_t pr[4];
+    const int npr = step_reads(P, pr);
+    for (int a = 0; a < npr; ++a) ok = ok && !G.overlap(pr[a], y);
+    for (size_t s = i + 1; s < j && ok; ++s) {
+      if (dead[s]) continue;
+      int32_t r[4], w[5];
+      const int nr = step_reads(W[s], r), nw = step_writes(W[s], w);
+      for (int a = 0; a < nr; ++a) ok = ok && !G.overlap(r[a], y);
+      for (int a = 0; a < nw; ++a) ok = ok && !G.overlap(w[a], y);
+    }
+    if (!ok) continue;
+    P.ln_out = y;
+    P.ln_out_c0 = int32_t(c0);
+    P.ln_out_scale = L.scale;
+    P.ln_out_bias = L.bias;
+    P.ln_out_op = W[j].op;
+    P.covers.insert(P.covers.end(), W[j].covers.begin(), W[j].covers.end());
+    dead[j] = 1;
+    ++S.ln_in_epilogue;
+    ++S.ops_fused;
+  }
+
   for (size_t i = 0; i < W.size(); ++i)
     if (!dead[i]) S.steps.push_back(std::move(W[i]));
 
@@ -482,7 +534,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
   touch(p.input, -1);
   touch(p.output, m);
   for (int t = 0; t < m; ++t) {
-    int32_t r[4], w[4];
+    int32_t r[4], w[5];
     const int nr = step_reads(S.steps[size_t(t)], r);
     const int nw = step_writes(S.steps[size_t(t)], w);
     for (int a = 0; a < nr; ++a) touch(r[a], t);

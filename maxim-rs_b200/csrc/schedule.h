@@ -79,6 +79,10 @@ struct SchedStep {
   int32_t stats_out[2] = {-1, -1};
   int32_t stats_c0[2] = {0, 0};
   int32_t stats_c = 0;
+  // A tensor-core 1x1 conv whose epilogue also writes the LayerNorm of the
+  // 32 output channels [ln_out_c0, ln_out_c0 + 32) to buffer ln_out (-1: none),
+  // with the LayerNorm's scale and bias weights: the LayerNorm op it covers.
+  int32_t ln_out = -1, ln_out_c0 = 0, ln_out_scale = -1, ln_out_bias = -1, ln_out_op = -1;
 };
 
 struct Schedule {
@@ -90,6 +94,7 @@ struct Schedule {
   int ops_fused = 0;          // plan ops carried out inside another op's step
   int ln_on_load = 0;         // LayerNorms applied by their consumer
   int stats_in_epilogue = 0;  // of those, statistics written by the producer's epilogue
+  int ln_in_epilogue = 0;     // LayerNorms written whole by their producer's epilogue
 };
 
 struct ScheduleHooks {

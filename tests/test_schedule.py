@@ -50,12 +50,17 @@ def test_schedule_shape(variant, h, w, mx):
     _, _, flags = mx.plan_schedule(plan, flags=True)
     stats_only = (flags & mx._native.SCHED_STATS_ONLY) > 0
     on_load = (flags & mx._native.SCHED_LN_ON_LOAD) > 0
+    ln_out = (flags & mx._native.SCHED_LN_IN_EPILOGUE) > 0
     ln = kinds == LN
-    in_epilogue = ln & (primary >= 0) & (primary != idx)
+    in_epilogue = ln & (primary >= 0) & (primary != idx) & ~ln_out
     assert on_load.sum() > 0 and stats_only.sum() + in_epilogue.sum() == on_load.sum()
     assert (kinds[stats_only] == LN).all() and (kinds[on_load] == CONV1X1).all()
     assert np.isin(kinds[primary[in_epilogue]], [CONV1X1, CONV3X3, 12]).all()
     assert in_epilogue.sum() > stats_only.sum()
+    # A LayerNorm over one 32-channel chunk of a tensor-core 1x1 conv's output
+    # is written whole by that conv's epilogue (the gMLP gates' v halves).
+    assert ln_out.sum() > 0 and (ln_out <= ln).all()
+    assert (kinds[primary[ln_out]] == CONV1X1).all() and all(ops[i].c == 32 for i in np.nonzero(ln_out)[0])
 
 
 def test_schedule_off_keeps_every_op(mx):
