@@ -434,6 +434,7 @@ struct UmmaEpi {
   int32_t ln_stats = -1;                 // LayerNorm on load: statistics buffer
   int64_t ln_scale = -1, ln_bias = -1;  // and the pool offsets of its weights
   int32_t lo_dst = -1, lo_c0 = 0;       // LayerNorm of output columns [lo_c0, +32) written to lo_dst
+  bool lo_only = false;                 // ...and those columns themselves not stored
   int64_t lo_scale = -1, lo_bias = -1;
   int32_t st_out[2] = {-1, -1};          // LayerNorm statistics the epilogue writes
   int32_t st_c0[2] = {0, 0};
@@ -601,6 +602,7 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
         uint64_t dy[2] = {32, uint64_t(y.npix)}, sy[1] = {uint64_t(y.stride) * 4};
         u->l = make_tensor_map(y.ptr, 2, dy, sy, bd);
         u->p.lo_col = E.lo_c0;
+        u->p.lo_only = E.lo_only ? 1 : 0;
         u->p.lo_scale = reinterpret_cast<const float*>(G->pool.dev + E.lo_scale);
         u->p.lo_bias = reinterpret_cast<const float*>(G->pool.dev + E.lo_bias);
       }
@@ -746,6 +748,7 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
     if (fs->ln_out >= 0) {
       E.lo_dst = fs->ln_out;
       E.lo_c0 = fs->ln_out_c0;
+      E.lo_only = fs->ln_out_only;
       E.lo_scale = raw(fs->ln_out_scale);
       E.lo_bias = raw(fs->ln_out_bias);
     }

@@ -121,6 +121,7 @@ struct UmmaConvParams {
   // CONV1 LayerNorm of output columns [lo_col, lo_col + 32), written through
   // the fifth tensor map (tmL) beside the plain output; lo_scale null if off.
   int lo_col;
+  int lo_only;  // the chunk itself has no reader: only its LayerNorm is stored
   const float* lo_scale;
   const float* lo_bias;
   const float* bias;  // per output column, or null
@@ -756,7 +757,7 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
       if (lane == 0) {
         const int col = n0 + j * 32;
         if (MODE == MODE_CONV1) {
-          tma_store_2d(&tmD, sb, col, a0 + 32 * q);
+          if (!(lnc && p.lo_only)) tma_store_2d(&tmD, sb, col, a0 + 32 * q);
         } else if (MODE == MODE_CONVT) {
           // Rows a0 + 32q .. +31 are one row segment of the input image.
           const int pix = a0 + 32 * q;

@@ -512,6 +512,19 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     P.ln_out_scale = L.scale;
     P.ln_out_bias = L.bias;
     P.ln_out_op = W[j].op;
+    // Whether any later step reads the chunk itself (before a step covers it
+    // with new values): if none does, the epilogue stores only its LayerNorm.
+    bool read = G.overlap(x, p.output);
+    for (size_t s = i + 1; s < W.size() && !read; ++s) {
+      if (dead[s] || s == j) continue;
+      int32_t r[4], w[5];
+      const int nr = step_reads(W[s], r), nw = step_writes(W[s], w);
+      for (int a = 0; a < nr; ++a) read = read || G.overlap(r[a], x);
+      bool gone = false;
+      for (int a = 0; a < nw; ++a) gone = gone || G.covers(w[a], x);
+      if (gone) break;
+    }
+    P.ln_out_only = !read;
     P.covers.insert(P.covers.end(), W[j].covers.begin(), W[j].covers.end());
     dead[j] = 1;
     ++S.ln_in_epilogue;

@@ -83,6 +83,8 @@ struct SchedStep {
   // 32 output channels [ln_out_c0, ln_out_c0 + 32) to buffer ln_out (-1: none),
   // with the LayerNorm's scale and bias weights: the LayerNorm op it covers.
   int32_t ln_out = -1, ln_out_c0 = 0, ln_out_scale = -1, ln_out_bias = -1, ln_out_op = -1;
+  // ...and nothing else reads the chunk itself, so it is not stored.
+  bool ln_out_only = false;
 };
 
 struct Schedule {
