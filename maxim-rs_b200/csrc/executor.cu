@@ -360,7 +360,7 @@ bool umma_gate_spatial_ok(const mx_gpu& g, const Layout& L, const mx_op& gate, c
 // 128-column slices) x MODE.
 #define MX_UMMA_INSTANCES(X)                                                                        \
   X(32, 0) X(64, 0) X(128, 0) X(32, 1) X(64, 1) X(128, 1) X(32, 2) X(64, 2) X(128, 2) X(32, 3) X(64, 3) \
-  X(128, 3) X(32, 4) X(64, 4) X(128, 4) X(32, 5) X(64, 5) X(128, 5) X(128, 6)
+  X(128, 3) X(32, 4) X(64, 4) X(128, 4) X(32, 5) X(64, 5) X(128, 5) X(128, 6) X(32, 7) X(64, 7)
 
 void umma_attrs_once() {
   static bool done = false;
@@ -616,7 +616,10 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
       const int OH = taps == 16 ? op.oh : H, OW = taps == 16 ? op.ow : W;
       uint64_t da[3] = {uint64_t(ci), uint64_t(W), uint64_t(H)};
       uint64_t sa[2] = {uint64_t(x.stride) * 4, uint64_t(W) * uint64_t(x.stride) * 4};
-      uint32_t ba[3] = {32, 16, 8};
+      // The 3x3 conv with at most 64 output columns per tile stages one
+      // 16 x 10 box per column shift instead (MODE_CONV3H).
+      const bool halo = taps == 9 && tn <= 64;
+      uint32_t ba[3] = {32, 16, uint32_t(halo ? 10 : 8)};
       if (taps == 16) {
         uint32_t ba2[3] = {32, 32, 16}, es[3] = {1, 2, 2};
         u->a = make_tensor_map(x.ptr, 3, da, sa, ba2, CU_TENSOR_MAP_SWIZZLE_128B, es);
@@ -645,7 +648,7 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
     u->p.status = G->status;
     u->n = tn;
     u->taps = taps;
-    u->mode = taps == 9 ? MODE_CONV3 : (taps == 16 ? MODE_CONV4 : MODE_CONV1);
+    u->mode = taps == 9 ? (tn <= 64 ? MODE_CONV3H : MODE_CONV3) : (taps == 16 ? MODE_CONV4 : MODE_CONV1);
     u->grid = std::min(u->p.tiles, G->sms);
     u->smem = umma_smem(tn, u->mode);
   };

@@ -18,6 +18,11 @@
 //               exactly in that layout. Block gating (t = position inside a
 //               block) and grid gating (t = the cell) differ only in the
 //               tensor map's strides.
+//   MODE_CONV3H the 3x3 conv for N <= 64 by column shift: a stage holds one
+//               16 x 10 box (the tile's rows with their halo) for shift kx
+//               and the weights of the three taps (ky, kx); tap ky reads the
+//               box from row 16 ky. Each input pixel is split once per shift
+//               rather than once per tap.
 //   MODE_CONVT  2x2 stride-2 transposed conv: a 1x1 product with N = 4 co
 //               whose four column groups are stored to the four output taps
 //
@@ -77,7 +82,8 @@ enum : int {
   MODE_GATE_GRID = 3,
   MODE_CONV4 = 4,
   MODE_GATE_SP = 5,
-  MODE_CONVT = 6
+  MODE_CONVT = 6,
+  MODE_CONV3H = 7
 };
 
 // The elementwise tail applied to each output value v before the store, with
@@ -185,18 +191,22 @@ __host__ __device__ constexpr bool umma_tmem_a(int n, int mode) {
 template <int N, int MODE>
 struct UmmaCfg {
   static constexpr bool TMEM_A = umma_tmem_a(N, MODE);
-  static constexpr int A_BYTES = 128 * 128;  // 128 rows x 32 fp32
-  static constexpr int B_BYTES = N * 128;    // N rows x 32 fp32
-  // A stage holds A (and A_lo unless it lives in TMEM), B and B_lo.
-  static constexpr int STAGE_BYTES = (TMEM_A ? 1 : 2) * A_BYTES + 2 * B_BYTES;
-  static constexpr int STAGES = TMEM_A ? (N <= 32 ? 6 : 4) : (N <= 64 ? 4 : 3);
+  static constexpr bool HALO = MODE == MODE_CONV3H;
+  static constexpr int A_BYTES = (HALO ? 160 : 128) * 128;  // rows x 32 fp32
+  static constexpr int B_BYTES = N * 128;                   // N rows x 32 fp32, per tap
+  static constexpr int B_TAPS = HALO ? 3 : 1;               // taps per stage
+  // A stage holds A (and A_lo unless it lives in TMEM), then B and B_lo of
+  // each of its taps.
+  static constexpr int STAGE_BYTES = (TMEM_A ? 1 : 2) * A_BYTES + 2 * B_TAPS * B_BYTES;
+  static constexpr int STAGES =
+      HALO ? (N <= 32 ? 3 : 2) : (TMEM_A ? (N <= 32 ? 6 : 4) : (N <= 64 ? 4 : 3));
   // The split stage: four warps, one per TMEM lane quarter, or for the 3x3 and
   // 4x4 convolutions (TMEM_A) eight, two per quarter, each taking 16 of the
   // k-block's 32 columns. Those convs split every input pixel once per tap,
   // and the quarters whose warps share a sub-partition with the producer or
   // the MMA issuer set the pace; halving their work per warp lets the MMA
   // issue set it instead.
-  static constexpr int SPLIT = TMEM_A && (MODE == MODE_CONV3 || MODE == MODE_CONV4) ? 8 : 4;
+  static constexpr int SPLIT = (TMEM_A && (MODE == MODE_CONV3 || MODE == MODE_CONV4)) || HALO ? 8 : 4;
   // An accumulator set is two N-column fp32 regions: the hi*hi products and
   // the two cross terms, summed once in the epilogue. Each set has its own
   // four epilogue warps, so while the next tile accumulates the epilogue
@@ -215,7 +225,7 @@ struct UmmaCfg {
   static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
   static_assert(!TMEM_A || A_COL0 + STAGES * 32 <= 512, "TMEM holds the accumulators and the A_lo slots");
   static_assert(2 * N <= 256, "one instruction covers B_hi and B_lo");
-  static_assert(SPLIT == 4 || TMEM_A, "eight split warps only write A_lo into TMEM");
+  static_assert(SPLIT == 4 || TMEM_A || HALO, "eight split warps: A_lo in TMEM, or the 160-row halo box");
 };
 
 enum : int {
@@ -252,8 +262,10 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
   using C = UmmaCfg<N, MODE>;
   constexpr bool TMEM_A = C::TMEM_A;
   using namespace sm100;
-  constexpr int TAPS = MODE == MODE_CONV3 ? 9 : (MODE == MODE_CONV4 ? 16 : 1);
-  constexpr bool SPATIAL = MODE == MODE_CONV3 || MODE == MODE_CONV4;  // 8x16-pixel output tiles
+  constexpr bool HALO = C::HALO;
+  // Stages per tile and channel block: taps, or column shifts (HALO).
+  constexpr int TAPS = HALO ? 3 : (MODE == MODE_CONV3 ? 9 : (MODE == MODE_CONV4 ? 16 : 1));
+  constexpr bool SPATIAL = MODE == MODE_CONV3 || MODE == MODE_CONV4 || HALO;  // 8x16-pixel output tiles
   constexpr bool GATE = MODE == MODE_GATE || MODE == MODE_GATE_GRID || MODE == MODE_GATE_SP;
   constexpr bool PER_GROUP = MODE == MODE_GATE_GRID || MODE == MODE_GATE_SP;  // one box per group
   extern __shared__ uint8_t smem_raw[];
@@ -353,11 +365,15 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
           uint8_t* st = base + s * C::STAGE_BYTES;
           int a_bytes = C::A_BYTES;
           if (PER_GROUP) a_bytes = 4096 * min(4, p.groups - a0);
-          mbar_arrive_expect_tx(&full[s], a_bytes + 2 * C::B_BYTES);
+          mbar_arrive_expect_tx(&full[s], a_bytes + 2 * C::B_TAPS * C::B_BYTES);
           if (MODE == MODE_CONV1 || MODE == MODE_CONVT) {
             tma_load_2d(st, &tmA, &full[s], cb * 32, a0);
           } else if (MODE == MODE_CONV3) {
             tma_load_3d(st, &tmA, &full[s], cb * 32, a0 + kx - 1, a1 + ky - 1);
+          } else if (HALO) {
+            // Column shift kx: the tile's 8 rows and the halo row on either
+            // side, 16 x 10 pixels from (x0 + kx - 1, y0 - 1).
+            tma_load_3d(st, &tmA, &full[s], cb * 32, a0 + kx - 1, a1 - 1);
           } else if (MODE == MODE_CONV4) {
             // Output pixel (oy, ox) reads input (2oy + ky - pt, 2ox + kx - pl):
             // the tensor map steps 2 input pixels per box element.
@@ -382,10 +398,20 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
                 }
               }
           }
-          const int kcol = tap * p.c_in + cb * 32;
           uint8_t* sbw = st + (TMEM_A ? 1 : 2) * C::A_BYTES;  // B follows A (and A_lo unless it lives in TMEM)
-          tma_load_2d(sbw, &tmB, &full[s], kcol, n0);
-          tma_load_2d(sbw + C::B_BYTES, &tmBlo, &full[s], kcol, n0);
+          if (HALO) {
+            // The weights of taps (0, kx), (1, kx), (2, kx), hi then lo each.
+#pragma unroll
+            for (int r = 0; r < 3; ++r) {
+              const int kcol = (r * 3 + kx) * p.c_in + cb * 32;
+              tma_load_2d(sbw + r * 2 * C::B_BYTES, &tmB, &full[s], kcol, n0);
+              tma_load_2d(sbw + r * 2 * C::B_BYTES + C::B_BYTES, &tmBlo, &full[s], kcol, n0);
+            }
+          } else {
+            const int kcol = tap * p.c_in + cb * 32;
+            tma_load_2d(sbw, &tmB, &full[s], kcol, n0);
+            tma_load_2d(sbw + C::B_BYTES, &tmBlo, &full[s], kcol, n0);
+          }
         }
       }
     }
@@ -433,23 +459,28 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
           const uint64_t da0 = GATE ? desc_mnmajor_sw128_32b(a, 4096) : desc_kmajor_sw128(a);
           const uint64_t dalo0 = GATE ? desc_mnmajor_sw128_32b(alo, 4096) : desc_kmajor_sw128(alo);
           const uint64_t db0 = desc_kmajor_sw128(b);
+          // HALO: tap ky of the stage reads the box from row 16 ky (2 KB, 128
+          // in the address field) and its weights from the ky-th B pair.
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            // GATE: MN-major, k-step k covers K rows 8k..8k+7 of each 4 KB
-            // group block; otherwise K-major, 8 fp32 = 32 bytes per k-step.
-            const uint64_t da = da0 + kStepK * k, db = db0 + 2u * k;
-            // The running sum of the hi*hi products takes one accumulator
-            // update per k-step; the cross terms, 2^-10 of its size or less,
-            // go to their own region, so the accumulator's rounding at each
-            // update is paid once per k-step at full magnitude.
-            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-            mma_tf32(d, da, db, idesc2, accum);
-            if (TMEM_A) {
-              mma_tf32_ts(dx, slot + 8 * k, db, idesc, 1u);
-            } else {
-              mma_tf32(dx, dalo0 + kStepK * k, db, idesc, 1u);
+          for (int ky = 0; ky < C::B_TAPS; ++ky)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              // GATE: MN-major, k-step k covers K rows 8k..8k+7 of each 4 KB
+              // group block; otherwise K-major, 8 fp32 = 32 bytes per k-step.
+              const uint32_t ra = 128u * ky, rb = uint32_t(2 * C::B_BYTES / 16) * ky;
+              const uint64_t da = da0 + ra + kStepK * k, db = db0 + rb + 2u * k;
+              // The running sum of the hi*hi products takes one accumulator
+              // update per k-step; the cross terms, 2^-10 of its size or less,
+              // go to their own region, so the accumulator's rounding at each
+              // update is paid once per k-step at full magnitude.
+              const uint32_t accum = (kb > 0 || ky > 0 || k > 0) ? 1u : 0u;
+              mma_tf32(d, da, db, idesc2, accum);
+              if (TMEM_A) {
+                mma_tf32_ts(dx, slot + 8 * k, db, idesc, 1u);
+              } else {
+                mma_tf32(dx, dalo0 + ra + kStepK * k, db, idesc, 1u);
+              }
             }
-          }
           mma_commit(&empty[s]);
           if (++s == C::STAGES) s = 0, ph ^= 1;
         }
@@ -459,7 +490,7 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
     }
   } else if (warp < C::EPI_WARP0) {
     // ------------------------------------------------------------ split
-    const int tid = threadIdx.x - 64;  // 0..127 (the SPLIT = 4 instances)
+    const int tid = threadIdx.x - 64;  // 0 .. 32 * SPLIT - 1
     // TMEM_A with SPLIT = 8: warps 2-5 take columns 0-15 of each row, warps
     // 6-9 columns 16-31; otherwise one warp takes all 32.
     constexpr int NCH = 32 / 4 / (C::SPLIT / 4);  // float4 chunks of a row per thread
@@ -517,7 +548,7 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
         if (p.ln_stats) {
           if (TMEM_A) {
             ln = ln_row(rq, lm, lr);
-          } else if (!GATE) {
+          } else if (!GATE && !HALO) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) lns[i] = ln_row((tid >> 3) + 16 * i, lms[i], lrs[i]);
           }
@@ -567,10 +598,12 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
         // every shared-memory access free of bank conflicts.
         float4* a = reinterpret_cast<float4*>(base + s * C::STAGE_BYTES) + tid;
         float4* alo = reinterpret_cast<float4*>(base + s * C::STAGE_BYTES + C::A_BYTES) + tid;
+        // 128 split threads over a 128-row tile, or (HALO) 256 over the
+        // 160-row box. Only the former normalises on load.
 #pragma unroll
-        for (int i = 0; i < 8 * 128; i += 128) {
+        for (int i = 0; i < C::A_BYTES / 16; i += 32 * C::SPLIT) {
           float4 v = a[i], l;
-          if (!GATE && p.ln_stats && lns[i >> 7]) {
+          if (!GATE && !HALO && p.ln_stats && lns[i >> 7]) {
             // float4 (tid + i) of the swizzled tile: row f / 8, chunk (f % 8) ^ (row % 8).
             const int f = tid + i, r = f >> 3, ch = cb * 32 + (((f & 7) ^ (r & 7)) << 2);
             v = ln_apply4(v, lms[i >> 7], lrs[i >> 7], ch);
