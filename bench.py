@@ -3,7 +3,8 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl native|reference]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...   (N > 1)
 
-Workload (BASELINE metric, config: MAXIM-3S, 1280x853):
+Workload (BASELINE metric, config: MAXIM-3S, 1280x853; at N=1 also the
+metric's 2048x2048 latency, BASELINE config 4, as `latency_2048`):
   * MAXIM-3S with seeded random-init He-normal weights (no checkpoint offline);
   * each GPU runs B distinct synthetic 1280x853 images (U[0,1), padded by the
     reference pipeline to 1280x896) per step; a step is one forward pass of
@@ -277,6 +278,58 @@ def run_timeline(args):
     return 0
 
 
+def latency_2048(mx, local, reps=3, warmup=2):
+    """BASELINE config 4, the metric's latency: MAXIM-3S with seed-3 weights
+    on one 2048x2048 dark image (U[0,0.25) plus noise of std 0.02 sqrt(v),
+    synth.image_dark), batch 1. `ms`: device time of one pass with the image
+    already in HBM (CUDA events on the executor's stream, median of `reps`);
+    `e2e_ms`: the same through mx_gpu_run from pinned host memory."""
+    import torch
+    synth = importlib.import_module("maxim-rs_b200.synth")
+    d = os.path.join(tempfile.gettempdir(), "maxim_b200_bench")
+    os.makedirs(d, exist_ok=True)
+    path = os.path.join(d, "S-3_seed3.safetensors")
+    synth.checkpoint(path, "S-3", 3)
+    img = synth.image_dark(synth.input_rng(3), 2048, 2048)
+    padded, _ = mx.preprocess(img, 64)
+    plan = mx.Plan(mx.Weights(path), padded.shape[1], padded.shape[2])
+    g = mx.Gpu(plan, device=local)
+    arena_mib = g.stats()["arena_bytes"] / 2**20
+    x = torch.from_numpy(np.ascontiguousarray(padded)).cuda(local)
+    y = torch.empty(g.out_shape, dtype=torch.float32, device="cuda:%d" % local)
+    stream = torch.cuda.ExternalStream(g.stream(), device=torch.device("cuda", local))
+
+    def one():
+        g.upload_input_device(x.data_ptr())
+        g.enqueue()
+        g.download_output_device(y.data_ptr())
+
+    for _ in range(warmup):
+        one()
+    g.sync()
+    dev = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        one()
+        e1.record(stream)
+        e1.synchronize()
+        dev.append(e0.elapsed_time(e1))
+    g.sync()
+    pin_in = torch.from_numpy(np.ascontiguousarray(padded)).pin_memory()
+    pin_out = torch.empty(g.out_shape, dtype=torch.float32).pin_memory()
+    host = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        g.run(pin_in.numpy(), pin_out.numpy())
+        host.append((time.perf_counter() - t0) * 1e3)
+    finite = bool(np.isfinite(pin_out.numpy()).all())
+    g.close()
+    return {"ms": statistics.median(dev), "e2e_ms": statistics.median(host), "reps": reps,
+            "config": "MAXIM-3S 2048x2048 (BASELINE config 4), seed-3 weights, one dark image, batch 1",
+            "arena_mib": round(arena_mib, 1), "output_finite": finite}
+
+
 def run_native(args):
     import torch
     import torch.distributed as dist
@@ -396,6 +449,10 @@ def run_native(args):
                     "d2h_bytes_per_step": int(B * out_dev[0].numel() * 4)},
             "gpu_launches": int(stats["kernels"] * args.steps * B),
             "roofline": roof, "clocks": clk.summary()}
+    if rank == 0 and world == 1:
+        with Clocks(uuid) as clk4:
+            line["latency_2048"] = latency_2048(mx, local)
+        line["latency_2048"]["clocks"] = clk4.summary()
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = len(os.sched_getaffinity(0))
         v, desc, _ = cpu_sample(threads)
