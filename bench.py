@@ -4,7 +4,8 @@
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...   (N > 1)
 
 Workload (BASELINE metric, config: MAXIM-3S, 1280x853; at N=1 also the
-metric's 2048x2048 latency, BASELINE config 4, as `latency_2048`):
+metric's 2048x2048 latency, BASELINE config 4, as `latency_2048`, and the
+MAXIM-2S throughput of config 5 as `config5_s2`):
   * MAXIM-3S with seeded random-init He-normal weights (no checkpoint offline);
   * each GPU runs B distinct synthetic 1280x853 images (U[0,1), padded by the
     reference pipeline to 1280x896) per step; a step is one forward pass of
@@ -330,6 +331,46 @@ def latency_2048(mx, local, reps=3, warmup=2):
             "arena_mib": round(arena_mib, 1), "output_finite": finite}
 
 
+def config5_s2(mx, local, n_img=4, reps=3, warmup=2):
+    """BASELINE config 5 on one GPU: MAXIM-2S with seed-4 weights over 1280x853
+    U[0,1) images (padded to 1280x896), in HBM, one pass per image; Mpx/s of
+    output pixels by CUDA events on the executor's stream (the scaling over
+    GPUs is the headline's, which runs the S-3 target)."""
+    import torch
+    synth = importlib.import_module("maxim-rs_b200.synth")
+    d = os.path.join(tempfile.gettempdir(), "maxim_b200_bench")
+    os.makedirs(d, exist_ok=True)
+    path = os.path.join(d, "S-2_seed4.safetensors")
+    synth.checkpoint(path, "S-2", 4)
+    rng = synth.input_rng(4)
+    imgs = [mx.preprocess(synth.image_uniform(rng, IMG_H, IMG_W), 64)[0] for _ in range(n_img)]
+    plan = mx.Plan(mx.Weights(path), PAD_H, PAD_W)
+    g = mx.Gpu(plan, device=local)
+    x = torch.from_numpy(np.stack(imgs)).cuda(local)
+    y = torch.empty((n_img,) + g.out_shape, dtype=torch.float32, device="cuda:%d" % local)
+    stream = torch.cuda.ExternalStream(g.stream(), device=torch.device("cuda", local))
+
+    def step():
+        for b in range(n_img):
+            g.upload_input_device(x[b].data_ptr())
+            g.enqueue()
+            g.download_output_device(y[b].data_ptr())
+
+    for _ in range(warmup):
+        step()
+    g.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * n_img)
+    g.close()
+    return {"value": OUT_MPX / (ms / 1000.0), "unit": "Mpx/s", "ms_per_image": ms,
+            "config": "MAXIM-2S 1280x853 (BASELINE config 5, one GPU), seed-4 weights, U[0,1) images"}
+
+
 def run_native(args):
     import torch
     import torch.distributed as dist
@@ -453,6 +494,9 @@ def run_native(args):
         with Clocks(uuid) as clk4:
             line["latency_2048"] = latency_2048(mx, local)
         line["latency_2048"]["clocks"] = clk4.summary()
+        with Clocks(uuid) as clk5:
+            line["config5_s2"] = config5_s2(mx, local)
+        line["config5_s2"]["clocks"] = clk5.summary()
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = len(os.sched_getaffinity(0))
         v, desc, _ = cpu_sample(threads)
