@@ -200,13 +200,14 @@ struct UmmaCfg {
   static constexpr int STAGE_BYTES = (TMEM_A ? 1 : 2) * A_BYTES + 2 * B_TAPS * B_BYTES;
   static constexpr int STAGES =
       HALO ? (N <= 32 ? 3 : 2) : (TMEM_A ? (N <= 32 ? 6 : 4) : (N <= 64 ? 4 : 3));
-  // The split stage: four warps, one per TMEM lane quarter, or for the 3x3 and
-  // 4x4 convolutions (TMEM_A) eight, two per quarter, each taking 16 of the
-  // k-block's 32 columns. Those convs split every input pixel once per tap,
-  // and the quarters whose warps share a sub-partition with the producer or
-  // the MMA issuer set the pace; halving their work per warp lets the MMA
-  // issue set it instead.
-  static constexpr int SPLIT = (TMEM_A && (MODE == MODE_CONV3 || MODE == MODE_CONV4)) || HALO ? 8 : 4;
+  // The split stage: four warps for the 1x1 convs and the gating matmuls,
+  // eight for the 3x3 and 4x4 convs. With A_lo in TMEM each warp writes its
+  // TMEM lane quarter, and with eight, two per quarter take 16 of the
+  // k-block's 32 columns each: the quarters whose warps share a
+  // sub-partition with the producer or the MMA issuer set the pace unless
+  // their work per warp is halved. With A_lo in shared memory (the halo box,
+  // the 128-column 3x3) the eight warps share the tile's float4s.
+  static constexpr int SPLIT = MODE == MODE_CONV3 || MODE == MODE_CONV4 || HALO ? 8 : 4;
   // An accumulator set is two N-column fp32 regions: the hi*hi products and
   // the two cross terms, summed once in the epilogue. Each set has its own
   // four epilogue warps, so while the next tile accumulates the epilogue
@@ -225,7 +226,6 @@ struct UmmaCfg {
   static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
   static_assert(!TMEM_A || A_COL0 + STAGES * 32 <= 512, "TMEM holds the accumulators and the A_lo slots");
   static_assert(2 * N <= 256, "one instruction covers B_hi and B_lo");
-  static_assert(SPLIT == 4 || TMEM_A || HALO, "eight split warps: A_lo in TMEM, or the 160-row halo box");
 };
 
 enum : int {
@@ -598,12 +598,12 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
         // every shared-memory access free of bank conflicts.
         float4* a = reinterpret_cast<float4*>(base + s * C::STAGE_BYTES) + tid;
         float4* alo = reinterpret_cast<float4*>(base + s * C::STAGE_BYTES + C::A_BYTES) + tid;
-        // 128 split threads over a 128-row tile, or (HALO) 256 over the
-        // 160-row box. Only the former normalises on load.
+        // 32 * SPLIT split threads over the tile (HALO: the 160-row box).
+        // Only the four-warp 1x1 instances normalise on load.
 #pragma unroll
         for (int i = 0; i < C::A_BYTES / 16; i += 32 * C::SPLIT) {
           float4 v = a[i], l;
-          if (!GATE && !HALO && p.ln_stats && lns[i >> 7]) {
+          if (!GATE && !HALO && C::SPLIT == 4 && p.ln_stats && lns[i >> 7]) {
             // float4 (tid + i) of the swizzled tile: row f / 8, chunk (f % 8) ^ (row % 8).
             const int f = tid + i, r = f >> 3, ch = cb * 32 + (((f & 7) ^ (r & 7)) << 2);
             v = ln_apply4(v, lms[i >> 7], lrs[i >> 7], ch);
