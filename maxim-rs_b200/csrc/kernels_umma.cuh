@@ -525,10 +525,42 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
       v.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, m), rs), w.w), b.w);
       return v;
     };
+    // In the 1x1 instances a thread's rows are the same for every k-block
+    // of a tile (TMEM_A: row rq; otherwise rows tid / 8 + 16 j), so their
+    // statistics are loaded once per tile, and a whole tile ahead: loaded
+    // just before the A wait they would still be in flight when the tile
+    // arrives (an L2 round trip, often to the far die, is longer than the
+    // gap between two tiles). Bit j of ln_next: row j is inside the image.
+    constexpr bool LN_AHEAD = MODE == MODE_CONV1;
+    constexpr int LN_ROWS = TMEM_A ? 1 : 8;
+    float2 st_next[LN_ROWS], st_cur[LN_ROWS];
+    uint32_t ln_next = 0, ln_cur = 0;
+    auto fetch_stats = [&](int tn) {
+      ln_next = 0;
+      if (tn < p.tiles) {
+        int b0, b1, m0;
+        decode(tn, b0, b1, m0);
+#pragma unroll
+        for (int j = 0; j < LN_ROWS; ++j) {
+          const int pix = b0 + (TMEM_A ? (warp & 3) * 32 + lane : (tid >> 3) + 16 * j);
+          if (pix < p.in_w) {
+            st_next[j] = p.ln_stats[pix];
+            ln_next |= 1u << j;
+          }
+        }
+      }
+    };
+    if (LN_AHEAD && p.ln_stats) fetch_stats(blockIdx.x);
     for (int t = blockIdx.x; t < p.tiles && !*vabort; t += gridDim.x) {
       bool ok = true;
       decode(t, a0, a1, n0);
       cb = 0, ky = 0, kx = 0;
+      if (LN_AHEAD && p.ln_stats) {
+#pragma unroll
+        for (int j = 0; j < LN_ROWS; ++j) st_cur[j] = st_next[j];
+        ln_cur = ln_next;
+        fetch_stats(t + gridDim.x);
+      }
       for (int kb = 0; kb < KB; ++kb, ++it) {
         if (kb > 0 && ++cb == p.kb_per_tap) {
           cb = 0;
@@ -536,17 +568,23 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
         }
         const int s = it % C::STAGES;
         const uint32_t ph = (it / C::STAGES) & 1;
-        // LayerNorm on load: the statistics this k-block needs depend only
-        // on the tile and the tap, so their loads go out before the wait for
-        // the A tile and overlap it. TMEM_A: one row per thread; otherwise
-        // the 8 rows of this thread's float4s (rows tid / 8 + 16 i).
+        // LayerNorm on load: the statistics of this thread's rows (TMEM_A:
+        // one row; otherwise the 8 rows tid / 8 + 16 i of its float4s). The
+        // 1x1 instances have them from a tile ahead; elsewhere they depend on
+        // the tap too and are loaded here, before the wait for the A tile.
         const int q = warp & 3, rq = q * 32 + lane;
         float lm = 0.0f, lr = 0.0f;
         bool ln = false;
         float lms[8], lrs[8];
         bool lns[8];
         if (p.ln_stats) {
-          if (TMEM_A) {
+          if (LN_AHEAD && TMEM_A) {
+            ln = ln_cur & 1u, lm = st_cur[0].x, lr = st_cur[0].y;
+          } else if (LN_AHEAD) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              lns[i] = (ln_cur >> i) & 1u, lms[i] = st_cur[i % LN_ROWS].x, lrs[i] = st_cur[i % LN_ROWS].y;
+          } else if (TMEM_A) {
             ln = ln_row(rq, lm, lr);
           } else if (!GATE && !HALO) {
 #pragma unroll
@@ -567,19 +605,36 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
           const int r = rq;
           uint8_t* arow = base + s * C::STAGE_BYTES + r * 128;
           float lo[4 * NCH];
+          if (p.ln_stats) {
+            // Branch-free over the chunks (a row outside the image keeps its
+            // zeros by selection), so the loads of all chunks and of the
+            // scale and bias can be in flight together.
 #pragma unroll
-          for (int c = 0; c < NCH; ++c) {
-            const int cc = half * NCH + c;  // float4 chunk of the row
-            float4* p4 = reinterpret_cast<float4*>(arow + ((cc ^ (r & 7)) << 4));
-            float4 v = *p4;
-            if (ln) {
-              v = ln_apply4(v, lm, lr, cb * 32 + 4 * cc);
+            for (int c = 0; c < NCH; ++c) {
+              const int cc = half * NCH + c;
+              float4* p4 = reinterpret_cast<float4*>(arow + ((cc ^ (r & 7)) << 4));
+              float4 v = *p4;
+              const float4 u = ln_apply4(v, lm, lr, cb * 32 + 4 * cc);
+              v.x = ln ? u.x : v.x;
+              v.y = ln ? u.y : v.y;
+              v.z = ln ? u.z : v.z;
+              v.w = ln ? u.w : v.w;
               *p4 = v;
+              lo[4 * c] = tf32_residual(v.x);
+              lo[4 * c + 1] = tf32_residual(v.y);
+              lo[4 * c + 2] = tf32_residual(v.z);
+              lo[4 * c + 3] = tf32_residual(v.w);
             }
-            lo[4 * c] = tf32_residual(v.x);
-            lo[4 * c + 1] = tf32_residual(v.y);
-            lo[4 * c + 2] = tf32_residual(v.z);
-            lo[4 * c + 3] = tf32_residual(v.w);
+          } else {
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+              const int cc = half * NCH + c;  // float4 chunk of the row
+              const float4 v = *reinterpret_cast<const float4*>(arow + ((cc ^ (r & 7)) << 4));
+              lo[4 * c] = tf32_residual(v.x);
+              lo[4 * c + 1] = tf32_residual(v.y);
+              lo[4 * c + 2] = tf32_residual(v.z);
+              lo[4 * c + 3] = tf32_residual(v.w);
+            }
           }
           const uint32_t slot = tmem + (uint32_t(q * 32) << 16) + C::A_COL0 + s * 32;
           if (NCH == 8) {
@@ -600,13 +655,20 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
         float4* alo = reinterpret_cast<float4*>(base + s * C::STAGE_BYTES + C::A_BYTES) + tid;
         // 32 * SPLIT split threads over the tile (HALO: the 160-row box).
         // Only the four-warp 1x1 instances normalise on load.
+        // Branch-free over the float4s, as in the TMEM_A case.
+        const bool norm = !GATE && !HALO && C::SPLIT == 4 && p.ln_stats;
 #pragma unroll
         for (int i = 0; i < C::A_BYTES / 16; i += 32 * C::SPLIT) {
           float4 v = a[i], l;
-          if (!GATE && !HALO && C::SPLIT == 4 && p.ln_stats && lns[i >> 7]) {
+          if (norm) {
             // float4 (tid + i) of the swizzled tile: row f / 8, chunk (f % 8) ^ (row % 8).
             const int f = tid + i, r = f >> 3, ch = cb * 32 + (((f & 7) ^ (r & 7)) << 2);
-            v = ln_apply4(v, lms[i >> 7], lrs[i >> 7], ch);
+            const bool on = lns[i >> 7];
+            const float4 u = ln_apply4(v, lms[i >> 7], lrs[i >> 7], ch);
+            v.x = on ? u.x : v.x;
+            v.y = on ? u.y : v.y;
+            v.z = on ? u.z : v.z;
+            v.w = on ? u.w : v.w;
             a[i] = v;
           }
           l.x = tf32_residual(v.x);
