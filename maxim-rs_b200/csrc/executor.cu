@@ -1051,8 +1051,22 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
       int64_t ty_j0 = int64_t(g.pool.put(ty.j0)), ty_w0 = int64_t(g.pool.put(ty.w0)),
               ty_c = int64_t(g.pool.put(ty.cnt)), ty_w = int64_t(g.pool.put(ty.w)),
               ty_s = int64_t(g.pool.put(ty.wsum)), ty_r = int64_t(g.pool.put(ty.wrcp));
-      st.kernels = 2;
-      st.run = [G, L, op, tx_j0, tx_w0, tx_c, tx_w, tx_s, tx_r, ty_j0, ty_w0, ty_c, ty_w, ty_s,
+      // Upsampling whose every tile of kRzTY output rows reads at most kRzRows
+      // input rows runs both passes in one launch (resize_hv4_kernel).
+      const int c4 = o.c / 4;
+      bool hv = o.win <= o.wout && o.hin <= o.hout && o.c % 4 == 0 && c4 > 0 && (c4 & (c4 - 1)) == 0 && c4 <= 256;
+      for (int y0 = 0; hv && y0 < o.hout; y0 += kRzTY) {
+        int r_lo = 1 << 30, r_hi = -1;
+        for (int yo = y0; yo < std::min(y0 + kRzTY, o.hout); ++yo) {
+          r_lo = std::min(r_lo, ty.j0[size_t(yo)]);
+          r_hi = std::max(r_hi, ty.j0[size_t(yo)] + ty.cnt[size_t(yo)] - 1);
+        }
+        hv = r_hi - r_lo + 1 <= kRzRows;
+      }
+      for (size_t i = 0; hv && i < ty.cnt.size(); ++i) hv = ty.cnt[i] <= kRzTaps;
+      for (size_t i = 0; hv && i < tx.cnt.size(); ++i) hv = tx.cnt[i] <= kRzTaps;
+      st.kernels = hv ? 1 : 2;
+      st.run = [G, L, op, hv, tx_j0, tx_w0, tx_c, tx_w, tx_s, tx_r, ty_j0, ty_w0, ty_c, ty_w, ty_s,
                 ty_r](cudaStream_t s) {
         auto I = [G](int64_t off) { return reinterpret_cast<const int*>(G->pool.dev + off); };
         auto F = [G](int64_t off) { return reinterpret_cast<const float*>(G->pool.dev + off); };
@@ -1064,6 +1078,13 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
           TapTable4 TY{I(ty_j0), I(ty_w0), I(ty_c), F(ty_w), F(ty_s), F(ty_r)};
           int lg4 = 0;
           while ((1 << lg4) < c4) ++lg4;
+          if (hv) {
+            const int cols = (kRzTile / 4) >> lg4;
+            const dim3 g((unsigned(op.wout) + cols - 1) / cols, (unsigned(op.hout) + kRzTY - 1) / kRzTY);
+            resize_hv4_kernel<<<g, kRzTile / 4, 0, s>>>(lg4, op.win, op.wout, op.hout, TX, TY, x.ptr, int(x.stride),
+                                                        d.ptr, int(d.stride));
+            return;
+          }
           const int row = op.wout * c4;
           const dim3 g1(unsigned(blocks_for(row, TPB)), unsigned(op.hin)), g2(unsigned(blocks_for(row, TPB)),
                                                                               unsigned(op.hout));

@@ -281,5 +281,72 @@ __global__ void __launch_bounds__(256, 8) resize_v4_kernel(int lg4, int wout, Ta
       tap_norm(acc, __ldg(t.wsum + yo), __ldg(t.wrcp + yo));
 }
 
+// Both passes in one launch, for upsampling (at most kRzTaps taps a side).
+// A CTA makes output rows [y0, y0 + kRzTY) of a strip of output columns
+// holding kRzTile floats a row (all channels). It first computes, into shared
+// memory, the horizontal pass of every input row those output rows read
+// (exactly what resize_h4_kernel writes to the intermediate), then the
+// vertical pass from there. Values and summation order are those of the two
+// kernels above, so the result is bit for bit theirs; the intermediate never
+// goes through DRAM. The host uses it only where every tile needs at most
+// kRzRows input rows; the kernel clamps to that bound all the same.
+constexpr int kRzTY = 16, kRzRows = 11, kRzTile = 1024, kRzTaps = 3;
+__global__ void __launch_bounds__(256) resize_hv4_kernel(int lg4, int win, int wout, int hout, TapTable4 tx,
+                                                         TapTable4 ty, const float* __restrict__ src, int ss,
+                                                         float* __restrict__ dst, int sd) {
+  __shared__ float4 rows[kRzRows][kRzTile / 4];
+  const int f = threadIdx.x;  // float4 of a strip row: column f >> lg4, channels 4 (f & (c4 - 1))
+  const int xo = blockIdx.x * ((kRzTile / 4) >> lg4) + (f >> lg4), c = (f & ((1 << lg4) - 1)) * 4;
+  const bool xin = xo < wout;
+  const int y0 = blockIdx.y * kRzTY, yend = min(y0 + kRzTY, hout);
+  int r_lo = 1 << 30, r_hi = -1;
+  for (int yo = y0; yo < yend; ++yo) {
+    const int j = __ldg(ty.j0 + yo);
+    r_lo = min(r_lo, j);
+    r_hi = max(r_hi, j + __ldg(ty.cnt + yo) - 1);
+  }
+  const int nrows = min(r_hi - r_lo + 1, kRzRows);
+  if (xin) {
+    // Four input rows at a time, all their taps' loads issued before any is
+    // used (the loads, not the arithmetic, are what a thread waits on).
+    const int j0 = __ldg(tx.j0 + xo), w0 = __ldg(tx.w0 + xo), n = min(__ldg(tx.cnt + xo), kRzTaps);
+    const float sm = __ldg(tx.wsum + xo), rc = __ldg(tx.wrcp + xo);
+    float w[kRzTaps];
+#pragma unroll
+    for (int k = 0; k < kRzTaps; ++k) w[k] = k < n ? __ldg(tx.w + w0 + k) : 0.0f;
+    for (int r0 = 0; r0 < nrows; r0 += 4) {
+      float4 v[4][kRzTaps];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float* s = src + (size_t(r_lo + min(r0 + q, nrows - 1)) * win + j0) * ss + c;
+#pragma unroll
+        for (int k = 0; k < kRzTaps; ++k)
+          v[q][k] = k < n ? *reinterpret_cast<const float4*>(s + size_t(k) * ss) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (r0 + q >= nrows) break;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < kRzTaps; ++k)
+          if (k < n) tap_acc(acc, w[k], v[q][k]);
+        rows[r0 + q][f] = tap_norm(acc, sm, rc);
+      }
+    }
+  }
+  __syncthreads();
+  if (!xin) return;
+  for (int yo = y0; yo < yend; ++yo) {
+    const int j0 = __ldg(ty.j0 + yo) - r_lo, w0 = __ldg(ty.w0 + yo), n = __ldg(ty.cnt + yo);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < n; ++k) {
+      const int r = j0 + k;
+      if (r < nrows) tap_acc(acc, __ldg(ty.w + w0 + k), rows[r][f]);
+    }
+    *reinterpret_cast<float4*>(dst + (size_t(yo) * wout + xo) * sd + c) =
+        tap_norm(acc, __ldg(ty.wsum + yo), __ldg(ty.wrcp + yo));
+  }
+}
+
 }  // namespace
 }  // namespace mx
