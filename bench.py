@@ -7,7 +7,7 @@ Workload (BASELINE metric, config: MAXIM-3S, 1280x853; at N=1 also the
 metric's 2048x2048 latency, BASELINE config 4, as `latency_2048`, and the
 MAXIM-2S throughput of config 5 as `config5_s2`):
   * MAXIM-3S with seeded random-init He-normal weights (no checkpoint offline);
-  * each GPU runs B distinct synthetic 1280x853 images (U[0,1), padded by the
+  * each GPU runs B (default 1) distinct synthetic 1280x853 images (U[0,1), padded by the
     reference pipeline to 1280x896) per step; a step is one forward pass of
     the plan over each of them; images are independent, so ranks shard them
     with no collective (weak scaling: per-GPU work is fixed as N grows);
@@ -15,12 +15,14 @@ MAXIM-2S throughput of config 5 as `config5_s2`):
 `value`: inputs resident in HBM, timed with CUDA events on the executor's
 stream, max over ranks. `e2e`: the same through the C ABI's mx_gpu_run from
 pinned host memory (H2D of the image and D2H of the result inside the timed
-region). Each pass touches a 2012 MiB arena, far beyond the 126 MB L2, so no
-L2 flush is needed between passes.
+region). Each pass touches a 1.9 GB arena, far beyond the 126 MB L2, so no
+L2 flush is needed between passes. `value` is the whole job's (all ranks);
+`value_per_gpu` is value / n_gpus, the metric's per-B200 figure.
 
 `--impl reference` times the reference's CPU algorithm on this box's host cores
 (the C++ restatement of its exec_cpu.rs: the Rust original cannot be built
-offline) on a bounded sample of the same workload.
+offline) on whole images of the same workload, through the oracle library
+alone (the GPU product library is never mapped into that process).
 """
 import argparse
 import importlib
@@ -126,83 +128,126 @@ def job_mpx_per_s(images_per_rank, world, seconds):
     return images_per_rank * world * OUT_MPX / seconds
 
 
-def make_images(n, rank, world):
-    """This rank's share of one seeded image stream (see shard)."""
+def make_images(n, rank, world, pre=None):
+    """This rank's share of one seeded image stream (see shard). `pre` pads an
+    image as the reference pipeline does (default: the product library's)."""
     synth = importlib.import_module("maxim-rs_b200.synth")
-    mx = importlib.import_module("maxim-rs_b200")
+    if pre is None:
+        pre = importlib.import_module("maxim-rs_b200").preprocess
     rng = synth.input_rng(IN_SEED)
     want = set(shard(n, rank, world))
     out = []
     for i in range(max(want) + 1):
         img = synth.image_uniform(rng, IMG_H, IMG_W)
         if i in want:
-            padded, _ = mx.preprocess(img, 64)
+            padded, _ = pre(img, 64)
             out.append(padded)
     return out
 
 
-def checkpoint_path():
+def bench_config(B):
+    """The workload both arms run (identical dict on both lines)."""
+    return {"workload": "MAXIM-3S 1280x853 (padded 1280x896), random-init He-normal weights seed %d, U[0,1) images"
+                        % W_SEED,
+            "images_per_gpu_per_step": B,
+            "parallelism": "replicas (images sharded round-robin over ranks, one arena per GPU, no collective)",
+            "l2": "no flush: each pass streams a 1.9 GB arena (L2 is 126 MB)"}
+
+
+def checkpoint_path(spec=None):
+    """The bench checkpoint (written once per box). `spec` is the parameter
+    inventory to generate from; by default the product library's builder's,
+    which is the same list the oracle library's own copy of the builder gives."""
     synth = importlib.import_module("maxim-rs_b200.synth")
     d = os.path.join(tempfile.gettempdir(), "maxim_b200_bench")
     os.makedirs(d, exist_ok=True)
     path = os.path.join(d, "%s_seed%d.safetensors" % (VARIANT, W_SEED))
-    synth.checkpoint(path, VARIANT, W_SEED)
+    synth.checkpoint(path, VARIANT, W_SEED, spec=spec)
     return path
 
 
-def cpu_sample(threads, budget_s=20.0):
-    """Time the CPU oracle on a bounded sample of the workload: MAXIM-3S on the
-    largest image size whose estimated time fits the budget (FLOPs per padded
-    pixel are size independent for this model), extrapolated to a 1280x853
-    image by padded pixels. Returns (Mpx/s, sample description)."""
-    mx = importlib.import_module("maxim-rs_b200")
-    synth = importlib.import_module("maxim-rs_b200.synth")
+def oracle_only():
+    """The CPU oracle library alone: built, loaded, and nothing of the GPU
+    product library mapped into this process."""
+    importlib.import_module("maxim-rs_b200.build").build()
     oracle = importlib.import_module("oracle")
-    work = importlib.import_module("maxim-rs_b200.work")
-    w = mx.Weights(checkpoint_path())
-    probe = mx.Plan(w, 128, 128)
-    img = synth.image_uniform(synth.input_rng(IN_SEED), 128, 128)
-    t = time.perf_counter()
-    oracle.output(probe, img, threads)
-    rate = (128 * 128) / (time.perf_counter() - t)  # padded px / s
-    h, wd = 128, 128
-    for (hh, ww) in [(448, 640), (320, 448), (256, 384), (192, 256)]:
-        if hh * ww / rate <= budget_s:
-            h, wd = hh, ww
-            break
-    plan = mx.Plan(w, h, wd)
-    img = synth.image_uniform(synth.input_rng(IN_SEED), h, wd)
+    oracle.lib()
+    return oracle
+
+
+def cpu_baseline(threads):
+    """The reference's CPU algorithm (oracle/exec_cpu.cpp, the C++ restatement
+    of src/exec_cpu.rs) timed on this box's host cores, through the oracle
+    library's own plan builder:
+      * value: one whole MAXIM-3S pass over the bench's first 1280x853 image
+        (padded 1280x896) with every host thread - measured, not scaled;
+      * one_thread: the same algorithm on one thread over a 256x256 image
+        (a bounded sample: a full-size image would take about ten minutes on
+        one core), as padded pixels per second; FLOPs per padded pixel do not
+        depend on the image size for this model (the gating matmuls contract
+        fixed 256- or 64-cell axes), so the Mpx/s it implies for a 1280x853
+        image is stated beside it."""
+    oracle = oracle_only()
+    synth = importlib.import_module("maxim-rs_b200.synth")
+    path = checkpoint_path(oracle.param_spec(VARIANT))
+    img = make_images(1, 0, 1, pre=oracle.preprocess)[0]
+    plan = oracle.HostPlan(path, PAD_H, PAD_W)
     t = time.perf_counter()
     oracle.output(plan, img, threads)
     dt = time.perf_counter() - t
-    per_image = dt * (PAD_H * PAD_W) / (h * wd)
-    gflop = sum(v[1] for v in work.census(plan).values()) / 1e9
-    desc = ("MAXIM-3S forward on one %dx%d image (%.0f GFLOP, %.1f s), extrapolated by padded pixels to a "
-            "1280x853 image (1280x896 padded)" % (wd, h, gflop, dt))
-    return OUT_MPX / per_image, desc, dt
+    del plan
+    small = oracle.HostPlan(path, 256, 256)
+    simg = synth.image_uniform(synth.input_rng(IN_SEED), 256, 256)
+    t = time.perf_counter()
+    oracle.output(small, simg, 1)
+    dt1 = time.perf_counter() - t
+    px_per_s = 256 * 256 / dt1
+    return {"value": OUT_MPX / dt, "unit": "Mpx/s", "cores": threads, "kind": "port",
+            "sample": "one whole MAXIM-3S pass over one 1280x853 image (padded 1280x896), %.1f s on %d threads; "
+                      "oracle/exec_cpu.cpp, the reference's exec_cpu.rs restated in C++" % (dt, threads),
+            "one_thread": {"padded_px_per_s": px_per_s, "seconds": dt1,
+                           "sample": "one MAXIM-3S pass over a 256x256 image on 1 thread",
+                           "implied_mpx_per_s_1280x853": OUT_MPX * px_per_s / (PAD_H * PAD_W)}}
 
 
 def run_reference(args):
+    """`--impl reference`: the reference's CPU algorithm on this box's host
+    cores, on the native arm's workload (same config, metric and unit).
+
+    Each step is B whole 1280x853 images (padded 1280x896) through the oracle
+    with every host thread, timed end to end: nothing is scaled. A full image
+    takes tens of seconds here, so the arm runs at most --ref-steps steps
+    (default 2) and one warm-up pass on a 128x128 image, and reports the steps
+    it actually ran. The process maps only the oracle library."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     threads = len(os.sched_getaffinity(0))
-    importlib.import_module("__graft_entry__").build()
-    times = []
-    desc = ""
-    for step in range(args.warmup + args.steps):
-        v, desc, dt = cpu_sample(threads)
-        if step >= args.warmup:
-            times.append(OUT_MPX / v)  # seconds per full image
-    value = args.steps / sum(times) if times else 0.0
-    line = {"metric": METRIC, "value": value, "unit": "Mpx/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * sum(times) / max(len(times), 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": "MAXIM-3S 1280x853 (padded 1280x896), random-init He-normal weights seed %d"
-                                   % W_SEED, "images_per_step": 1, "parallelism": "host threads"},
+    oracle = oracle_only()
+    synth = importlib.import_module("maxim-rs_b200.synth")
+    path = checkpoint_path(oracle.param_spec(VARIANT))
+    B = args.batch
+    imgs = make_images(B, 0, 1, pre=oracle.preprocess)
+    plan = oracle.HostPlan(path, PAD_H, PAD_W)
+    warm = oracle.HostPlan(path, 128, 128)
+    oracle.output(warm, synth.image_uniform(synth.input_rng(IN_SEED), 128, 128), threads)
+    del warm
+    steps = max(1, min(args.steps, args.ref_steps))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        for b in range(B):
+            oracle.output(plan, imgs[b], threads)
+    dt = time.perf_counter() - t0
+    value = steps * B * OUT_MPX / dt
+    line = {"metric": METRIC, "value": value, "unit": "Mpx/s", "n_gpus": args.gpus, "steps": steps,
+            "steps_requested": args.steps, "warmup": 1, "warmup_requested": args.warmup,
+            "ms_per_step": 1000.0 * dt / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "impl": "reference", "config": bench_config(B),
             "cpu_baseline": {"value": value, "unit": "Mpx/s", "cores": threads, "kind": "port",
-                             "sample": desc + "; the reference's exec_cpu.rs restated in C++ (oracle/exec_cpu.cpp)"},
+                             "sample": "%d step(s) of %d whole 1280x853 image(s) (padded 1280x896) each, %.1f s "
+                                       "in all, on %d threads; warm-up one 128x128 pass; oracle/exec_cpu.cpp, the "
+                                       "reference's exec_cpu.rs restated in C++ (the Rust original cannot be built "
+                                       "offline)" % (steps, B, dt, threads)},
             "e2e": {"value": value, "unit": "Mpx/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -267,14 +312,22 @@ def run_timeline(args):
     print("%s %dx%d (padded %dx%d): one pass %.2f ms, %d ops in %d steps (%d fused, %d permutations dropped), "
           "%d kernel launches" % (args.variant, args.width, args.height, padded.shape[2], padded.shape[1], tot,
                                   plan.n_ops, st["steps"], st["ops_fused"], st["perms_dropped"], st["kernels"]))
-    print("%-26s %5s %9s %6s %9s %9s" % ("step family", "steps", "ms", "share", "TFLOP/s", "GB/s"))
+    hbm, _, tf_sus, _ = peaks()
+    print("roofline per family: the slower of HBM (algorithmic bytes at %.0f GB/s) and the tensor pipe (3 TF32 "
+          "products per useful MAC at %.0f TFLOP/s, half the sustained bf16 figure)" % (hbm, tf_sus / 2))
+    print("%-26s %5s %9s %6s %9s %9s %6s %6s" % ("step family", "steps", "ms", "share", "TFLOP/s", "GB/s", "bound",
+                                                 "frac"))
     for k, (n, ms, f, b) in sorted(fam.items(), key=lambda kv: -kv[1][1]):
         ms_ = max(ms, 1e-9)
-        print("%-26s %5d %9.2f %5.1f%% %9.1f %9.0f" % (k, n, ms, 100 * ms / tot, f / ms_ / 1e9, b / ms_ / 1e6))
+        r = work.roofline(k, f, b, ms_ / 1e3, hbm, tf_sus / 2)
+        print("%-26s %5d %9.2f %5.1f%% %9.1f %9.0f %6s %6.2f" % (k, n, ms, 100 * ms / tot, f / ms_ / 1e9,
+                                                                 b / ms_ / 1e6, r["bound"], r["frac"]))
     print("top shapes:")
     for k, (n, ms, f, b) in sorted(shp.items(), key=lambda kv: -kv[1][1])[:24]:
         ms_ = max(ms, 1e-9)
-        print("  %8.2f ms %4dx  %-48s %7.1f TFLOP/s %6.0f GB/s" % (ms, n, k, f / ms_ / 1e9, b / ms_ / 1e6))
+        r = work.roofline(k, f, b, ms_ / 1e3, hbm, tf_sus / 2)
+        print("  %8.2f ms %4dx  %-48s %7.1f TFLOP/s %6.0f GB/s  %s %.2f" % (ms, n, k, f / ms_ / 1e9, b / ms_ / 1e6,
+                                                                          r["bound"], r["frac"]))
     gpu.close()
     return 0
 
@@ -371,6 +424,71 @@ def config5_s2(mx, local, n_img=4, reps=3, warmup=2):
             "config": "MAXIM-2S 1280x853 (BASELINE config 5, one GPU), seed-4 weights, U[0,1) images"}
 
 
+def config3_gmlp(mx, local, reps=5, warmup=3):
+    """BASELINE config 3, the isolated multi-axis gMLP block op: one residual
+    split-head multi-axis gMLP layer (the builder's own split_head_gmlp,
+    src/model.rs:576-603, as the "gMLP-64" plan) over an NHWC [1,512,512,64]
+    N(0,1) tensor, Dense weights N(0, 0.02), seed 2. `ms`: device time of one
+    pass with the tensor in HBM (CUDA events on the executor's stream, median
+    of `reps`); `e2e_ms`: the same through mx_gpu_run from pinned host memory.
+    The roofline: 39.5 GFLOP of useful products issued as 3 TF32 products
+    each, against the TF32 dense rate (half the measured bf16 burst), and the
+    134 MB the layer must move (read x, write y) against the measured copy
+    bandwidth."""
+    import torch
+    synth = importlib.import_module("maxim-rs_b200.synth")
+    work = importlib.import_module("maxim-rs_b200.work")
+    d = os.path.join(tempfile.gettempdir(), "maxim_b200_bench")
+    os.makedirs(d, exist_ok=True)
+    path = os.path.join(d, "gMLP-64_seed2.safetensors")
+    if not os.path.exists(path):
+        synth.write_safetensors(path, synth.make_params("gMLP-64", 2, dense_std=0.02), "gMLP-64")
+    x = synth.input_rng(2).standard_normal((1, 512, 512, 64)).astype(np.float32)[0].transpose(2, 0, 1).copy()
+    plan = mx.Plan(mx.Weights(path), 512, 512)
+    g = mx.Gpu(plan, device=local)
+    flop = sum(v[1] for v in work.census(plan).values())
+    xd = torch.from_numpy(x).cuda(local)
+    yd = torch.empty(g.out_shape, dtype=torch.float32, device="cuda:%d" % local)
+    stream = torch.cuda.ExternalStream(g.stream(), device=torch.device("cuda", local))
+
+    def one():
+        g.upload_input_device(xd.data_ptr())
+        g.enqueue()
+        g.download_output_device(yd.data_ptr())
+
+    for _ in range(warmup):
+        one()
+    g.sync()
+    dev = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        one()
+        e1.record(stream)
+        e1.synchronize()
+        dev.append(e0.elapsed_time(e1))
+    g.sync()
+    pin_in = torch.from_numpy(x).pin_memory()
+    pin_out = torch.empty(g.out_shape, dtype=torch.float32).pin_memory()
+    host = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        g.run(pin_in.numpy(), pin_out.numpy())
+        host.append((time.perf_counter() - t0) * 1e3)
+    g.close()
+    ms = statistics.median(dev)
+    hbm, tf_burst, _, _ = peaks()
+    tf32 = tf_burst / 2
+    issued = 3 * flop
+    min_bytes = 2 * x.nbytes
+    return {"ms": ms, "e2e_ms": statistics.median(host), "reps": reps,
+            "config": "one split-head multi-axis gMLP layer, NHWC [1,512,512,64] N(0,1), Dense N(0,0.02), seed 2",
+            "gflop": flop / 1e9, "useful_tflops": flop / ms / 1e9,
+            "roofline": {"bound": "tensor", "achieved": issued / ms / 1e9, "peak": tf32, "unit": "TFLOP/s",
+                         "frac": issued / ms / 1e9 / tf32, "peak_source": "TF32 dense = half the measured bf16 burst",
+                         "min_bytes": min_bytes, "hbm_frac_of_min_traffic": min_bytes / (ms / 1e3) / 1e9 / hbm}}
+
+
 def run_native(args):
     import torch
     import torch.distributed as dist
@@ -445,8 +563,9 @@ def run_native(args):
     e2e_s = max_over_ranks(e2e_s, world, "cuda:%d" % local)
     e2e = job_mpx_per_s(args.steps * B, world, e2e_s)
 
-    # Roofline of the dominant kernel family, from per-op CUDA events on the
-    # executor's stream over one pass of the same workload.
+    # Roofline of the dominant step family, from per-step CUDA events on the
+    # executor's stream over one pass of the same workload (a kernel timed
+    # inside a long pass: the sustained peaks).
     hbm, tf_burst, tf_sus, src = peaks()
     gpu.set_timeline(True)
     gpu.upload_input_device(in_dev[0].data_ptr())
@@ -465,27 +584,19 @@ def run_native(args):
         e[3] += b
     dom = max(fam, key=lambda k: fam[k][1])
     n_l, ms_tot, fl, by = fam[dom]
-    avg_s = ms_tot / 1000.0 / n_l
-    t_mem, t_tc = (by / n_l) / (hbm * 1e9), (fl / n_l) / (tf_sus * 1e12)
-    if t_tc > t_mem:
-        roof = {"bound": "tensor", "achieved": fl / n_l / avg_s / 1e12, "peak": tf_sus, "unit": "TFLOP/s"}
-    else:
-        roof = {"bound": "hbm", "achieved": by / n_l / avg_s / 1e9, "peak": hbm, "unit": "GB/s"}
-    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof = work.roofline(dom, fl / n_l, by / n_l, ms_tot / 1000.0 / n_l, hbm, tf_sus / 2)
     roof["traffic"] = traffic_from_profiles(dom)
     roof["kernel"] = dom
     roof["launches_per_pass"] = n_l
     roof["share_of_pass"] = ms_tot / total
-    roof["peak_source"] = src + (" bf16 sustained" if roof["bound"] == "tensor" else " copy")
+    roof["peak_source"] = src + (" copy" if roof["bound"] == "hbm" else
+                                 " TF32 dense = half the sustained bf16 figure (3 TF32 products per useful MAC)")
     roof["algorithmic_per_launch"] = {"flop": fl / n_l, "bytes": by / n_l}
 
-    line = {"metric": METRIC, "value": value, "unit": "Mpx/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "MAXIM-3S 1280x853 (padded 1280x896), random-init He-normal weights seed %d, "
-                                   "U[0,1) images" % W_SEED, "images_per_gpu_per_step": B,
-                       "parallelism": "replicas x%d (images sharded, no collective)" % world,
-                       "l2": "no flush: each pass streams a 2012 MiB arena (L2 is 126 MB)"},
+    line = {"metric": METRIC, "value": value, "value_per_gpu": value / world, "unit": "Mpx/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": bench_config(B),
             "e2e": {"value": e2e, "unit": "Mpx/s", "h2d_bytes_per_step": int(B * in_dev[0].numel() * 4),
                     "d2h_bytes_per_step": int(B * out_dev[0].numel() * 4)},
             "gpu_launches": int(stats["kernels"] * args.steps * B),
@@ -497,12 +608,12 @@ def run_native(args):
         with Clocks(uuid) as clk5:
             line["config5_s2"] = config5_s2(mx, local)
         line["config5_s2"]["clocks"] = clk5.summary()
-    if rank == 0 and world == 1 and not args.no_cpu:
-        threads = len(os.sched_getaffinity(0))
-        v, desc, _ = cpu_sample(threads)
-        line["cpu_baseline"] = {"value": v, "unit": "Mpx/s", "cores": threads, "kind": "port",
-                                "sample": desc + "; oracle/exec_cpu.cpp, the reference's exec_cpu.rs in C++"}
+        with Clocks(uuid) as clk3:
+            line["config3_gmlp"] = config3_gmlp(mx, local)
+        line["config3_gmlp"]["clocks"] = clk3.summary()
     gpu.close()
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(len(os.sched_getaffinity(0)))
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -514,11 +625,13 @@ def run_native(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--batch", type=int, default=4, help="images per GPU per step")
+    ap.add_argument("--batch", type=int, default=1, help="images per GPU per step")
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--ref-steps", type=int, default=2,
+                    help="--impl reference: most steps to run (each is B whole images on the CPU)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--timeline", action="store_true",
                     help="print the per-op-family device time of one pass and exit (no JSON line)")
     ap.add_argument("--variant", default=VARIANT, help="--timeline only: model variant")

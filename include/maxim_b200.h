@@ -160,13 +160,28 @@ int mx_gpu_download_output_device(mx_gpu* g, float* dev_output);
  * can order its own work or record timing events against the pass. */
 int mx_gpu_stream(mx_gpu* g, void** stream);
 
-/* `Gpu::begin` / `step_op` / `read_buf` / `read_into` / `read_arena`
- * (src/exec_gpu.rs:329-357): the op-by-op walk behind `--verify-gpu`.
- * read_buf returns buffer `id` in the plan's [c][h][w] layout (converted from
- * the executor's internal layout). step_op runs op `i` alone, unfused. */
+/* `Gpu::begin` / `step_op` / `read_buf` (src/exec_gpu.rs:329-357): the
+ * op-by-op walk behind `--verify-gpu`. step_op runs op `i` alone, unfused,
+ * after mx_gpu_begin. read_buf returns buffer `id` in the plan's [c][h][w]
+ * layout (converted from the executor's internal NHWC layout), after a walk
+ * or after a pass.
+ *
+ * `Gpu::read_into` / `read_arena` (src/exec_gpu.rs:292-303): the arena as the
+ * reference's executor leaves it - every buffer at its plan offset
+ * (`mx_plan.offs`, element units) in [c][h][w] order. read_into copies `len`
+ * floats starting at element `off` (run_gpu reads the output with it,
+ * src/main.rs:501); read_arena copies all `arena_len` floats (`--dump`,
+ * src/main.rs:494-499). Buffers still live at the end of the plan - the
+ * output, and every named activation of a plan built with dumps - read
+ * exactly. Reading the output after a pass is one copy; any other range after
+ * a pass replays the plan op by op from the staged input first (the same
+ * values), then transposes each buffer into place. Ranges no buffer wrote
+ * read as zero, and the stale remains of buffers that died earlier are not
+ * reproduced. */
 int mx_gpu_begin(mx_gpu* g, const float* input);
 int mx_gpu_step_op(mx_gpu* g, int32_t i);
 int mx_gpu_read_buf(mx_gpu* g, int32_t id, float* out, int64_t len);
+int mx_gpu_read_into(mx_gpu* g, int64_t off, float* out, int64_t len);
 int mx_gpu_read_arena(mx_gpu* g, float* out, int64_t len);
 
 /* `Gpu::set_timeline` / `timeline` (src/exec_gpu.rs:180-265): with the
@@ -174,6 +189,10 @@ int mx_gpu_read_arena(mx_gpu* g, float* out, int64_t len);
  * per_op_ms[i] receives op i's device time (0 for ops fused into another). */
 int mx_gpu_set_timeline(mx_gpu* g, int on);
 int mx_gpu_timeline(mx_gpu* g, float* per_op_ms, int32_t n_ops, float* total_ms);
+/* `Timeline::kernels_per_op` (src/exec_gpu.rs:68-72): kernel launches op i
+ * made in the last timed pass (a fused op's launches count to the op whose
+ * step carried it out; ops fused into another read 0). */
+int mx_gpu_timeline_kernels(mx_gpu* g, int32_t* kernels_per_op, int32_t n_ops);
 
 /* `device_name` / `arena_bytes` / `weight_bytes` / `pool_bytes` /
  * `ops_launched` (src/exec_gpu.rs:160-190). `kernels` is the number of kernel
@@ -227,8 +246,10 @@ int mx_plan_schedule(const mx_plan* plan, mx_gpu_stats* stats, int32_t* primary,
  * contiguous, pixel_stride floats between pixels, 16-byte aligned) and the
  * output out (c floats), both in device memory; the partial sums live in one
  * fixed 1 MiB device array inside the library (held on every GPU that loads
- * it, until the process exits) instead of in allocated scratch.
- * Limits: c a multiple of 4 and at most 1024; npix and npix * pixel_stride
+ * it, until the process exits) instead of in allocated scratch. The result is
+ * bit for bit the executor's own channel mean of the same tensor (the same
+ * partition of pixels into blocks, the same two kernels).
+ * Limits: c a multiple of 4 and at most 256; npix and npix * pixel_stride
  * below 2^31. Larger sizes are rejected with MX_E_INVALID.
  * The first call on each device looks up that device's address of the array
  * (with the device current) and caches it; make that first call before any
@@ -253,7 +274,12 @@ int mx_weights_variant(const mx_weights* w, char* buf, size_t len);
 
 /* The parameter inventory a checkpoint of `variant` must hold, in the
  * builder's request order: one "name\tshape\n" line per tensor, shape as
- * comma-separated dims. `*needed` receives the full byte length. */
+ * comma-separated dims. `*needed` receives the full byte length.
+ * Variants: "S-1".."S-3", "M-1".."M-3" (src/config.rs:34-62), and
+ * "gMLP-<c>": one residual split-head multi-axis gMLP layer over a c-channel
+ * input with 16x16 blocks and a 16x16 grid, the builder's own
+ * `split_head_gmlp` (src/model.rs:576-603) as a plan of its own (input and
+ * output [c][H][W]). A checkpoint holding that layer's tensors opens as it. */
 int mx_param_spec(const char* variant, char* buf, size_t len, size_t* needed);
 
 /* `Builder::new(..)[.without_dumps()].build(h, w)` (src/model.rs:743-891):

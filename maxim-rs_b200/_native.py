@@ -83,10 +83,12 @@ _SIGS = {
     "mx_gpu_begin": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "mx_gpu_step_op": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32]),
     "mx_gpu_read_buf": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64]),
+    "mx_gpu_read_into": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64]),
     "mx_gpu_read_arena": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64]),
     "mx_gpu_set_timeline": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "mx_gpu_timeline": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                        ctypes.POINTER(ctypes.c_float)]),
+    "mx_gpu_timeline_kernels": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32]),
     "mx_gpu_get_stats": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(mx_gpu_stats)]),
     "mx_gpu_schedule": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32]),
     "mx_plan_schedule": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(mx_gpu_stats), ctypes.c_void_p,
@@ -331,7 +333,14 @@ class Gpu:
         check(lib().mx_gpu_read_buf(self._h, i, _ptr(out), out.size), "read_buf")
         return out
 
+    def read_into(self, off, n):
+        """`Gpu::read_into`: n floats of the plan-layout arena from element off."""
+        out = np.empty(n, np.float32)
+        check(lib().mx_gpu_read_into(self._h, off, _ptr(out), n), "read_into")
+        return out
+
     def read_arena(self):
+        """`Gpu::read_arena`: the whole arena in the plan's layout."""
         out = np.empty(self.plan.arena_len, np.float32)
         check(lib().mx_gpu_read_arena(self._h, _ptr(out), out.size), "read_arena")
         return out
@@ -344,6 +353,12 @@ class Gpu:
         tot = ctypes.c_float()
         check(lib().mx_gpu_timeline(self._h, _ptr(per), self.plan.n_ops, ctypes.byref(tot)), "timeline")
         return per, tot.value
+
+    def timeline_kernels(self):
+        """`Timeline::kernels_per_op` of the last timed pass."""
+        k = np.zeros(self.plan.n_ops, np.int32)
+        check(lib().mx_gpu_timeline_kernels(self._h, _ptr(k), self.plan.n_ops), "timeline kernels")
+        return k
 
     def stats(self):
         s = mx_gpu_stats()

@@ -8,7 +8,8 @@ Outputs (in-tree, git-ignored, shipped with the repository snapshot):
     maxim-rs_b200/libmaxim_b200.so   host contract + GPU executor + sm_100a kernels
     maxim-rs_b200/maxim              the PNG-in / PNG-out CLI
     oracle/_build/libmaxim_oracle.so the CPU restatement of the reference
-                                     executor (test infrastructure only)
+                                     executor with its own copy of the host
+                                     contract (test infrastructure only)
 
 CUDA code is compiled for sm_100a only (`-gencode arch=compute_100a,code=sm_100a`);
 nvcc cross-compiles it without a GPU. The CUDA runtime is linked statically and
@@ -40,6 +41,8 @@ NVFLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I" 
 LIB = os.path.join(PKG, "libmaxim_b200.so")
 CLI = os.path.join(PKG, "maxim")
 ORACLE_LIB = os.path.join(ORACLE_BUILD, "libmaxim_oracle.so")
+# The host-contract sources the oracle library carries its own copy of.
+ORACLE_HOST_SOURCES = ["capi_host.cpp", "config.cpp", "image.cpp", "model.cpp", "safetensors.cpp", "weights.cpp"]
 
 
 def _newer(out, deps):
@@ -86,12 +89,18 @@ def build(verbose=False):
     if os.path.exists(cli_src) and _newer(CLI, [cli_src, LIB] + hdrs):
         logs.append(_run(["g++"] + CXXFLAGS + [cli_src, "-o", CLI, "-L" + PKG, "-lmaxim_b200",
                                                "-Wl,-rpath,$ORIGIN"]))
-    osrc = os.path.join(ORACLE, "exec_cpu.cpp")
-    if _newer(ORACLE_LIB, [osrc] + [os.path.join(INC, f) for f in os.listdir(INC)]):
+    # The oracle library: the CPU executor plus its own copy of the host
+    # contract (plan builder, safetensors, image pipeline), compiled with
+    # hidden visibility and re-exported under mxo_ names, so a CPU-only run
+    # needs nothing from the product library.
+    osrcs = [os.path.join(ORACLE, "exec_cpu.cpp"), os.path.join(ORACLE, "host_api.cpp")] + \
+        [os.path.join(CSRC, f) for f in ORACLE_HOST_SOURCES]
+    if _newer(ORACLE_LIB, osrcs + hdrs):
         # No FMA contraction: the reference's accumulations are separate
         # multiplies and adds, and contracting them changes every rounding.
         logs.append(_run(["g++", "-O3", "-march=x86-64-v3", "-ffp-contract=off", "-std=c++17", "-fPIC", "-shared",
-                          "-I" + INC, osrc, "-o", ORACLE_LIB, "-lpthread"]))
+                          "-fvisibility=hidden", "-fvisibility-inlines-hidden", "-I" + INC, "-I" + CSRC] + osrcs +
+                         ["-o", ORACLE_LIB, "-lz", "-lpthread"]))
     if verbose:
         for l in logs:
             if l.strip():

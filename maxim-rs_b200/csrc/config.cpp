@@ -2,13 +2,28 @@
 
 #include <algorithm>
 #include <cctype>
+#include <cstdlib>
 
 #include "common.h"
 #include "safetensors.h"
 
 namespace mx {
 
+// The tensor a checkpoint of the isolated gMLP layer is recognised by.
+static const char* kBlockProbe = "SplitHeadMultiAxisGmlpLayer/in_project/kernel";
+
 Config Config::variant(const std::string& v) {
+  if (v.rfind("gMLP-", 0) == 0) {
+    const int c = std::atoi(v.c_str() + 5);
+    if (c <= 0 || c % 2 != 0 || v != "gMLP-" + std::to_string(c))
+      throw Error("unknown variant " + v + " (gMLP-<c> takes an even channel count)");
+    Config g;
+    g.name = v;
+    g.features = c;
+    g.num_stages = 0;
+    g.block_only = true;
+    return g;
+  }
   int features, stages;
   if (v == "S-1") features = 32, stages = 1;
   else if (v == "S-2") features = 32, stages = 2;
@@ -25,6 +40,11 @@ Config Config::variant(const std::string& v) {
 }
 
 Config Config::of_checkpoint(const SafeTensors& f) {
+  if (f.contains(kBlockProbe) && !f.contains("stage_0_encoder_block_0/Conv_0/kernel")) {
+    const auto& s = f.info(kBlockProbe).shape;  // Dense [c][2c]
+    if (s.size() != 2) throw Error(std::string(kBlockProbe) + " is not a Dense kernel", MX_E_IO);
+    return variant("gMLP-" + std::to_string(s[0]));
+  }
   const std::string name = "stage_0_encoder_block_0/Conv_0/kernel";
   if (!f.contains(name)) throw Error(name + " is missing (not a converted MAXIM checkpoint?)", MX_E_IO);
   const auto& s = f.info(name).shape;

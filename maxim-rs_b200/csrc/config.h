@@ -25,8 +25,12 @@ struct Config {
   int grid_size_lr = 8;
   int channels_reduction = 4;
   int num_bottleneck_blocks = 2;
+  // "gMLP-<c>": not a model but ONE residual split-head multi-axis gMLP layer
+  // (src/model.rs:576-603) over a c-channel input, block = grid = 16: the
+  // isolated block op BASELINE's config 3 measures. `features` is c.
+  bool block_only = false;
 
-  // `Config::variant` (src/config.rs:34-62).
+  // `Config::variant` (src/config.rs:34-62), plus "gMLP-<c>".
   static Config variant(const std::string& v);
   // `Config::of_checkpoint` (src/config.rs:71-100): the width is c_out of
   // `stage_0_encoder_block_0/Conv_0/kernel`, the stage count is the highest N

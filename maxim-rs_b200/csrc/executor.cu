@@ -22,6 +22,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -217,7 +218,14 @@ struct mx_gpu {
   cudaGraphExec_t graph_exec = nullptr;
   bool timeline_on = false;
   std::vector<float> timeline_ms;
+  std::vector<int32_t> timeline_kernels;
   float timeline_total = 0.0f;
+  // What the arena holds: nothing yet, the scheduled pass's state (at foffs),
+  // or the op-by-op walk's (at the plan's offsets).
+  enum { HOLDS_NOTHING, HOLDS_PASS, HOLDS_WALK } holds = HOLDS_NOTHING;
+  std::vector<int32_t> write_order;  // storage roots by their last write in the plan (input first)
+  float* readback = nullptr;         // device staging for plan-layout read-back (largest root)
+  int64_t readback_len = 0;
   int64_t kernels = 0;
   int64_t umma_ops = 0;
   std::string name;
@@ -1254,6 +1262,113 @@ void validate_weights(const mx_plan& plan) {
   }
 }
 
+// ------------------------------------------------- plan-layout read-back
+// The reference's executor keeps every buffer at the plan's offset in
+// [c][h][w] order, and its callers read that arena back directly
+// (`Gpu::read_into` / `read_arena`, src/exec_gpu.rs:284-303; `--dump`,
+// src/main.rs:494-499). This executor keeps its buffers NHWC, and a scheduled
+// pass packs them at its own offsets. The read-back below rebuilds the
+// plan's view: the op-by-op walk (at the plan's offsets) provides the values,
+// and every storage root is transposed to [c][h][w] into its plan region,
+// later writers over earlier ones.
+
+// Storage roots in the order of their last write by the plan's ops (the
+// input, written before the first op, comes first).
+const std::vector<int32_t>& write_order(mx_gpu& g) {
+  if (!g.write_order.empty()) return g.write_order;
+  const size_t nb = g.offs.size();  // the plan's buffers (the schedule's extras are not in the plan's arena)
+  std::vector<int64_t> last(nb, INT64_MIN);
+  last[size_t(root_of(g, g.input))] = -1;
+  for (size_t i = 0; i < g.ops.size(); ++i) {
+    const mx_op& o = g.ops[i];
+    if (o.dst >= 0) last[size_t(root_of(g, o.dst))] = int64_t(i);
+    if (o.kind == MX_OP_RESIZE && o.tmp >= 0) last[size_t(root_of(g, o.tmp))] = int64_t(i);
+  }
+  std::vector<int32_t> roots;
+  for (size_t b = 0; b < nb; ++b)
+    if (last[b] != INT64_MIN) roots.push_back(int32_t(b));
+  std::stable_sort(roots.begin(), roots.end(), [&](int32_t a, int32_t b) { return last[size_t(a)] < last[size_t(b)]; });
+  g.write_order = std::move(roots);
+  return g.write_order;
+}
+
+// Put the op-by-op walk's state in the arena. After a scheduled pass the
+// input is still staged, so the walk is replayed from it (bit-identical to
+// the pass: every value is computed by the same operations in the same order).
+void hold_walk(mx_gpu& g) {
+  if (g.holds == mx_gpu::HOLDS_WALK) return;
+  if (g.holds == mx_gpu::HOLDS_NOTHING) throw Error("the arena holds nothing yet: run a pass or begin a walk first");
+  for (size_t i = 0; i + 1 < g.steps.size(); ++i) g.steps[i].run(g.stream);  // input transpose, every op
+  check_launch();
+  MX_CUDA(cudaStreamSynchronize(g.stream));
+  check_status(g);
+  g.holds = mx_gpu::HOLDS_WALK;
+}
+
+// Elements [off, off + len) of the arena in the plan's layout, into host
+// memory. Regions no plan buffer wrote read as zero. A buffer still live at
+// the end of the plan (its output, and every named activation of a plan built
+// with dumps) reads exactly; the stale remains of buffers that died earlier
+// are not reproduced (the reference leaves whatever was last written there).
+void read_plan_layout(mx_gpu& g, int64_t off, int64_t len, float* out) {
+  if (off < 0 || len < 0 || off + len > g.arena_len) throw Error("read: the range runs past the arena");
+  if (len == 0) return;
+  const int64_t oo = g.offs[size_t(g.output)], on = len_of(g.bufs[size_t(g.output)]);
+  if (g.holds == mx_gpu::HOLDS_PASS && off >= oo && off + len <= oo + on) {
+    // The pass's output transpose already left the output in [c][h][w].
+    MX_CUDA(cudaMemcpyAsync(out, g.io_out + (off - oo), size_t(len) * 4, cudaMemcpyDeviceToHost, g.stream));
+    MX_CUDA(cudaStreamSynchronize(g.stream));
+    return;
+  }
+  hold_walk(g);
+  memset(out, 0, size_t(len) * 4);
+  const std::vector<int32_t>& order = write_order(g);
+  std::vector<std::pair<int64_t, int64_t>> covered;  // sorted, disjoint
+  for (size_t k = order.size(); k-- > 0;) {
+    const int32_t r = order[k];
+    const mx_buf& b = g.bufs[size_t(r)];
+    const int64_t r0 = g.offs[size_t(r)], rn = len_of(b);
+    const int64_t lo = std::max(off, r0), hi = std::min(off + len, r0 + rn);
+    if (lo >= hi) continue;
+    std::vector<std::pair<int64_t, int64_t>> vis;  // [lo, hi) less what later writers cover
+    int64_t a = lo;
+    for (const auto& c : covered) {
+      if (c.second <= a) continue;
+      if (c.first >= hi) break;
+      if (c.first > a) vis.push_back({a, c.first});
+      a = std::max(a, c.second);
+      if (a >= hi) break;
+    }
+    if (a < hi) vis.push_back({a, hi});
+    if (vis.empty()) continue;
+    if (g.readback_len < rn) {
+      cudaFree(g.readback);
+      g.readback = nullptr;
+      g.readback_len = 0;
+      MX_CUDA(cudaMalloc(&g.readback, size_t(rn) * 4));
+      g.readback_len = rn;
+    }
+    const int64_t npix = b.h * b.w;
+    nhwc_to_nchw_kernel<<<blocks_for(npix * b.c, TPB), TPB, 0, g.stream>>>(npix, int(b.c), g.arena + r0, b.c,
+                                                                           g.readback);
+    check_launch();
+    for (const auto& v : vis)
+      MX_CUDA(cudaMemcpyAsync(out + (v.first - off), g.readback + (v.first - r0), size_t(v.second - v.first) * 4,
+                              cudaMemcpyDeviceToHost, g.stream));
+    MX_CUDA(cudaStreamSynchronize(g.stream));
+    covered.push_back({lo, hi});
+    std::sort(covered.begin(), covered.end());
+    std::vector<std::pair<int64_t, int64_t>> merged;
+    for (const auto& c : covered) {
+      if (!merged.empty() && c.first <= merged.back().second)
+        merged.back().second = std::max(merged.back().second, c.second);
+      else
+        merged.push_back(c);
+    }
+    covered.swap(merged);
+  }
+}
+
 }  // namespace
 
 const char* describe_kind(int k) {
@@ -1404,6 +1519,7 @@ void mx_gpu_free(mx_gpu* g) {
   cudaFree(g->io_out);
   cudaFree(g->status);
   cudaFree(g->scratch);
+  cudaFree(g->readback);
   if (g->stream) cudaStreamDestroy(g->stream);
   delete g;
 }
@@ -1461,19 +1577,25 @@ int mx_gpu_enqueue(mx_gpu* g) {
       MX_CUDA(cudaEventSynchronize(ev[n]));
       check_status(*g);
       g->timeline_ms.assign(g->ops.size(), 0.0f);
+      g->timeline_kernels.assign(g->ops.size(), 0);
       g->timeline_total = 0.0f;
       for (size_t i = 0; i < n; ++i) {
         float ms = 0.0f;
         MX_CUDA(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
         g->timeline_total += ms;
         int op = g->fsteps[i].op;  // a fused step's time goes to its primary op
-        if (op >= 0) g->timeline_ms[size_t(op)] += ms;
+        if (op >= 0) {
+          g->timeline_ms[size_t(op)] += ms;
+          g->timeline_kernels[size_t(op)] += g->fsteps[i].kernels;
+        }
       }
       for (auto& e : ev) cudaEventDestroy(e);
+      g->holds = mx_gpu::HOLDS_PASS;
       return;
     }
     capture_graph(*g);
     MX_CUDA(cudaGraphLaunch(g->graph_exec, g->stream));
+    g->holds = mx_gpu::HOLDS_PASS;
   });
 }
 
@@ -1515,12 +1637,14 @@ int mx_gpu_begin(mx_gpu* g, const float* input) {
     check_launch();
     MX_CUDA(cudaStreamSynchronize(g->stream));
     check_status(*g);
+    g->holds = mx_gpu::HOLDS_WALK;
   });
 }
 
 int mx_gpu_step_op(mx_gpu* g, int32_t i) {
   return guard([&] {
     if (!g || i < 0 || size_t(i) >= g->ops.size()) throw Error("mx_gpu_step_op: op index out of range");
+    if (g->holds != mx_gpu::HOLDS_WALK) throw Error("mx_gpu_step_op: begin the walk first (mx_gpu_begin)");
     DevicePin pin(g->device);
     int s = g->step_of_op[size_t(i)];
     if (s >= 0) g->steps[size_t(s)].run(g->stream);
@@ -1535,6 +1659,12 @@ int mx_gpu_read_buf(mx_gpu* g, int32_t id, float* out, int64_t len) {
     if (!g || !out || id < 0 || size_t(id) >= g->offs.size()) throw Error("mx_gpu_read_buf: bad argument");
     if (len != len_of(g->bufs[size_t(id)])) throw Error("mx_gpu_read_buf: length does not match the buffer");
     DevicePin pin(g->device);
+    if (g->holds == mx_gpu::HOLDS_PASS && id == g->output) {
+      MX_CUDA(cudaMemcpyAsync(out, g->io_out, size_t(len) * 4, cudaMemcpyDeviceToHost, g->stream));
+      MX_CUDA(cudaStreamSynchronize(g->stream));
+      return;
+    }
+    hold_walk(*g);
     View v = view_of(*g, g->offs, id);
     float* tmp = nullptr;
     MX_CUDA(cudaMalloc(&tmp, size_t(std::max<int64_t>(len, 1)) * 4));
@@ -1547,12 +1677,19 @@ int mx_gpu_read_buf(mx_gpu* g, int32_t id, float* out, int64_t len) {
   });
 }
 
+int mx_gpu_read_into(mx_gpu* g, int64_t off, float* out, int64_t len) {
+  return guard([&] {
+    if (!g || (!out && len > 0)) throw Error("mx_gpu_read_into: null argument");
+    DevicePin pin(g->device);
+    read_plan_layout(*g, off, len, out);
+  });
+}
+
 int mx_gpu_read_arena(mx_gpu* g, float* out, int64_t len) {
   return guard([&] {
     if (!g || !out || len != g->arena_len) throw Error("mx_gpu_read_arena: bad argument");
     DevicePin pin(g->device);
-    MX_CUDA(cudaMemcpyAsync(out, g->arena, size_t(len) * 4, cudaMemcpyDeviceToHost, g->stream));
-    MX_CUDA(cudaStreamSynchronize(g->stream));
+    read_plan_layout(*g, 0, len, out);
   });
 }
 
@@ -1572,6 +1709,15 @@ int mx_gpu_timeline(mx_gpu* g, float* per_op_ms, int32_t n_ops, float* total_ms)
       memcpy(per_op_ms, g->timeline_ms.data(), g->ops.size() * 4);
     }
     if (total_ms) *total_ms = g->timeline_total;
+  });
+}
+
+int mx_gpu_timeline_kernels(mx_gpu* g, int32_t* kernels_per_op, int32_t n_ops) {
+  return guard([&] {
+    if (!g || !kernels_per_op) throw Error("mx_gpu_timeline_kernels: null argument");
+    if (g->timeline_kernels.empty()) throw Error("no timeline recorded: turn it on and run a pass first");
+    if (size_t(n_ops) != g->ops.size()) throw Error("mx_gpu_timeline_kernels: n_ops does not match the plan");
+    memcpy(kernels_per_op, g->timeline_kernels.data(), g->ops.size() * sizeof(int32_t));
   });
 }
 

@@ -38,6 +38,7 @@ class Builder {
   }
 
   std::unique_ptr<Plan> build(int64_t h, int64_t wd);
+  std::unique_ptr<Plan> build_block(int64_t h, int64_t wd);
 
  private:
   const Weights& w_;
@@ -541,7 +542,21 @@ class Builder {
   std::unique_ptr<Plan> finish(int32_t input, int32_t output, mx_buf shape);
 };
 
+// One residual split-head multi-axis gMLP layer on its own (BASELINE's
+// isolated block op): the same builder method the model calls
+// (`split_head_gmlp`, src/model.rs:576-603), over a c-channel input.
+std::unique_ptr<Plan> Builder::build_block(int64_t h, int64_t wd) {
+  const int64_t c = cfg_.features;
+  int32_t input = buf(c, h, wd, "input");
+  rec("input", input);
+  int32_t out = split_head_gmlp("SplitHeadMultiAxisGmlpLayer", input, c, h, wd, cfg_.block_size_hr,
+                                cfg_.grid_size_hr);
+  rec("final", out);
+  return finish(input, out, mx_buf{c, h, wd});
+}
+
 std::unique_ptr<Plan> Builder::build(int64_t h, int64_t wd) {
+  if (cfg_.block_only) return build_block(h, wd);
   const int depth = cfg_.depth, stages = cfg_.num_stages, nss = cfg_.num_supervision_scales;
   const int64_t features = cfg_.features;
   const int64_t red = cfg_.channels_reduction;

@@ -15,6 +15,12 @@
 // writes every partial it later reads, so nothing has to start at zero, but
 // two calls that overlap on the GPU (different streams, no ordering) race on
 // it and give wrong results.
+//
+// The partition (one block per 512 pixels, at most 1024 blocks) and both
+// kernels are the executor's own, so a call returns bit for bit what the
+// executor's ChanMean step returns for the same tensor. The array holds that
+// partition's 1024 partial rows for up to 256 channels, which is why the
+// channel limit is 256 (the model's widest channel attention has 128).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -28,9 +34,9 @@
 namespace mx {
 namespace {
 
-constexpr int kMaxScratch = 1 << 18;  // floats of per-block partial sums (1 MiB)
-constexpr int kMaxChannels = 1024;
-constexpr int kMaxBlocks = 1024;
+constexpr int kMaxBlocks = 1024;                       // the executor's partition cap
+constexpr int kMaxChannels = 256;
+constexpr int kMaxScratch = kMaxBlocks * kMaxChannels;  // floats of partial sums (1 MiB)
 
 __device__ __align__(256) float g_mean_scratch[kMaxScratch];
 
@@ -78,14 +84,13 @@ extern "C" int mx_channel_mean_noalloc(const float* x, int64_t npix, int32_t c, 
     if (npix * pixel_stride >= (int64_t(1) << 31))
       throw Error("mx_channel_mean_noalloc: the input spans 2^31 or more floats");
     float* part = scratch_on_current_device();
-    // The executor's partition (one block per 512 pixels, at most 1024
-    // blocks), capped by what the fixed scratch holds.
-    const int nb = int(std::max<int64_t>(
-        1, std::min<int64_t>(std::min<int64_t>((npix + 511) / 512, kMaxBlocks), kMaxScratch / c)));
+    // The executor's partition: one block per 512 pixels, at most 1024
+    // blocks; nb * c <= kMaxScratch by the channel limit above.
+    const int nb = int(std::max<int64_t>(1, std::min<int64_t>((npix + 511) / 512, kMaxBlocks)));
     const int per = int((npix + nb - 1) / nb);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     chan_mean_partial_kernel<<<unsigned(nb), 256, 0, s>>>(int(npix), c / 4, per, x, int(pixel_stride), part);
-    chan_mean_final_kernel<<<unsigned((c + 127) / 128), 128, 0, s>>>(nb, c, int(npix), part, out);
+    chan_mean_final_tree_kernel<<<unsigned(c), 256, 0, s>>>(nb, c, int(npix), part, out);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) throw Error(std::string("mx_channel_mean_noalloc: launch: ") + cudaGetErrorString(e), MX_E_CUDA);
   });

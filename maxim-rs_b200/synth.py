@@ -27,9 +27,10 @@ import numpy as np
 from . import _native
 
 
-def make_params(variant, seed, gain=1.0, rich=False, dense_std=None):
-    """{name: float32 array} for every tensor `variant` needs."""
-    spec = dict(_native.param_spec(variant))
+def make_params(variant, seed, gain=1.0, rich=False, dense_std=None, spec=None):
+    """{name: float32 array} for every tensor `variant` needs. `spec` is the
+    parameter inventory [(name, shape)]; by default the library's builder's."""
+    spec = dict(spec if spec is not None else _native.param_spec(variant))
     rng = np.random.default_rng(seed)
     out = {}
     for name in sorted(spec):
@@ -74,10 +75,10 @@ def write_safetensors(path, params, variant, task="synthetic"):
     return path
 
 
-def checkpoint(path, variant, seed, gain=1.0, rich=False):
+def checkpoint(path, variant, seed, gain=1.0, rich=False, spec=None):
     """Write (or reuse) a synthetic checkpoint and return its path."""
     if not os.path.exists(path):
-        write_safetensors(path, make_params(variant, seed, gain, rich), variant)
+        write_safetensors(path, make_params(variant, seed, gain, rich, spec=spec), variant)
     return path
 
 

@@ -105,3 +105,29 @@ def census(plan):
         e[1] += f
         e[2] += b
     return out
+
+
+# Op kinds whose products run on the tensor cores as the 3xTF32 split: each
+# useful multiply-add is issued as three TF32 products (a_hi*b_hi, a_hi*b_lo,
+# a_lo*b_hi).
+TENSOR_KINDS = ("conv1x1", "conv3x3", "conv4x4s2", "convt2x2", "gate_mm")
+TF32_PRODUCTS = 3
+
+
+def roofline(family, flops, nbytes, seconds, hbm_gbs, tf32_tflops):
+    """The roofline of one step family over `seconds` of device time.
+
+    The bound is whichever of HBM (algorithmic bytes at the measured copy
+    bandwidth) and the tensor pipe (issued TF32 FLOPs, three per useful
+    multiply-add, at the TF32 dense rate) takes longer; `frac` is the
+    family's attainable time over its measured time, i.e. achieved / peak on
+    that bound. Families that are not contractions are HBM-bound."""
+    base = family.split("+")[0].split("(")[0]
+    issued = flops * (TF32_PRODUCTS if base in TENSOR_KINDS else 0)
+    t_mem = nbytes / (hbm_gbs * 1e9)
+    t_tc = issued / (tf32_tflops * 1e12) if issued else 0.0
+    if t_tc > t_mem:
+        return {"bound": "tensor", "achieved": issued / seconds / 1e12, "peak": tf32_tflops, "unit": "TFLOP/s",
+                "frac": t_tc / seconds, "frac_hbm": t_mem / seconds}
+    return {"bound": "hbm", "achieved": nbytes / seconds / 1e9, "peak": hbm_gbs, "unit": "GB/s",
+            "frac": t_mem / seconds, "frac_tensor": t_tc / seconds}

@@ -542,7 +542,7 @@ extern "C" {
 
 // Run the whole plan. `arena` holds plan->arena_len floats with the input
 // image already at offs[input]. `threads` <= 0 means all hardware threads.
-int mxo_run(const mx_plan* plan, float* arena, int threads) {
+__attribute__((visibility("default"))) int mxo_run(const mx_plan* plan, float* arena, int threads) {
   if (!plan || !arena) return MX_E_INVALID;
   Pool pool(threads > 0 ? threads : int(std::thread::hardware_concurrency()));
   Ctx ctx{*plan, arena, pool};
@@ -551,7 +551,8 @@ int mxo_run(const mx_plan* plan, float* arena, int threads) {
 }
 
 // Run ops [first, last) - the op-by-op walk `--verify-gpu` uses (`step`).
-int mxo_run_range(const mx_plan* plan, float* arena, int32_t first, int32_t last, int threads) {
+__attribute__((visibility("default"))) int mxo_run_range(const mx_plan* plan, float* arena, int32_t first,
+                                                        int32_t last, int threads) {
   if (!plan || !arena || first < 0 || last > plan->n_ops || first > last) return MX_E_INVALID;
   Pool pool(threads > 0 ? threads : int(std::thread::hardware_concurrency()));
   Ctx ctx{*plan, arena, pool};

@@ -102,7 +102,7 @@ def test_gpu_read_arena_and_stats(mx, checkpoint):
     z, w, img = golden_setup(mx, checkpoint, "m1_64")
     plan = mx.Plan(w, 64, 64)
     gpu = mx.Gpu(plan)
-    gpu.run(img)
+    out = gpu.run(img)
     s = gpu.stats()
     assert s["arena_bytes"] == plan.arena_bytes
     assert s["ops"] == plan.n_ops
@@ -110,6 +110,51 @@ def test_gpu_read_arena_and_stats(mx, checkpoint):
     assert "B200" in s["device_name"] or s["device_name"]
     a = gpu.read_arena()
     assert a.size == plan.arena_len
+    o = plan.off(plan.output)
+    assert np.array_equal(a[o:o + out.size].reshape(out.shape), out)
+
+
+def test_gpu_read_into_and_read_arena_match_the_plan_layout(mx, oracle, checkpoint):
+    """`run_gpu`'s two read paths (src/main.rs:494-501): `read_into` at
+    plan.offs[output] and, for `--dump`, `read_arena` followed by slicing every
+    named activation out of it at its plan offset in [c][h][w] order. A plan
+    built with dumps keeps those activations live to the end, so each must
+    match the CPU path's arena at the same offset; the output must be exactly
+    what mx_gpu_run returned, through either read."""
+    z, w, img = golden_setup(mx, checkpoint, "s2_64_rich")
+    plan = mx.Plan(w, 64, 64, dumps=True)
+    gpu = mx.Gpu(plan)
+    out = gpu.run(img)
+    o, n = plan.off(plan.output), out.size
+    assert np.array_equal(gpu.read_into(o, n).reshape(out.shape), out)
+    assert np.array_equal(gpu.read_buf(plan.output), out)
+    arena = gpu.read_arena()
+    assert arena.size == plan.arena_len
+    assert np.array_equal(arena[o:o + n].reshape(out.shape), out)
+    cpu = oracle.run(plan, img)
+    dumps = plan.dumps()
+    assert len(dumps) > 10
+    for name, bid in dumps:
+        c, h, ww = plan.buf(bid)
+        off, k = plan.off(bid), c * h * ww
+        ref, got = cpu[off:off + k], arena[off:off + k]
+        if np.abs(ref).max() > 0:
+            assert psnr(ref, got) >= 50.0, name
+        else:
+            assert np.abs(got).max() == 0, name
+    name, bid = dumps[len(dumps) // 2]
+    off, k = plan.off(bid), int(np.prod(plan.buf(bid)))
+    assert np.array_equal(gpu.read_into(off, k), arena[off:off + k]), name
+    assert np.array_equal(gpu.read_buf(bid).reshape(-1), arena[off:off + k]), name
+    # The op-by-op walk leaves the same arena.
+    gpu.begin(img)
+    for i in range(plan.n_ops):
+        gpu.step_op(i)
+    assert np.array_equal(gpu.read_arena(), arena)
+    # And a pass after the walk reads its output without a replay.
+    again = gpu.run(img)
+    assert np.array_equal(again, out)
+    assert np.array_equal(gpu.read_into(o, n).reshape(out.shape), out)
 
 
 def test_timeline_covers_every_op(mx, checkpoint):
@@ -120,8 +165,13 @@ def test_timeline_covers_every_op(mx, checkpoint):
     gpu.set_timeline(True)
     out = gpu.run(img)
     per, total = gpu.timeline()
+    kern = gpu.timeline_kernels()
     assert np.array_equal(ref, out)
     assert per.shape == (plan.n_ops,) and total > 0 and (per >= 0).all()
+    # `kernels_per_op` (src/exec_gpu.rs:68-72): every launch of the pass but
+    # the two boundary transposes belongs to a plan op.
+    assert kern.shape == (plan.n_ops,) and (kern >= 0).all()
+    assert int(kern.sum()) == gpu.stats()["kernels"] - 2
 
 
 def test_oversized_pass_is_refused_before_allocating(mx, checkpoint):
