@@ -373,8 +373,10 @@ bool umma_gate_spatial_ok(const mx_gpu& g, const Layout& L, const mx_op& gate, c
 void umma_attrs_once() {
   static bool done = false;
   if (done) return;
-#define MX_UMMA_ATTR(NN, MM)                                                                       \
-  MX_CUDA(cudaFuncSetAttribute(umma_conv_kernel<NN, MM>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+#define MX_UMMA_ATTR(NN, MM)                                                                              \
+  MX_CUDA(cudaFuncSetAttribute(umma_conv_kernel<NN, MM, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                               UmmaCfg<NN, MM>::SMEM_BYTES));                                                \
+  MX_CUDA(cudaFuncSetAttribute(umma_conv_kernel<NN, MM, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
                                UmmaCfg<NN, MM>::SMEM_BYTES));
   MX_UMMA_INSTANCES(MX_UMMA_ATTR)
 #undef MX_UMMA_ATTR
@@ -391,11 +393,15 @@ int umma_smem(int n, int mode) {
 // Columns per tile for an output of n columns (32..256), and the slices.
 int umma_tile_n(int n) { return n > 128 ? 128 : n; }
 void launch_umma(cudaStream_t s, const UmmaOp& u) {
-#define MX_UMMA_CASE(NN, MM)                                                                      \
-  if (u.n == NN && u.mode == MM) {                                                                \
-    umma_conv_kernel<NN, MM>                                                                      \
-        <<<unsigned(u.grid), UmmaCfg<NN, MM>::THREADS, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.l, u.p);      \
-    return;                                                                                       \
+#define MX_UMMA_CASE(NN, MM)                                                                              \
+  if (u.n == NN && u.mode == MM) {                                                                        \
+    if (u.p.epi >= UEPI_ADD)                                                                              \
+      umma_conv_kernel<NN, MM, true>                                                                      \
+          <<<unsigned(u.grid), UmmaCfg<NN, MM>::THREADS, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.l, u.p);    \
+    else                                                                                                  \
+      umma_conv_kernel<NN, MM, false>                                                                     \
+          <<<unsigned(u.grid), UmmaCfg<NN, MM>::THREADS, u.smem, s>>>(u.a, u.b, u.blo, u.d, u.l, u.p);    \
+    return;                                                                                               \
   }
   MX_UMMA_INSTANCES(MX_UMMA_CASE)
 #undef MX_UMMA_CASE

@@ -75,6 +75,70 @@ __device__ __forceinline__ float gelu_f(float x) {
   return fmaf(-__fmul_rn(u, e), p, fmaxf(x, 0.0f));
 }
 __device__ __forceinline__ float sigmoid_f(float a) { return 1.0f / (1.0f + expf(-a)); }
+
+// Paired fp32 arithmetic (the f32x2 instructions of sm_100): one instruction
+// carries out the same IEEE round-to-nearest operation on two lanes, each
+// lane rounded exactly as the scalar instruction rounds it, so a paired
+// evaluation is bit-identical to the scalar one and halves the instructions
+// the epilogue issues for it.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// a += b and c += d as one paired add.
+__device__ __forceinline__ void f2_add_to(float& a, float& c, float b, float d) {
+  f2_unpack(f2_add(f2_pack(a, c), f2_pack(b, d)), a, c);
+}
+
+// gelu_f on two values at once, bit-identical to gelu_f on each. With
+// w = -u = max(-|x|, -5.6) and kGeluRw[k] = (-1)^k kGeluR[k] (the magnitudes:
+// R's coefficients alternate in sign), Horner over w gives (-1)^k times every
+// partial sum of Horner over u - the same magnitudes, rounded the same way -
+// and ends on exactly R(u); w e is then exactly -(u e), the scalar form's
+// first factor.
+__device__ __forceinline__ void gelu_f2(float& a, float& b) {
+  constexpr float kGeluRw[12] = {
+      0.4999999701976776f,
+      0.3989405930042267f,
+      0.24997256696224213f,
+      0.13280577957630157f,
+      0.06192392110824585f,
+      0.025471799075603485f,
+      0.009003829210996628f,
+      0.0025900795590132475f,
+      0.0005636486457660794f,
+      8.47700794111006e-05f,
+      7.708666089456528e-06f,
+      3.155372496621567e-07f};
+  const uint64_t w = f2_pack(fmaxf(-fabsf(a), -5.6f), fmaxf(-fabsf(b), -5.6f));
+  uint64_t p = f2_pack(kGeluRw[11], kGeluRw[11]);
+#pragma unroll
+  for (int k = 10; k >= 0; --k) p = f2_fma(p, w, f2_pack(kGeluRw[k], kGeluRw[k]));
+  const uint64_t x = f2_pack(a, b);
+  float ta, tb;
+  f2_unpack(f2_mul(f2_mul(x, f2_pack(-0.72134752f, -0.72134752f)), x), ta, tb);
+  const uint64_t s = f2_mul(w, f2_pack(ex2_approx(ta), ex2_approx(tb)));
+  f2_unpack(f2_fma(s, p, f2_pack(fmaxf(a, 0.0f), fmaxf(b, 0.0f))), a, b);
+}
 #endif
 
 }  // namespace mx

@@ -152,16 +152,32 @@ __device__ __forceinline__ void gate_sp_coords(const UmmaConvParams& p, int G, i
   else fy = t0 >> p.sp_shift;
 }
 
+// GELU runs on value pairs (f32x2): the same roundings as the scalar form
+// (the elementwise kernels' gelu_f), half the instructions. The binary tails
+// stay scalar: their operand registers leave the 96-register instances no
+// room for pairing.
 template <int KIND>
 __device__ __forceinline__ void epi_chunk(float (&v)[16], const float (&e)[16], float slope) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    if (KIND == UEPI_GELU) v[i] = gelu_f(v[i]);
-    else if (KIND == UEPI_LRELU) v[i] = v[i] >= 0.0f ? v[i] : slope * v[i];
-    else if (KIND == UEPI_SIGMOID) v[i] = sigmoid_f(v[i]);
-    else if (KIND == UEPI_ADD) v[i] = v[i] + e[i];
-    else if (KIND == UEPI_MUL) v[i] = e[i] * v[i];
-    else if (KIND == UEPI_GATE) v[i] = e[i] * (v[i] + 1.0f);
+  for (int i = 0; i < 16; i += 2) {
+    if (KIND == UEPI_GELU) {
+      gelu_f2(v[i], v[i + 1]);
+    } else if (KIND == UEPI_LRELU) {
+      v[i] = v[i] >= 0.0f ? v[i] : slope * v[i];
+      v[i + 1] = v[i + 1] >= 0.0f ? v[i + 1] : slope * v[i + 1];
+    } else if (KIND == UEPI_SIGMOID) {
+      v[i] = sigmoid_f(v[i]);
+      v[i + 1] = sigmoid_f(v[i + 1]);
+    } else if (KIND == UEPI_ADD) {
+      v[i] = v[i] + e[i];
+      v[i + 1] = v[i + 1] + e[i + 1];
+    } else if (KIND == UEPI_MUL) {
+      v[i] = e[i] * v[i];
+      v[i + 1] = e[i + 1] * v[i + 1];
+    } else if (KIND == UEPI_GATE) {
+      v[i] = e[i] * (v[i] + 1.0f);
+      v[i + 1] = e[i + 1] * (v[i + 1] + 1.0f);
+    }
   }
 }
 
@@ -254,7 +270,10 @@ __device__ __forceinline__ float tf32_residual(float v) {
   return __uint_as_float((__float_as_uint(r) + 0x1000u) & 0xFFFFE000u);
 }
 
-template <int N, int MODE>
+// E: the epilogue's tail reads a second operand (UEPI_ADD / _MUL / _GATE).
+// Instances without one keep no operand registers, which the 96-register
+// 576-thread instances need for their paired GELU.
+template <int N, int MODE, bool E>
 __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
     umma_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmD,
@@ -693,13 +712,14 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
     const int set = ew >> 2;
     const int q = warp & 3;         // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;  // accumulator row this thread owns
-    const bool has_e = p.epi >= UEPI_ADD;
+    constexpr int NE = E ? 32 : 1;  // operand values held per thread
     uint8_t* sb = staging + ew * 4096;
 
     // The second operand's values for this thread in chunk j of tile t: for
     // row layouts its output pixel's 32 channels, for gating layouts its
     // channel at the chunk's 32 output positions of its group.
-    auto load_e = [&](int t, int j, float(&e)[32]) {
+    auto load_e = [&](int t, int j, float(&e)[NE]) {
+      if constexpr (E) {
       int a0, a1, n0;
       decode(t, a0, a1, n0);
       const int col = n0 + j * 32;
@@ -746,6 +766,7 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
           e[i] = ok ? src[size_t(pix) * p.estride] : 0.0f;
         }
       }
+      }
     };
 
     const int tstep = C::ACC_SETS * gridDim.x;
@@ -759,7 +780,7 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
     // previous chunk was finishing), stage and store, then start loading the
     // next chunk's operand values into `ecur`. Returns false when the
     // pipeline failed.
-    auto step = [&](float(&ecur)[32]) -> bool {
+    auto step = [&](float(&ecur)[NE]) -> bool {
       if (j == 0) {
         bool ok = mbar_wait(&acc_full[set], use & 1, vabort);
         ok = __all_sync(0xffffffffu, ok);
@@ -779,21 +800,37 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
       for (int h = 0; h < 2; ++h) {
         float v[16], x[16], e[16];
         tmem_ld16x2(tcol + h * 16, tcol + N + h * 16, v, x);
+        // The two regions' sum and the bias: paired adds where the registers
+        // allow (no second operand held), scalar adds otherwise; the same
+        // roundings either way.
+        if constexpr (E) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] += x[i];
+          for (int i = 0; i < 16; ++i) v[i] += x[i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) f2_add_to(v[i], v[i + 1], x[i], x[i + 1]);
+        }
         if (p.bias) {
           const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0 + j * 32 + h * 16);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const float4 b = __ldg(b4 + i);
-            v[4 * i] += b.x;
-            v[4 * i + 1] += b.y;
-            v[4 * i + 2] += b.z;
-            v[4 * i + 3] += b.w;
+            if constexpr (E) {
+              v[4 * i] += b.x;
+              v[4 * i + 1] += b.y;
+              v[4 * i + 2] += b.z;
+              v[4 * i + 3] += b.w;
+            } else {
+              f2_add_to(v[4 * i], v[4 * i + 1], b.x, b.y);
+              f2_add_to(v[4 * i + 2], v[4 * i + 3], b.z, b.w);
+            }
           }
         }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) e[i] = ecur[h * 16 + i];
+        for (int i = 0; i < 16; ++i) {
+          if constexpr (E) e[i] = ecur[h * 16 + i];
+          else e[i] = 0.0f;
+        }
         epi_apply(p.epi, v, e, p.slope);
         if (!GATE && MODE != MODE_CONVT && p.st_out[0]) {
           const int colh = n0 + j * 32 + h * 16;
@@ -915,14 +952,14 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
         }
       }
       if (++j == N / 32) j = 0, t += tstep;
-      if (has_e && t < p.tiles) load_e(t, j, ecur);
+      if (E && t < p.tiles) load_e(t, j, ecur);
       return true;
     };
 
-    float e[32];
+    float e[NE];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) e[i] = 0.0f;
-    if (has_e && t < p.tiles) load_e(t, 0, e);
+    for (int i = 0; i < NE; ++i) e[i] = 0.0f;
+    if (E && t < p.tiles) load_e(t, 0, e);
     while (t < p.tiles && step(e)) {
     }
     if (lane == 0) bulk_wait<0>();

@@ -122,7 +122,7 @@ def roofline(family, flops, nbytes, seconds, hbm_gbs, tf32_tflops):
     multiply-add, at the TF32 dense rate) takes longer; `frac` is the
     family's attainable time over its measured time, i.e. achieved / peak on
     that bound. Families that are not contractions are HBM-bound."""
-    base = family.split("+")[0].split("(")[0]
+    base = family.split()[0].split("+")[0].split("(")[0]
     issued = flops * (TF32_PRODUCTS if base in TENSOR_KINDS else 0)
     t_mem = nbytes / (hbm_gbs * 1e9)
     t_tc = issued / (tf32_tflops * 1e12) if issued else 0.0

@@ -77,3 +77,38 @@ def test_gelu_polynomial_special_values():
     with np.errstate(invalid="ignore", over="ignore"):
         g = gelu_device(x, c)
     assert g[0] == np.inf and g[1] == 0.0 and np.isnan(g[2]) and g[3] == 0.0
+
+
+def paired_coefficients():
+    text = open(SRC).read()
+    m = re.search(r"kGeluRw\[(\d+)\]\s*=\s*\{([^}]*)\}", text)
+    assert m, "kGeluRw not found in gpu_common.cuh"
+    return [np.float32(v.strip().rstrip("f")) for v in m.group(2).split(",") if v.strip()]
+
+
+def gelu_device_paired(x, cw):
+    """gelu_f2's evaluation: Horner over w = -min(|x|, 5.6) with kGeluRw."""
+    x = x.astype(np.float32)
+    w = np.maximum(-np.abs(x), np.float32(-5.6))
+    p = np.full_like(x, cw[-1])
+    for k in range(len(cw) - 2, -1, -1):
+        p = fma32(p, w, np.full_like(x, cw[k]))
+    with np.errstate(over="ignore"):
+        a = (x * np.float32(-0.72134752)).astype(np.float32)
+        a = (a * x).astype(np.float32)
+    e = np.exp2(a.astype(np.float64)).astype(np.float32)
+    s = (w * e).astype(np.float32)
+    return fma32(s, p, np.maximum(x, np.float32(0)))
+
+
+def test_paired_gelu_is_bit_identical_to_the_scalar_one():
+    """The epilogue's paired GELU (gelu_f2) must give exactly gelu_f's bits,
+    so a fused GELU step still equals the unfused op bit for bit."""
+    c, cw = coefficients(), paired_coefficients()
+    assert len(c) == len(cw)
+    for k in range(len(c)):
+        assert cw[k] == np.float32((-1) ** k) * c[k], k
+    xs = np.concatenate([np.linspace(-12, 12, 600_001, dtype=np.float64),
+                         np.array([5.6, -5.6, 0.0, -0.0, 1e30, -1e30, 3e-39, -3e-39])]).astype(np.float32)
+    a, b = gelu_device(xs, c), gelu_device_paired(xs, cw)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
