@@ -638,11 +638,11 @@ def main():
     ap.add_argument("--height", type=int, default=IMG_H, help="--timeline only: image height")
     ap.add_argument("--width", type=int, default=IMG_W, help="--timeline only: image width")
     args = ap.parse_args()
+    if args.timeline:
+        return run_timeline(args)  # a census, not a timed number: any warm-up count
     if args.warmup < 3:
         log("bench: raising --warmup to 3")
         args.warmup = 3
-    if args.timeline:
-        return run_timeline(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_native(args)
