@@ -943,7 +943,62 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
       int64_t wo = cached(g, o.w, WT_KTAP, ktap), bo = raw(o.bias);
       int h = o.h, wd = o.wd;
       if (ks == 3 && (ci == 3 || co == 3)) {
-        // The image-facing convs (3 input or 3 output channels).
+        // The image-facing convs (3 input or 3 output channels). Their
+        // weights travel as a kernel parameter (a constant bank): per
+        // 32-output-channel chunk for c_in = 3, whole for c_out = 3 with
+        // c_in in {32, 64, 128}.
+        const std::vector<float> wk = ktap(), bk = W(o.bias);
+        const bool cout_c = co == 3 && ci == 32 || co == 3 && ci == 64 || co == 3 && ci == 128;
+        if (ci == 3) {
+          std::vector<Cin3Weights> chunks(size_t((co + 31) / 32));
+          for (size_t k = 0; k < chunks.size(); ++k) {
+            Cin3Weights& c = chunks[k];
+            memset(&c, 0, sizeof(c));
+            for (int oo = 0; oo < 32 && int(k) * 32 + oo < co; ++oo) {
+              const int oc = int(k) * 32 + oo;
+              for (int t = 0; t < 27; ++t) c.w[oo * 27 + t] = wk[size_t(oc) * 27 + t];
+              c.b[oo] = bk.empty() ? 0.0f : bk[size_t(oc)];
+            }
+          }
+          st.kernels = int(chunks.size());
+          st.run = [G, L, dst, src, co, h, wd, chunks](cudaStream_t s) {
+            View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
+            for (size_t k = 0; k < chunks.size(); ++k)
+              conv3x3_cin3c_kernel<<<unsigned((h * wd + 127) / 128), 128, 0, s>>>(
+                  h, wd, std::min(32, co - int(k) * 32), x.ptr, int(x.stride), d.ptr + 32 * k, int(d.stride),
+                  chunks[k]);
+          };
+          break;
+        }
+        if (cout_c) {
+          auto fill = [&](auto& c) {
+            memset(&c, 0, sizeof(c));
+            for (size_t i = 0; i < wk.size(); ++i) c.w[i] = wk[i];
+            for (int oc = 0; oc < 3; ++oc) c.b[oc] = bk.empty() ? 0.0f : bk[size_t(oc)];
+          };
+          auto c32 = std::make_shared<Cout3Weights<32>>();
+          auto c64 = std::make_shared<Cout3Weights<64>>();
+          auto c128 = std::make_shared<Cout3Weights<128>>();
+          if (ci == 32) fill(*c32);
+          if (ci == 64) fill(*c64);
+          if (ci == 128) fill(*c128);
+          st.run = [G, L, P, dst, src, wo, bo, ci, h, wd, c32, c64, c128](cudaStream_t s) {
+            View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
+            dim3 grid(unsigned((wd + 15) / 16), unsigned((h + 15) / 16));
+            if (!aligned4(x)) {
+              conv3x3_cout3_kernel<<<grid, 256, 0, s>>>(h, wd, ci, x.ptr, int(x.stride), P(wo), P(bo), d.ptr,
+                                                        int(d.stride));
+            } else if (ci == 32) {
+              conv3x3_cout3c_kernel<32><<<grid, 256, 0, s>>>(h, wd, x.ptr, int(x.stride), d.ptr, int(d.stride), *c32);
+            } else if (ci == 64) {
+              conv3x3_cout3c_kernel<64><<<grid, 256, 0, s>>>(h, wd, x.ptr, int(x.stride), d.ptr, int(d.stride), *c64);
+            } else {
+              conv3x3_cout3c_kernel<128><<<grid, 256, 0, s>>>(h, wd, x.ptr, int(x.stride), d.ptr, int(d.stride),
+                                                              *c128);
+            }
+          };
+          break;
+        }
         st.run = [G, L, P, dst, src, wo, bo, ci, co, h, wd](cudaStream_t s) {
           View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
           if (ci == 3) {

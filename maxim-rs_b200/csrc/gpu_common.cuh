@@ -99,10 +99,26 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
+}
+// The sum t + b where t is the result of a paired multiply. Written as the
+// paired add, it is fused with that multiply by the assembler (measured on
+// B200: mul.rn.f32x2 followed by add.rn.f32x2 comes out as one fused
+// multiply-add, its rounding differing from the two roundings in about a
+// quarter of cases, whatever the contraction flag says). A fused
+// multiply-add of t by a one the assembler cannot see is exactly one rounded
+// addition (t * 1 is exact), so it keeps the separate rounding.
+static __constant__ float kOnePair[2] = {1.0f, 1.0f};
+__device__ __forceinline__ uint64_t f2_add_after_mul(uint64_t t, uint64_t b) {
+  return f2_fma(t, *reinterpret_cast<const uint64_t*>(kOnePair), b);
 }
 // a += b and c += d as one paired add.
 __device__ __forceinline__ void f2_add_to(float& a, float& c, float b, float d) {

@@ -115,5 +115,116 @@ __global__ void __launch_bounds__(256) conv3x3_cout3_kernel(int h, int wd, int c
   }
 }
 
+// The same two convs with their weights passed by value as a kernel
+// parameter: the parameter space is a constant bank, so each multiply-add
+// takes its weight as a constant operand and no instruction loads it. The
+// loops over weights are fully unrolled (their indices are compile-time),
+// and every output's sum runs in the same order as in the kernels above, so
+// the results are theirs bit for bit.
+//
+// c_in == 3, one 32-output-channel chunk per launch (weights [o][tap][c],
+// 27 per output): one output pixel per thread, all 32 outputs.
+struct Cin3Weights {
+  float w[32 * 27];
+  float b[32];
+};
+__global__ void __launch_bounds__(128) conv3x3_cin3c_kernel(int h, int wd, int n, const float* __restrict__ x, int sx,
+                                                            float* __restrict__ y, int sy,
+                                                            const __grid_constant__ Cin3Weights cw) {
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= h * wd) return;
+  const int py = p / wd, px = p - py * wd;
+  float in[27];
+#pragma unroll
+  for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx) {
+      const int iy = py + ky - 1, ix = px + kx - 1;
+      const bool ok = iy >= 0 && iy < h && ix >= 0 && ix < wd;
+      const float* s = x + size_t(iy * wd + ix) * sx;
+#pragma unroll
+      for (int c = 0; c < 3; ++c) in[(ky * 3 + kx) * 3 + c] = ok ? __ldg(s + c) : 0.0f;
+    }
+  float acc[32];
+#pragma unroll
+  for (int o = 0; o < 32; ++o) acc[o] = cw.b[o];
+#pragma unroll
+  for (int k = 0; k < 27; ++k)
+#pragma unroll
+    for (int o = 0; o < 32; ++o) acc[o] = fmaf(in[k], cw.w[o * 27 + k], acc[o]);
+  float* d = y + size_t(p) * sy;
+  if (n == 32 && (reinterpret_cast<uintptr_t>(d) % 16) == 0) {
+#pragma unroll
+    for (int o = 0; o < 32; o += 4) *reinterpret_cast<float4*>(d + o) = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
+  } else {
+#pragma unroll
+    for (int o = 0; o < 32; ++o)
+      if (o < n) d[o] = acc[o];
+  }
+}
+
+// c_out == 3 with CI input channels (a multiple of 32; weights [o][tap][ci]):
+// a 16x16 block of output pixels per 256-thread block, input channels in
+// chunks of 32 through a shared halo tile read as float4s (rows padded to
+// 36 floats: the eight float4 reads of a quarter-warp hit distinct banks).
+template <int CI>
+struct Cout3Weights {
+  float w[3 * 9 * CI];
+  float b[3];
+};
+template <int CI>
+__global__ void __launch_bounds__(256) conv3x3_cout3c_kernel(int h, int wd, const float* __restrict__ x, int sx,
+                                                             float* __restrict__ y, int sy,
+                                                             const __grid_constant__ Cout3Weights<CI> cw) {
+  constexpr int T = 16, HALO = T + 2, R = 36;
+  __shared__ float4 tile[HALO * HALO * R / 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int x0 = blockIdx.x * T, y0 = blockIdx.y * T;
+  float a0 = cw.b[0], a1 = cw.b[1], a2 = cw.b[2];
+#pragma unroll
+  for (int cb = 0; cb < CI; cb += 32) {
+    if (cb) __syncthreads();
+    for (int i = threadIdx.x; i < HALO * HALO * 8; i += 256) {
+      const int pix = i >> 3, c4 = i & 7;
+      const int hy = pix / HALO, hx = pix - hy * HALO;
+      const int iy = y0 + hy - 1, ix = x0 + hx - 1;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (iy >= 0 && iy < h && ix >= 0 && ix < wd)
+        v = __ldg(reinterpret_cast<const float4*>(x + size_t(iy * wd + ix) * sx + cb) + c4);
+      tile[pix * (R / 4) + c4] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < 9; ++t) {
+      const int ky = t / 3, kx = t - ky * 3;
+      const float4* s = tile + ((ty + ky) * HALO + tx + kx) * (R / 4);
+#pragma unroll
+      for (int c4 = 0; c4 < 8; ++c4) {
+        const float4 v = s[c4];
+        const int c = cb + 4 * c4;
+        a0 = fmaf(v.x, cw.w[(0 * 9 + t) * CI + c], a0);
+        a1 = fmaf(v.x, cw.w[(1 * 9 + t) * CI + c], a1);
+        a2 = fmaf(v.x, cw.w[(2 * 9 + t) * CI + c], a2);
+        a0 = fmaf(v.y, cw.w[(0 * 9 + t) * CI + c + 1], a0);
+        a1 = fmaf(v.y, cw.w[(1 * 9 + t) * CI + c + 1], a1);
+        a2 = fmaf(v.y, cw.w[(2 * 9 + t) * CI + c + 1], a2);
+        a0 = fmaf(v.z, cw.w[(0 * 9 + t) * CI + c + 2], a0);
+        a1 = fmaf(v.z, cw.w[(1 * 9 + t) * CI + c + 2], a1);
+        a2 = fmaf(v.z, cw.w[(2 * 9 + t) * CI + c + 2], a2);
+        a0 = fmaf(v.w, cw.w[(0 * 9 + t) * CI + c + 3], a0);
+        a1 = fmaf(v.w, cw.w[(1 * 9 + t) * CI + c + 3], a1);
+        a2 = fmaf(v.w, cw.w[(2 * 9 + t) * CI + c + 3], a2);
+      }
+    }
+  }
+  const int py = y0 + ty, px = x0 + tx;
+  if (py < h && px < wd) {
+    float* d = y + size_t(py * wd + px) * sy;
+    d[0] = a0;
+    d[1] = a1;
+    d[2] = a2;
+  }
+}
+
 }  // namespace
 }  // namespace mx

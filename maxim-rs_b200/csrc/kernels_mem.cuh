@@ -236,11 +236,20 @@ struct TapTable4 {
   const float* wrcp;
 };
 
+// acc += w * v per channel, the product and the sum each rounded (no fused
+// multiply-add).
 __device__ __forceinline__ void tap_acc(float4& acc, float w, float4 v) {
   acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
   acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
   acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
   acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+}
+// The same as paired f32x2 instructions (the same roundings, half the
+// instructions), where the registers allow.
+__device__ __forceinline__ void tap_acc_x2(float4& acc, float w, float4 v) {
+  const uint64_t ww = f2_pack(w, w);
+  f2_unpack(f2_add_after_mul(f2_mul(ww, f2_pack(v.x, v.y)), f2_pack(acc.x, acc.y)), acc.x, acc.y);
+  f2_unpack(f2_add_after_mul(f2_mul(ww, f2_pack(v.z, v.w)), f2_pack(acc.z, acc.w)), acc.z, acc.w);
 }
 __device__ __forceinline__ float4 tap_norm(float4 acc, float sm, float rcp) {
   if (rcp != 0.0f)
@@ -295,17 +304,40 @@ __global__ void __launch_bounds__(256) resize_hv4_kernel(int lg4, int win, int w
                                                          TapTable4 ty, const float* __restrict__ src, int ss,
                                                          float* __restrict__ dst, int sd) {
   __shared__ float4 rows[kRzRows][kRzTile / 4];
+  // The vertical taps of the CTA's output rows, read once by one warp:
+  // first input row (relative to r_lo), tap count, weights, sum, reciprocal.
+  __shared__ int s_j[kRzTY], s_n[kRzTY];
+  __shared__ float s_w[kRzTY][kRzTaps], s_sum[kRzTY], s_rcp[kRzTY];
+  __shared__ int s_rlo, s_nrows;
   const int f = threadIdx.x;  // float4 of a strip row: column f >> lg4, channels 4 (f & (c4 - 1))
   const int xo = blockIdx.x * ((kRzTile / 4) >> lg4) + (f >> lg4), c = (f & ((1 << lg4) - 1)) * 4;
   const bool xin = xo < wout;
-  const int y0 = blockIdx.y * kRzTY, yend = min(y0 + kRzTY, hout);
-  int r_lo = 1 << 30, r_hi = -1;
-  for (int yo = y0; yo < yend; ++yo) {
-    const int j = __ldg(ty.j0 + yo);
-    r_lo = min(r_lo, j);
-    r_hi = max(r_hi, j + __ldg(ty.cnt + yo) - 1);
+  const int y0 = blockIdx.y * kRzTY, ny = min(kRzTY, hout - y0);
+  if (f < 32) {
+    int j = 1 << 30, hi = -1;
+    if (f < ny) {
+      const int yo = y0 + f;
+      j = __ldg(ty.j0 + yo);
+      const int n = __ldg(ty.cnt + yo), w0 = __ldg(ty.w0 + yo);
+      hi = j + n - 1;
+      s_n[f] = n;
+#pragma unroll
+      for (int k = 0; k < kRzTaps; ++k) s_w[f][k] = k < n ? __ldg(ty.w + w0 + k) : 0.0f;
+      s_sum[f] = __ldg(ty.wsum + yo);
+      s_rcp[f] = __ldg(ty.wrcp + yo);
+    }
+    int lo = j;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+      hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    if (f < ny) s_j[f] = j - lo;
+    if (f == 0) s_rlo = lo, s_nrows = min(hi - lo + 1, kRzRows);
   }
-  const int nrows = min(r_hi - r_lo + 1, kRzRows);
+  __syncthreads();
+  const int r_lo = s_rlo, nrows = s_nrows;
+  static_assert(kRzTaps == 3, "the vertical pass is written for three taps");
   if (xin) {
     // Four input rows at a time, all their taps' loads issued before any is
     // used (the loads, not the arithmetic, are what a thread waits on).
@@ -314,14 +346,16 @@ __global__ void __launch_bounds__(256) resize_hv4_kernel(int lg4, int win, int w
     float w[kRzTaps];
 #pragma unroll
     for (int k = 0; k < kRzTaps; ++k) w[k] = k < n ? __ldg(tx.w + w0 + k) : 0.0f;
+    const float* base = src + (size_t(r_lo) * win + j0) * ss + c;
+    const size_t rstep = size_t(win) * ss;
     for (int r0 = 0; r0 < nrows; r0 += 4) {
       float4 v[4][kRzTaps];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const float* s = src + (size_t(r_lo + min(r0 + q, nrows - 1)) * win + j0) * ss + c;
+        const float* s = base + size_t(min(r0 + q, nrows - 1)) * rstep;
 #pragma unroll
         for (int k = 0; k < kRzTaps; ++k)
-          v[q][k] = k < n ? *reinterpret_cast<const float4*>(s + size_t(k) * ss) : make_float4(0.f, 0.f, 0.f, 0.f);
+          v[q][k] = k < n ? *reinterpret_cast<const float4*>(s + k * ss) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -329,22 +363,36 @@ __global__ void __launch_bounds__(256) resize_hv4_kernel(int lg4, int win, int w
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int k = 0; k < kRzTaps; ++k)
-          if (k < n) tap_acc(acc, w[k], v[q][k]);
+          if (k < n) tap_acc_x2(acc, w[k], v[q][k]);
         rows[r0 + q][f] = tap_norm(acc, sm, rc);
       }
     }
   }
   __syncthreads();
-  if (!xin) return;
-  for (int yo = y0; yo < yend; ++yo) {
-    const int j0 = __ldg(ty.j0 + yo) - r_lo, w0 = __ldg(ty.w0 + yo), n = __ldg(ty.cnt + yo);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < n; ++k) {
-      const int r = j0 + k;
-      if (r < nrows) tap_acc(acc, __ldg(ty.w + w0 + k), rows[r][f]);
+  // Vertical pass, one output row per warp at a time: the row's taps are
+  // read once into registers and serve all 256 float4s of the strip row
+  // (eight per lane), and each warp-wide store covers consecutive floats.
+  const int warp = f >> 5, lane = f & 31;
+  const int xs = blockIdx.x * ((kRzTile / 4) >> lg4);  // the strip's first column
+  const int cmask = (1 << lg4) - 1;
+  for (int yy = warp; yy < ny; yy += 8) {
+    const int j0 = s_j[yy], n = s_n[yy];
+    const float w0 = s_w[yy][0], w1 = s_w[yy][1], w2 = s_w[yy][2], sm = s_sum[yy], rc = s_rcp[yy];
+    const bool t0 = n > 0 && j0 < nrows, t1 = n > 1 && j0 + 1 < nrows, t2 = n > 2 && j0 + 2 < nrows;
+    const float4* r0 = rows[min(j0, kRzRows - 1)];
+    const float4* r1 = rows[min(j0 + 1, kRzRows - 1)];
+    const float4* r2 = rows[min(j0 + 2, kRzRows - 1)];
+    float* drow = dst + size_t(y0 + yy) * wout * sd;
+#pragma unroll 4
+    for (int g = lane; g < kRzTile / 4; g += 32) {
+      const int x = xs + (g >> lg4);
+      if (x >= wout) break;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (t0) tap_acc_x2(acc, w0, r0[g]);
+      if (t1) tap_acc_x2(acc, w1, r1[g]);
+      if (t2) tap_acc_x2(acc, w2, r2[g]);
+      *reinterpret_cast<float4*>(drow + size_t(x) * sd + (g & cmask) * 4) = tap_norm(acc, sm, rc);
     }
-    *reinterpret_cast<float4*>(dst + (size_t(yo) * wout + xo) * sd + c) =
-        tap_norm(acc, __ldg(ty.wsum + yo), __ldg(ty.wrcp + yo));
   }
 }
 

@@ -535,13 +535,18 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
     // (x - m) * rstd * scale + bias, in the LayerNorm kernel's exact order,
     // over 4 channels from ch (a multiple of 4; every thread reads the same
     // scale and bias, so the read-only cache serves them).
+    // ((v - m) * rs) * w + b per channel, every operation rounded on its own
+    // (the LayerNorm kernel's order), as paired f32x2 instructions.
     auto ln_apply4 = [&](float4 v, float m, float rs, int ch) {
       const float4 w = __ldg(reinterpret_cast<const float4*>(p.ln_scale + ch));
       const float4 b = __ldg(reinterpret_cast<const float4*>(p.ln_bias + ch));
-      v.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, m), rs), w.x), b.x);
-      v.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, m), rs), w.y), b.y);
-      v.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, m), rs), w.z), b.z);
-      v.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, m), rs), w.w), b.w);
+      const uint64_t mm = f2_pack(m, m), rr = f2_pack(rs, rs);
+      f2_unpack(f2_add_after_mul(f2_mul(f2_mul(f2_sub(f2_pack(v.x, v.y), mm), rr), f2_pack(w.x, w.y)),
+                                 f2_pack(b.x, b.y)),
+                v.x, v.y);
+      f2_unpack(f2_add_after_mul(f2_mul(f2_mul(f2_sub(f2_pack(v.z, v.w), mm), rr), f2_pack(w.z, w.w)),
+                                 f2_pack(b.z, b.w)),
+                v.z, v.w);
       return v;
     };
     // In the 1x1 instances a thread's rows are the same for every k-block
@@ -553,6 +558,8 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
     constexpr bool LN_AHEAD = MODE == MODE_CONV1;
     constexpr int LN_ROWS = TMEM_A ? 1 : 8;
     float2 st_next[LN_ROWS], st_cur[LN_ROWS];
+#pragma unroll
+    for (int j = 0; j < LN_ROWS; ++j) st_next[j] = st_cur[j] = make_float2(0.0f, 0.0f);
     uint32_t ln_next = 0, ln_cur = 0;
     auto fetch_stats = [&](int tn) {
       ln_next = 0;
@@ -634,10 +641,17 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
               float4* p4 = reinterpret_cast<float4*>(arow + ((cc ^ (r & 7)) << 4));
               float4 v = *p4;
               const float4 u = ln_apply4(v, lm, lr, cb * 32 + 4 * cc);
-              v.x = ln ? u.x : v.x;
-              v.y = ln ? u.y : v.y;
-              v.z = ln ? u.z : v.z;
-              v.w = ln ? u.w : v.w;
+              if (MODE == MODE_CONV1) {
+                // A row past the last pixel only feeds an output row the
+                // store clips, so it needs no selection (its statistics
+                // are finite: zero, or an earlier row's).
+                v = u;
+              } else {
+                v.x = ln ? u.x : v.x;
+                v.y = ln ? u.y : v.y;
+                v.z = ln ? u.z : v.z;
+                v.w = ln ? u.w : v.w;
+              }
               *p4 = v;
               lo[4 * c] = tf32_residual(v.x);
               lo[4 * c + 1] = tf32_residual(v.y);
@@ -684,10 +698,14 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
             const int f = tid + i, r = f >> 3, ch = cb * 32 + (((f & 7) ^ (r & 7)) << 2);
             const bool on = lns[i >> 7];
             const float4 u = ln_apply4(v, lms[i >> 7], lrs[i >> 7], ch);
-            v.x = on ? u.x : v.x;
-            v.y = on ? u.y : v.y;
-            v.z = on ? u.z : v.z;
-            v.w = on ? u.w : v.w;
+            if (MODE == MODE_CONV1) {
+              v = u;  // as above: rows past the last pixel feed clipped outputs
+            } else {
+              v.x = on ? u.x : v.x;
+              v.y = on ? u.y : v.y;
+              v.z = on ? u.z : v.z;
+              v.w = on ? u.w : v.w;
+            }
             a[i] = v;
           }
           l.x = tf32_residual(v.x);

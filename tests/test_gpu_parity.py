@@ -204,3 +204,42 @@ def test_config2_s3_600x400_parity(mx, synth, oracle, checkpoint, gain):
     if gain == 0.5:
         assert psnr(cpu, out, peak=1.0) >= 50.0
     assert lsb_fraction(cpu, out) >= 0.999
+
+
+# Ops whose device kernels follow the CPU path's operation order exactly
+# (no fused multiply-add, the same summation order), so that from the same
+# input they must give the same bits: copies, elementwise add / multiply /
+# gate / leaky ReLU, the channel LayerNorm, channel scale, block
+# permutation, resize and nearest downsampling.
+EXACT_KINDS = {0: "copy", 1: "add", 2: "mul", 3: "gate_apply", 5: "lrelu", 7: "chan_ln", 9: "chan_scale",
+               15: "block_perm", 16: "resize", 17: "down_s"}
+
+
+def test_gpu_memory_bound_ops_are_bit_exact(mx, synth, oracle, checkpoint):
+    """For every op of those kinds in an S-1 walk at 256x320, hand the CPU
+    oracle the device's own inputs (read back from the GPU arena) and require
+    the device's output bit for bit."""
+    w = mx.Weights(checkpoint("S-1", 5, 0.5, True))
+    img = synth.image_uniform(synth.input_rng(5), 256, 320)
+    plan = mx.Plan(w, 256, 320)
+    gpu = mx.Gpu(plan)
+    gpu.begin(img)
+    arena = oracle.new_arena(plan, img)
+    seen, bad = {}, []
+    for i, op in enumerate(plan.ops()):
+        if op.kind in EXACT_KINDS:
+            for b in (op.src, op.src2):
+                if b >= 0:
+                    c, h, ww = plan.buf(b)
+                    o = plan.off(b)
+                    arena[o:o + c * h * ww] = gpu.read_buf(b).reshape(-1)
+            oracle.run_range(plan, arena, i, i + 1, threads=4)
+            gpu.step_op(i)
+            cpu, got = oracle.take(plan, arena, op.dst), gpu.read_buf(op.dst)
+            seen[EXACT_KINDS[op.kind]] = seen.get(EXACT_KINDS[op.kind], 0) + 1
+            if not np.array_equal(cpu.view(np.uint32), got.view(np.uint32)):
+                bad.append((i, EXACT_KINDS[op.kind], int((cpu.view(np.uint32) != got.view(np.uint32)).sum())))
+        else:
+            gpu.step_op(i)
+    assert {"resize", "chan_ln", "add", "copy", "block_perm"} <= set(seen), seen
+    assert not bad, bad[:10]
