@@ -138,6 +138,11 @@ int mx_device_count(int* count);
  * allocation and upload every weight in the kernels' layouts (resident, not
  * lazy). The plan is copied; the caller may free its view afterwards. */
 int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out);
+/* The same with a device-memory budget: the pass is refused, with the same
+ * message, when it needs more than budget_bytes even if the device has more
+ * free (a GPU shared with other work). 0 means the device's free memory. No
+ * counterpart in the reference. */
+int mx_gpu_new_budget(int device, const mx_plan* plan, int64_t budget_bytes, mx_gpu** out);
 void mx_gpu_free(mx_gpu* g);
 
 /* `Gpu::run` (src/exec_gpu.rs:196-229): input [3][H][W] host floats in,
@@ -152,6 +157,11 @@ int mx_gpu_upload_input(mx_gpu* g, const float* input);
 int mx_gpu_enqueue(mx_gpu* g);
 int mx_gpu_download_output(mx_gpu* g, float* output);
 int mx_gpu_sync(mx_gpu* g);
+/* The status of the passes finished so far, without waiting for the stream:
+ * MX_E_DEVICE when a kernel has recorded a pipeline failure (the record is
+ * then cleared), else MX_OK. For callers that wait on their own events and
+ * keep the next pass running meanwhile. */
+int mx_gpu_poll(mx_gpu* g);
 /* The same two copies from / to DEVICE memory of the handle's device (a
  * batch of images already resident in HBM): device-to-device, async. */
 int mx_gpu_upload_input_device(mx_gpu* g, const float* dev_input);
@@ -259,6 +269,59 @@ int mx_plan_schedule(const mx_plan* plan, mx_gpu_stats* stats, int32_t* primary,
  * (null for the legacy default stream); the call is asynchronous on it. */
 int mx_channel_mean_noalloc(const float* x, int64_t npix, int32_t c, int64_t pixel_stride, float* out,
                             void* stream);
+
+/* ------------------------------------------------------ the batch runner
+ * Independent images sharded round-robin over GPUs: one worker thread and
+ * one executor handle (arena, weights, stream, graph) per device, and no
+ * collective between them. The reference restores one image per process
+ * (src/main.rs:173-458); this is the multi-GPU batch mode built on group 1,
+ * with host-side failure handling:
+ *   - each worker has a status (mx_batch_workers);
+ *   - a device whose executor cannot be built (the pass does not fit its
+ *     memory, or its budget) is left out and the batch runs on the others;
+ *     mx_batch_new fails only when no device can take it;
+ *   - a worker that fails on an image is retired, and the images it had not
+ *     finished, the failing one included, go round-robin to the workers
+ *     still standing. An image no worker could restore keeps the status of
+ *     its last attempt in image_status, and mx_batch_run returns that error
+ *     (with a message naming the image and the device) - it does not hang:
+ *     the executors' device-side waits are bounded in time.
+ * The executor is pluggable: null means this library's GPU executor (the
+ * plan in `cfg`, copied per device; the caller may free it after
+ * mx_batch_new). A caller-supplied executor must return from every call;
+ * `open`, `run` and `close` run on the worker threads (one thread per
+ * handle at a time). */
+typedef struct mx_batch mx_batch;
+enum { MX_WORKER_READY = 0, MX_WORKER_FAILED = 1 };
+typedef struct mx_batch_worker {
+  int32_t device;      /* the device the worker drives */
+  int32_t state;       /* MX_WORKER_READY or MX_WORKER_FAILED */
+  int32_t error_code;  /* MX_OK, or the status that retired it */
+  int32_t images_done; /* images it restored in the last mx_batch_run */
+  double seconds;      /* its wall time in the last mx_batch_run */
+  char error[256];     /* the message behind error_code */
+} mx_batch_worker;
+typedef struct mx_batch_config {
+  const mx_plan* plan;       /* the plan every image runs (the GPU executor's) */
+  int64_t device_mem_budget; /* bytes a device's pass may use; 0: its free memory */
+} mx_batch_config;
+typedef struct mx_batch_executor {
+  void* ctx;
+  int (*open)(void* ctx, int32_t device, void** handle);
+  int (*run)(void* ctx, void* handle, const float* input, float* output);
+  void (*close)(void* ctx, void* handle);
+} mx_batch_executor;
+int mx_batch_new(const mx_batch_config* cfg, const int32_t* devices, int32_t n_devices,
+                 const mx_batch_executor* executor, mx_batch** out);
+/* Restore n_images: inputs[i] ([3][H][W] host floats, the plan's input) to
+ * outputs[i] (the plan's output shape); image i goes to the (i mod R)-th of
+ * the R ready workers. image_status (may be null) receives each image's
+ * MX_OK / MX_E_*. Synchronous. */
+int mx_batch_run(mx_batch* b, int32_t n_images, const float* const* inputs, float* const* outputs,
+                 int32_t* image_status);
+int32_t mx_batch_worker_count(const mx_batch* b);
+int mx_batch_workers(const mx_batch* b, mx_batch_worker* out, int32_t n);
+void mx_batch_free(mx_batch* b);
 
 /* ================================================= 2. the host contract ==== */
 

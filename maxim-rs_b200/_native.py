@@ -53,6 +53,25 @@ class mx_gpu_stats(ctypes.Structure):
                 ("perms_dropped", ctypes.c_int64), ("pass_arena_bytes", ctypes.c_int64)]
 
 
+class mx_batch_worker(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int32), ("state", ctypes.c_int32), ("error_code", ctypes.c_int32),
+                ("images_done", ctypes.c_int32), ("seconds", ctypes.c_double), ("error", ctypes.c_char * 256)]
+
+
+class mx_batch_config(ctypes.Structure):
+    _fields_ = [("plan", ctypes.POINTER(mx_plan)), ("device_mem_budget", ctypes.c_int64)]
+
+
+EXEC_OPEN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p))
+EXEC_RUN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_float),
+                            ctypes.POINTER(ctypes.c_float))
+EXEC_CLOSE = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_void_p)
+
+
+class mx_batch_executor(ctypes.Structure):
+    _fields_ = [("ctx", ctypes.c_void_p), ("open", EXEC_OPEN), ("run", EXEC_RUN), ("close", EXEC_CLOSE)]
+
+
 class mx_image(ctypes.Structure):
     _fields_ = [("c", ctypes.c_int32), ("h", ctypes.c_int32), ("w", ctypes.c_int32),
                 ("data", ctypes.POINTER(ctypes.c_float))]
@@ -77,6 +96,7 @@ _SIGS = {
     "mx_gpu_enqueue": (ctypes.c_int, [ctypes.c_void_p]),
     "mx_gpu_download_output": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "mx_gpu_sync": (ctypes.c_int, [ctypes.c_void_p]),
+    "mx_gpu_poll": (ctypes.c_int, [ctypes.c_void_p]),
     "mx_gpu_stream": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
     "mx_gpu_upload_input_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "mx_gpu_download_output_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
@@ -95,6 +115,15 @@ _SIGS = {
                                         ctypes.c_void_p, ctypes.c_int32]),
     "mx_channel_mean_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int64,
                                                ctypes.c_void_p, ctypes.c_void_p]),
+    "mx_gpu_new_budget": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(mx_plan), ctypes.c_int64,
+                                         ctypes.POINTER(ctypes.c_void_p)]),
+    "mx_batch_new": (ctypes.c_int, [ctypes.POINTER(mx_batch_config), ctypes.POINTER(ctypes.c_int32), ctypes.c_int32,
+                                    ctypes.POINTER(mx_batch_executor), ctypes.POINTER(ctypes.c_void_p)]),
+    "mx_batch_run": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p),
+                                    ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_int32)]),
+    "mx_batch_worker_count": (ctypes.c_int32, [ctypes.c_void_p]),
+    "mx_batch_workers": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(mx_batch_worker), ctypes.c_int32]),
+    "mx_batch_free": (None, [ctypes.c_void_p]),
     "mx_weights_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
     "mx_weights_free": (None, [ctypes.c_void_p]),
     "mx_weights_variant": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]),
@@ -372,6 +401,102 @@ class Gpu:
         fl = np.zeros(self.plan.n_ops, np.int32)
         check(lib().mx_gpu_schedule(self._h, _ptr(out), _ptr(fl), self.plan.n_ops), "schedule")
         return (out, fl) if flags else out
+
+
+class Batch:
+    """`mx_batch_*`: independent images round-robin over devices, one worker
+    thread and executor handle per device, with the runner's failure
+    handling (a device that cannot be built is left out; a worker that fails
+    is retired and its unfinished images go to the others).
+
+    By default the executor is this library's GPU executor for `plan`. A
+    Python `executor` may replace it: an object with `in_len` / `out_len`
+    (floats per image) and `open(device) -> handle`, `run(handle, x, y)`
+    (x, y float32 arrays; raise to fail) and `close(handle)`."""
+
+    def __init__(self, plan=None, devices=(0,), mem_budget=0, executor=None):
+        self._h = ctypes.c_void_p()
+        self.plan = plan
+        self._py = executor
+        cfg = mx_batch_config(plan.view if plan is not None else None, int(mem_budget))
+        devs = (ctypes.c_int32 * len(devices))(*devices)
+        ex = None
+        if executor is not None:
+            import itertools
+            import threading
+            self._handles, self._keys, self._mu = {}, itertools.count(1), threading.Lock()
+            ex = mx_batch_executor(None, EXEC_OPEN(self._open), EXEC_RUN(self._run), EXEC_CLOSE(self._close))
+            self._ex = ex  # the callbacks must outlive the batch
+            self.in_len, self.out_len = executor.in_len, executor.out_len
+        else:
+            c, h, w = plan.buf(plan.input)
+            self.in_len = c * h * w
+            self.out_shape = plan.buf(plan.output)
+            self.out_len = int(np.prod(self.out_shape))
+        check(lib().mx_batch_new(ctypes.byref(cfg), devs, len(devices), ctypes.byref(ex) if ex else None,
+                                 ctypes.byref(self._h)), "batch")
+
+    # Python-executor trampolines (run on the runner's worker threads).
+    def _open(self, ctx, device, handle):
+        try:
+            h = self._py.open(int(device))
+        except Exception:
+            return -1
+        with self._mu:
+            key = next(self._keys)
+            self._handles[key] = h
+        handle[0] = key
+        return 0
+
+    def _run(self, ctx, handle, x, y):
+        try:
+            xa = np.ctypeslib.as_array(x, shape=(self.in_len,))
+            ya = np.ctypeslib.as_array(y, shape=(self.out_len,))
+            self._py.run(self._handles[handle], xa, ya)
+        except Exception:
+            return -1
+        return 0
+
+    def _close(self, ctx, handle):
+        try:
+            self._py.close(self._handles.pop(handle))
+        except Exception:
+            pass
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().mx_batch_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def run(self, images, outs=None, raise_on_error=True):
+        """Restore every image; returns (outputs, per-image status codes)."""
+        xs = [np.ascontiguousarray(im, dtype=np.float32).reshape(-1) for im in images]
+        for x in xs:
+            if x.size != self.in_len:
+                raise ValueError("an image has %d values, the batch's input %d" % (x.size, self.in_len))
+        if outs is None:
+            shape = getattr(self, "out_shape", (self.out_len,))
+            outs = [np.empty(shape, np.float32) for _ in xs]
+        n = len(xs)
+        ip = (ctypes.c_void_p * n)(*[x.ctypes.data for x in xs])
+        op = (ctypes.c_void_p * n)(*[o.ctypes.data for o in outs])
+        st = (ctypes.c_int32 * n)()
+        rc = lib().mx_batch_run(self._h, n, ip, op, st)
+        status = [int(v) for v in st]
+        if rc != MX_OK and raise_on_error:
+            raise MaximError(rc, "batch: " + last_error())
+        return outs, status
+
+    def workers(self):
+        n = lib().mx_batch_worker_count(self._h)
+        arr = (mx_batch_worker * n)()
+        check(lib().mx_batch_workers(self._h, arr, n), "batch workers")
+        return [{"device": w.device, "state": "ready" if w.state == 0 else "failed", "error_code": w.error_code,
+                 "images_done": w.images_done, "seconds": w.seconds, "error": w.error.decode(errors="replace")}
+                for w in arr]
 
 
 def _stats_dict(s):

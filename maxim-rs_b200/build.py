@@ -34,7 +34,9 @@ ORACLE_BUILD = os.path.join(ORACLE, "_build")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CXXFLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wextra", "-Wno-unused-parameter", "-I" + INC, "-I" + CSRC]
+CUDA_INC = os.path.join(os.path.dirname(os.path.dirname(NVCC)), "include")
+CXXFLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wextra", "-Wno-unused-parameter", "-I" + INC, "-I" + CSRC,
+            "-I" + CUDA_INC]
 NVFLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I" + INC, "-I" + CSRC,
                   "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
 

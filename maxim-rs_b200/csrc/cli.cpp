@@ -2,11 +2,15 @@
 // (the reference's CLI, src/main.rs:17-156, over this library's C ABI).
 //
 //     maxim -m maxim-s3.safetensors -i in.png -o out.png
+//     maxim -m maxim-s3.safetensors --batch in_dir out_dir [--devices 0,1,..|all]
 //
 // The plan is built for the padded input shape (reflect pad to a multiple of
 // 64, src/image.rs:171-207), run on the GPU executor, and the result is
 // cropped back the way the reference eval script does. There is no CPU
 // backend here: a missing driver is an error, never a silent fallback.
+#include <dirent.h>
+
+#include <algorithm>
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
@@ -35,6 +39,9 @@ const char* kVersion = "0.1.0";
           "        --gpu-index <n>   which CUDA device (default 0)\n"
           "        --profile         per-op-kind device time of the pass\n"
           "        --factor <n>      pad to a multiple of n (default 64, as the reference)\n"
+          "        --batch <in> <out>  restore every .png of directory <in> into <out>, images\n"
+          "                          round-robin over the devices (one worker per GPU)\n"
+          "        --devices <list>  the batch's CUDA devices: comma-separated, or all (default)\n"
           "    -q, --quiet           no progress output\n"
           "    -h, --help            this text\n"
           "    -V, --version         print the version\n",
@@ -61,6 +68,115 @@ std::vector<uint8_t> read_all(FILE* f) {
   return v;
 }
 
+// `--batch`: every PNG of a directory, grouped by padded shape (one plan
+// per shape), each group through the batch runner over the chosen devices.
+// A file that cannot be read or padded is reported and skipped; an image the
+// runner could not restore is reported; the others are written. Exit status
+// 1 if anything failed.
+int run_batch(mx_weights* w, const std::string& in_dir, const std::string& out_dir, std::vector<int32_t> devices,
+              int factor, bool quiet) {
+  std::vector<std::string> names;
+  if (DIR* d = opendir(in_dir.c_str())) {
+    while (dirent* e = readdir(d)) {
+      std::string n = e->d_name;
+      if (n.size() > 4 && n.compare(n.size() - 4, 4, ".png") == 0) names.push_back(n);
+    }
+    closedir(d);
+  } else {
+    fprintf(stderr, "maxim: cannot read directory %s\n", in_dir.c_str());
+    return 1;
+  }
+  std::sort(names.begin(), names.end());
+  if (devices.empty()) {
+    int n = 0;
+    if (mx_device_count(&n) != MX_OK || n == 0) return fail("cuda");
+    for (int i = 0; i < n; ++i) devices.push_back(i);
+  }
+  struct Item {
+    std::string name;
+    mx_image img{}, padded{};
+    int32_t eh = 0, ew = 0;
+  };
+  std::map<std::pair<int32_t, int32_t>, std::vector<Item>> groups;
+  int failed = 0, written = 0;
+  for (const auto& n : names) {
+    Item it;
+    it.name = n;
+    if (mx_png_read((in_dir + "/" + n).c_str(), &it.img) != MX_OK ||
+        mx_preprocess(&it.img, factor, &it.padded, &it.eh, &it.ew) != MX_OK) {
+      fprintf(stderr, "maxim: %s: %s (skipped)\n", n.c_str(), last_error().c_str());
+      mx_image_free(&it.img);
+      ++failed;
+      continue;
+    }
+    groups[{it.padded.h, it.padded.w}].push_back(it);
+  }
+  for (auto& kv : groups) {
+    auto& items = kv.second;
+    mx_plan_handle* plan = nullptr;
+    if (mx_plan_build(w, kv.first.first, kv.first.second, 0, &plan) != MX_OK) {
+      fprintf(stderr, "maxim: plan for %dx%d: %s\n", kv.first.second, kv.first.first, last_error().c_str());
+      failed += int(items.size());
+      continue;
+    }
+    const mx_plan* pv = mx_plan_view(plan);
+    mx_batch_config cfg{pv, 0};
+    mx_batch* b = nullptr;
+    auto t0 = std::chrono::steady_clock::now();
+    if (mx_batch_new(&cfg, devices.data(), int32_t(devices.size()), nullptr, &b) != MX_OK) {
+      fprintf(stderr, "maxim: %dx%d: %s\n", kv.first.second, kv.first.first, last_error().c_str());
+      failed += int(items.size());
+      mx_plan_free(plan);
+      continue;
+    }
+    const mx_buf& ob = pv->bufs[pv->output];
+    const size_t n_out = size_t(ob.c * ob.h * ob.w);
+    std::vector<std::vector<float>> outs(items.size(), std::vector<float>(n_out));
+    std::vector<const float*> ins;
+    std::vector<float*> outp;
+    for (size_t i = 0; i < items.size(); ++i) ins.push_back(items[i].padded.data), outp.push_back(outs[i].data());
+    std::vector<int32_t> st(items.size(), 0);
+    auto t1 = std::chrono::steady_clock::now();
+    const int rc = mx_batch_run(b, int32_t(items.size()), ins.data(), outp.data(), st.data());
+    auto t2 = std::chrono::steady_clock::now();
+    if (rc != MX_OK) fprintf(stderr, "maxim: %s\n", last_error().c_str());
+    std::vector<mx_batch_worker> ws(size_t(mx_batch_worker_count(b)));
+    mx_batch_workers(b, ws.data(), int32_t(ws.size()));
+    if (!quiet) {
+      fprintf(stderr, "maxim: %zu image(s) at %dx%d on %zu device(s): setup %.2fs, run %.2fs\n", items.size(),
+              kv.first.second, kv.first.first, ws.size(), std::chrono::duration<double>(t1 - t0).count(),
+              std::chrono::duration<double>(t2 - t1).count());
+      for (const auto& x : ws)
+        fprintf(stderr, "maxim:   device %d: %s, %d image(s)%s%s\n", x.device,
+                x.state == MX_WORKER_READY ? "ready" : "failed", x.images_done, x.error[0] ? " - " : "", x.error);
+    }
+    for (size_t i = 0; i < items.size(); ++i) {
+      Item& it = items[i];
+      if (st[i] != MX_OK) {
+        fprintf(stderr, "maxim: %s: not restored (status %d)\n", it.name.c_str(), st[i]);
+        ++failed;
+      } else {
+        mx_image pred{3, int32_t(it.padded.h), int32_t(it.padded.w), outs[i].data()};
+        mx_image cropped{};
+        if (mx_crop_out(&pred, it.img.h, it.img.w, it.eh, it.ew, &cropped) != MX_OK ||
+            mx_png_write((out_dir + "/" + it.name).c_str(), &cropped) != MX_OK) {
+          fprintf(stderr, "maxim: %s: %s\n", it.name.c_str(), last_error().c_str());
+          ++failed;
+        } else {
+          ++written;
+        }
+        mx_image_free(&cropped);
+      }
+      mx_image_free(&it.padded);
+      mx_image_free(&it.img);
+    }
+    mx_batch_free(b);
+    mx_plan_free(plan);
+  }
+  if (!quiet) fprintf(stderr, "maxim: wrote %d image(s) to %s, %d failed\n", written, out_dir.c_str(), failed);
+  return failed ? 1 : 0;
+}
+
 const char* kKind[] = {"copy", "add", "mul", "gate", "gelu", "lrelu", "sigmoid", "chanln", "chanmean",
                        "chanscale", "conv1x1", "conv3x3", "convdown", "convt", "gatemm", "blockperm",
                        "resize", "down"};
@@ -69,7 +185,7 @@ const char* kKind[] = {"copy", "add", "mul", "gate", "gelu", "lrelu", "sigmoid",
 
 int main(int argc, char** argv) {
   if (argc < 2) usage();
-  std::string model, input = "-", output = "-", device = "gpu";
+  std::string model, input = "-", output = "-", device = "gpu", batch_in, batch_out, devices_arg = "all";
   int gpu_index = 0, factor = 64;
   bool quiet = false, profile = false;
   for (int i = 1; i < argc; ++i) {
@@ -86,6 +202,8 @@ int main(int argc, char** argv) {
     else if (a == "--cpu") device = "cpu";
     else if (a == "--gpu-index") gpu_index = atoi(next().c_str());
     else if (a == "--factor") factor = atoi(next().c_str());
+    else if (a == "--batch") batch_in = next(), batch_out = next();
+    else if (a == "--devices") devices_arg = next();
     else if (a == "--profile" || a == "--timeline") profile = true;
     else if (a == "-q" || a == "--quiet") quiet = true;
     else if (a == "-h" || a == "--help") usage();
@@ -112,6 +230,23 @@ int main(int argc, char** argv) {
   if (mx_weights_open(model.c_str(), &w) != MX_OK) return fail("");
   char variant[16];
   mx_weights_variant(w, variant, sizeof(variant));
+
+  if (!batch_in.empty()) {
+    std::vector<int32_t> devs;
+    if (devices_arg != "all") {
+      size_t p = 0;
+      while (p <= devices_arg.size()) {
+        size_t q = devices_arg.find(',', p);
+        if (q == std::string::npos) q = devices_arg.size();
+        if (q > p) devs.push_back(int32_t(atoi(devices_arg.substr(p, q - p).c_str())));
+        p = q + 1;
+      }
+    }
+    if (mx_driver_ready() != MX_OK) return fail("cuda");
+    const int rc = run_batch(w, batch_in, batch_out, devs, factor, quiet);
+    mx_weights_free(w);
+    return rc;
+  }
 
   mx_image img{};
   if (input == "-") {

@@ -1464,9 +1464,12 @@ int mx_device_count(int* count) {
   });
 }
 
-int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) {
+int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) { return mx_gpu_new_budget(device, plan, 0, out); }
+
+int mx_gpu_new_budget(int device, const mx_plan* plan, int64_t budget_bytes, mx_gpu** out) {
   std::unique_ptr<mx_gpu> g;
   int rc = guard([&] {
+    if (budget_bytes < 0) throw Error("mx_gpu_new_budget: negative budget");
     if (!plan || !out) throw Error("mx_gpu_new: null argument");
     if (plan->input < 0 || plan->output < 0 || plan->n_ops <= 0) throw Error("mx_gpu_new: empty plan");
     int ndev = 0;
@@ -1515,16 +1518,19 @@ int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) {
     // (src/exec_gpu.rs:96-146). One arena serves both walks.
     size_t free_b = 0, total_b = 0;
     MX_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    const bool budgeted = budget_bytes > 0 && size_t(budget_bytes) < free_b;
+    if (budgeted) free_b = size_t(budget_bytes);
     int64_t arena_bytes = std::max(plan->arena_len, g->farena_len) * 4;
     int64_t io_bytes = (len_of(g->bufs[size_t(g->input)]) + len_of(g->bufs[size_t(g->output)])) * 4;
     int64_t need = arena_bytes + int64_t(g->pool.size()) + io_bytes + g->scratch_len * 4;
     if (need > int64_t(free_b))
       throw Error(fmt("not enough device memory for a %lldx%lld pass\n"
-                      "maxim: the arena needs %lld MiB and the weights %lld MiB; %lld MiB is free\n"
+                      "maxim: the arena needs %lld MiB and the weights %lld MiB; %lld MiB is %s\n"
                       "maxim: the arena is exact - the larger of the plan's own packed size and the executor's "
                       "schedule's, not an estimate - so this is a hard limit, not a guess",
                       (long long)plan->shape.w, (long long)plan->shape.h, (long long)(arena_bytes >> 20),
-                      (long long)(g->pool.size() >> 20), (long long)(free_b >> 20)),
+                      (long long)(g->pool.size() >> 20), (long long)(free_b >> 20),
+                      budgeted ? "the budget" : "free"),
                   MX_E_OOM);
     // The vectorised kernels index with 32 bits.
     for (const mx_buf& b : g->bufs)
@@ -1675,6 +1681,14 @@ int mx_gpu_sync(mx_gpu* g) {
     DevicePin pin(g->device);
     MX_CUDA(cudaStreamSynchronize(g->stream));
     check_status(*g);
+  });
+}
+
+int mx_gpu_poll(mx_gpu* g) {
+  return guard([&] {
+    if (!g) throw Error("mx_gpu_poll: null handle");
+    DevicePin pin(g->device);
+    check_status(*g);  // a plain copy: it does not wait for the handle's (non-blocking) stream
   });
 }
 
