@@ -53,6 +53,8 @@
 
 #include <cuda.h>
 
+#include <type_traits>
+
 #include "sm100.cuh"
 
 namespace mx {
@@ -758,29 +760,50 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
           const float4 v = ok ? src[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
           e[4 * i] = v.x, e[4 * i + 1] = v.y, e[4 * i + 2] = v.z, e[4 * i + 3] = v.w;
         }
+      } else if (MODE == MODE_GATE_SP) {
+        // Positions col .. col + 31 of group G, in rows of 1 << sp_shift
+        // positions: consecutive positions lie sc pixels apart, rows sr
+        // pixels apart (grid gating: position = cell, group = the pixel's
+        // place in its cell; block gating: position = place in the block,
+        // group = the block). With the row length a compile-time constant
+        // every load's offset is one add from the last.
+        const int G = a0 + q;
+        const bool ok = G < p.groups;
+        int pix0, sc, sr;
+        if (p.sp_mode == 0) {
+          const int fx = G % p.fw, fy = G / p.fw;
+          pix0 = ((col >> p.sp_shift) * p.fh + fy) * p.e_w + fx;
+          sc = p.fw, sr = p.fh * p.e_w;
+        } else {
+          const int gx = G % p.gw, gy = G / p.gw;
+          pix0 = (gy * p.fh + (col >> p.sp_shift)) * p.e_w + gx * p.fw;
+          sc = 1, sr = p.e_w;
+        }
+        const float* src = p.eptr + a1 + lane + size_t(ok ? pix0 : 0) * p.estride;
+        const int dc = sc * p.estride, dr = sr * p.estride;
+        auto rows = [&](auto lg) {
+          constexpr int RL = 1 << decltype(lg)::value;
+#pragma unroll
+          for (int r = 0; r < 32 / RL; ++r)
+#pragma unroll
+            for (int c = 0; c < RL; ++c) e[r * RL + c] = ok ? src[r * dr + c * dc] : 0.0f;
+        };
+        switch (p.sp_shift) {
+          case 0: rows(std::integral_constant<int, 0>()); break;
+          case 1: rows(std::integral_constant<int, 1>()); break;
+          case 2: rows(std::integral_constant<int, 2>()); break;
+          case 3: rows(std::integral_constant<int, 3>()); break;
+          case 4: rows(std::integral_constant<int, 4>()); break;
+          default: rows(std::integral_constant<int, 5>()); break;
+        }
       } else {
         const int G = a0 + q;
         const bool ok = G < p.groups;
         const float* src = p.eptr + a1 + lane;
-        int fx = 0, fy = 0, gx = 0, gy = 0;
-        if (MODE == MODE_GATE_SP) {
-          if (p.sp_mode == 0) fx = G % p.fw, fy = G / p.fw;
-          else gx = G % p.gw, gy = G / p.gw;
-        }
-        const int msk = (1 << p.sp_shift) - 1, rows0 = col >> p.sp_shift;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int a = col + i;
-          int pix;
-          if (MODE == MODE_GATE) {
-            pix = G * p.e_pp + a;
-          } else if (MODE == MODE_GATE_GRID) {
-            pix = a * p.e_pp + G;
-          } else if (p.sp_mode == 0) {
-            pix = ((rows0 + (i >> p.sp_shift)) * p.fh + fy) * p.e_w + (i & msk) * p.fw + fx;
-          } else {
-            pix = (gy * p.fh + rows0 + (i >> p.sp_shift)) * p.e_w + gx * p.fw + (i & msk);
-          }
+          const int pix = MODE == MODE_GATE ? G * p.e_pp + a : a * p.e_pp + G;
           e[i] = ok ? src[size_t(pix) * p.estride] : 0.0f;
         }
       }

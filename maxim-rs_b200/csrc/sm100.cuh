@@ -45,14 +45,20 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                "r"(bytes)
                : "memory");
 }
+// The suspend-time hint lets a waiting thread sleep until the phase
+// completes (the hardware wakes it then) for up to kSuspendNs, rather than
+// returning after a short system-dependent time to poll again: a waiting
+// warp then takes almost no issue slots from the working warps of its
+// sub-partition. The bounded wait below still checks its time limit.
+constexpr uint32_t kSuspendNs = 1000000;  // 1 ms
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -65,7 +71,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63) == 0) {
+    if ((i & 3) == 0) {
       if (abort && *abort) return false;
       if (global_ns() - t0 > kWaitLimitNs) return false;
     }
