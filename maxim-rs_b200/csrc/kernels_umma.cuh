@@ -832,11 +832,10 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
         tc_fence_after();
         decode(t, a0, a1, n0);
       }
-      if (lane == 0) bulk_wait_read<0>();  // this warp's previous store has read the buffer
-      __syncwarp();
       const uint32_t tcol = tmem + (uint32_t(q * 32) << 16) + set * 2 * N + j * 32;
       // The chunk whose LayerNorm this step also writes (below).
       const bool lnc = MODE == MODE_CONV1 && p.lo_scale != nullptr && n0 + j * 32 == p.lo_col;
+#pragma unroll
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         float v[16], x[16], e[16];
@@ -902,6 +901,13 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
               ss1[g] = 0.0f, ss2[g] = 0.0f;
             }
           }
+        }
+        if (h == 0) {
+          // This warp's previous store must have read the staging buffer;
+          // waiting only now lets that read overlap the TMEM loads and the
+          // arithmetic above.
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
         }
         if (GATE) {
           // Staging is [a][channel] for this warp's group: this thread

@@ -30,6 +30,7 @@ def lib():
         sigs = {
             "mxo_run": (ctypes.c_int, [vp, vp, ctypes.c_int]),
             "mxo_run_range": (ctypes.c_int, [vp, vp, i32, i32, ctypes.c_int]),
+            "mxo_run_bf16_storage": (ctypes.c_int, [vp, vp, ctypes.c_int]),
             "mxo_last_error": (sz, [ctypes.c_char_p, sz]),
             "mxo_param_spec": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, sz, ctypes.POINTER(sz)]),
             "mxo_weights_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(vp)]),
@@ -155,3 +156,14 @@ def take(plan, arena, buf_id):
 
 def output(plan, image, threads=0):
     return take(plan, run(plan, image, threads), plan.output)
+
+
+def output_bf16_storage(plan, image, threads=0):
+    """The plan's output with every activation rounded to bfloat16 as it is
+    written (a what-if for bf16 activation storage, not the reference)."""
+    arena = new_arena(plan, image)
+    rc = lib().mxo_run_bf16_storage(ctypes.cast(plan.view, ctypes.c_void_p), arena.ctypes.data_as(ctypes.c_void_p),
+                                    threads)
+    if rc != 0:
+        raise RuntimeError("oracle bf16-storage run failed (%d)" % rc)
+    return take(plan, arena, plan.output)

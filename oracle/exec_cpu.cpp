@@ -560,4 +560,29 @@ __attribute__((visibility("default"))) int mxo_run_range(const mx_plan* plan, fl
   return MX_OK;
 }
 
+// The whole plan with every op's output rounded to bfloat16 (nearest, ties
+// to even) as it is written: what storing activations in bf16 would do to
+// the result, measured against mxo_run. Not the reference's arithmetic - a
+// what-if for the storage precision of the activations.
+__attribute__((visibility("default"))) int mxo_run_bf16_storage(const mx_plan* plan, float* arena, int threads) {
+  if (!plan || !arena) return MX_E_INVALID;
+  Pool pool(threads > 0 ? threads : int(std::thread::hardware_concurrency()));
+  Ctx ctx{*plan, arena, pool};
+  for (int32_t i = 0; i < plan->n_ops; ++i) {
+    ctx.op(plan->ops[i]);
+    float* d = ctx.p(plan->ops[i].dst);
+    const int64_t n = ctx.blen(plan->ops[i].dst);  // a channel view is contiguous in [c][h][w]
+    pool.run((n + 65535) / 65536, [&](int64_t t) {
+      const int64_t e = std::min(n, (t + 1) * 65536);
+      for (int64_t k = t * 65536; k < e; ++k) {
+        uint32_t b;
+        memcpy(&b, &d[k], 4);
+        if ((b & 0x7f800000u) != 0x7f800000u) b = (b + 0x7fffu + ((b >> 16) & 1u)) & 0xffff0000u;
+        memcpy(&d[k], &b, 4);
+      }
+    });
+  }
+  return MX_OK;
+}
+
 }  // extern "C"
