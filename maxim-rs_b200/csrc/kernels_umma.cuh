@@ -260,16 +260,32 @@ enum : int {
 // shared memory is A_hi = trunc(v) as it stands and only the residual
 // A_lo = v - trunc(v) is computed and stored. The subtraction is exact; the
 // residual is then rounded to the nearest TF32 value, ties away from zero:
-// adding half a TF32 ulp (bit 12) to the sign-magnitude bits and clearing
-// the 13 low bits does that and carries into the exponent where it should.
-// All on the integer and fp32 ALUs at the full issue rate (the TF32
-// conversion instruction runs on a slower pipe). A NaN residual would wrap
-// to zero, but it only comes with a NaN or infinite A_hi, which the product
-// carries.
+// adding half a TF32 ulp (bit 12) to the sign-magnitude bits does that,
+// carrying into the exponent where it should, once the 13 low bits are
+// cleared - and the tensor core clears them itself as it reads the operand,
+// so the stored word keeps them (one instruction less per value). All on the
+// integer and fp32 ALUs at the full issue rate (the TF32 conversion
+// instruction runs on a slower pipe). A NaN residual would wrap to a zero
+// TF32 value, but it only comes with a NaN or infinite A_hi, which the
+// product carries.
 __device__ __forceinline__ float tf32_residual(float v) {
   const float hi = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
   const float r = __fsub_rn(v, hi);
-  return __uint_as_float((__float_as_uint(r) + 0x1000u) & 0xFFFFE000u);
+  return __uint_as_float(__float_as_uint(r) + 0x1000u);
+}
+// The same for four values, the subtractions paired (f32x2).
+__device__ __forceinline__ void tf32_residual4(const float4 v, float* o) {
+  const float4 hi = make_float4(__uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u),
+                                __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u),
+                                __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u),
+                                __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u));
+  float r0, r1, r2, r3;
+  f2_unpack(f2_sub(f2_pack(v.x, v.y), f2_pack(hi.x, hi.y)), r0, r1);
+  f2_unpack(f2_sub(f2_pack(v.z, v.w), f2_pack(hi.z, hi.w)), r2, r3);
+  o[0] = __uint_as_float(__float_as_uint(r0) + 0x1000u);
+  o[1] = __uint_as_float(__float_as_uint(r1) + 0x1000u);
+  o[2] = __uint_as_float(__float_as_uint(r2) + 0x1000u);
+  o[3] = __uint_as_float(__float_as_uint(r3) + 0x1000u);
 }
 
 // E: the epilogue's tail reads a second operand (UEPI_ADD / _MUL / _GATE).
@@ -655,20 +671,14 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
                 v.w = ln ? u.w : v.w;
               }
               *p4 = v;
-              lo[4 * c] = tf32_residual(v.x);
-              lo[4 * c + 1] = tf32_residual(v.y);
-              lo[4 * c + 2] = tf32_residual(v.z);
-              lo[4 * c + 3] = tf32_residual(v.w);
+              tf32_residual4(v, lo + 4 * c);
             }
           } else {
 #pragma unroll
             for (int c = 0; c < NCH; ++c) {
               const int cc = half * NCH + c;  // float4 chunk of the row
               const float4 v = *reinterpret_cast<const float4*>(arow + ((cc ^ (r & 7)) << 4));
-              lo[4 * c] = tf32_residual(v.x);
-              lo[4 * c + 1] = tf32_residual(v.y);
-              lo[4 * c + 2] = tf32_residual(v.z);
-              lo[4 * c + 3] = tf32_residual(v.w);
+              tf32_residual4(v, lo + 4 * c);
             }
           }
           const uint32_t slot = tmem + (uint32_t(q * 32) << 16) + C::A_COL0 + s * 32;
@@ -710,10 +720,7 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
             }
             a[i] = v;
           }
-          l.x = tf32_residual(v.x);
-          l.y = tf32_residual(v.y);
-          l.z = tf32_residual(v.z);
-          l.w = tf32_residual(v.w);
+          tf32_residual4(v, &l.x);
           alo[i] = l;
         }
         fence_proxy_async_smem();

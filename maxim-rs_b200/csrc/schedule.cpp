@@ -374,6 +374,54 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
       S.ops_fused += int(B.covers.size());
     }
   }
+  // 2b. Copy elision. A Copy left after folding has a source with other
+  // readers (or no producer to fold into). Where its destination is a whole
+  // buffer that later steps read only as a whole, and neither it nor the
+  // source is written while it is still read, those readers read the source
+  // instead and the Copy is removed (it moved the same values).
+  for (size_t c = 0; fuse && c < W.size(); ++c) {
+    if (dead[c] || W[c].o.kind != MX_OP_COPY || p.ops[W[c].op].kind != MX_OP_COPY || W[c].epi != EPI_NONE) continue;
+    const int32_t D = W[c].o.dst, Sr = W[c].o.src;
+    if (D < 0 || Sr < 0 || G.root[size_t(D)] != D || !G.whole(D) || G.overlap(D, p.output) || G.overlap(Sr, D))
+      continue;
+    const mx_buf& bd = p.bufs[D];
+    const mx_buf& bs = p.bufs[Sr];
+    if (bd.c != bs.c || bd.h != bs.h || bd.w != bs.w || W[c].o.n != bd.c * bd.h * bd.w) continue;
+    if (!H.tma_view(Sr, int(bd.c)) && H.tma_view(D, int(bd.c))) continue;
+    std::vector<size_t> rd;
+    bool ok = true, src_written = false;
+    for (size_t s = c + 1; s < W.size() && ok; ++s) {
+      if (dead[s]) continue;
+      int32_t r[4], w[5];
+      const int nr = step_reads(W[s], r), nw = step_writes(W[s], w);
+      bool reads_d = false;
+      for (int a = 0; a < nr; ++a)
+        if (G.overlap(r[a], D)) {
+          if (r[a] != D) ok = false;
+          reads_d = true;
+        }
+      if (reads_d) {
+        if (src_written) ok = false;
+        rd.push_back(s);
+      }
+      bool d_written = false;
+      for (int a = 0; a < nw; ++a) {
+        if (G.overlap(w[a], Sr)) src_written = true;
+        if (G.overlap(w[a], D)) d_written = true;
+      }
+      if (d_written) break;
+    }
+    if (!ok || rd.empty()) continue;
+    for (size_t s : rd) {
+      SchedStep& R = W[s];
+      if (R.o.src == D) R.o.src = Sr;
+      if (R.o.src2 == D) R.o.src2 = Sr;
+      if (R.epi_src == D) R.epi_src = Sr;
+    }
+    dead[c] = 1;
+    ++S.copies_elided;
+  }
+
   // 3. LayerNorm on load: a LayerNorm whose only reader is a conv that can
   // normalise its A operand becomes a statistics step, and the conv reads
   // the LayerNorm's input instead of its output.

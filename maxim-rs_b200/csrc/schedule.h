@@ -97,6 +97,7 @@ struct Schedule {
   int ln_on_load = 0;         // LayerNorms applied by their consumer
   int stats_in_epilogue = 0;  // of those, statistics written by the producer's epilogue
   int ln_in_epilogue = 0;     // LayerNorms written whole by their producer's epilogue
+  int copies_elided = 0;      // Copies whose readers read the source instead
 };
 
 struct ScheduleHooks {

@@ -26,11 +26,13 @@ def test_schedule_shape(variant, h, w, mx):
     ops = plan.ops()
     st, primary = _sched(mx, plan)
     kinds = np.array([o.kind for o in ops])
-    forward = np.array([o.kind == BLOCK_PERM and o.forward for o in ops])
+    forward = np.array([o.kind == BLOCK_PERM and bool(o.forward) for o in ops], dtype=bool)
     # Every forward block permutation goes (the gating reads the blocks in
-    # place); nothing else is removed outright.
+    # place); otherwise only Copies are removed outright (their readers read
+    # the source).
     assert st["perms_dropped"] == forward.sum()
-    assert ((primary < 0) == forward).all()
+    assert (primary[forward] < 0).all()
+    assert (kinds[(primary < 0) & ~forward] == COPY).all()
     # An absorbed op runs in the step of an earlier op.
     idx = np.arange(len(ops))
     assert (primary[primary >= 0] <= idx[primary >= 0]).all()
