@@ -839,7 +839,9 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
         if (aligned4(d) && aligned4(x) && (c == 32 || c == 64 || c == 128 || c == 256)) {
           const int pb = c <= 64 ? 128 : (c == 128 ? 64 : 32);
           const unsigned grid = unsigned((np + pb - 1) / pb);
-          const size_t smem = size_t(pb) * (c + 1) * sizeof(float);
+          // the tile (rows of c + 1 floats, rounded to an even count), then
+          // pb (mean, rstd) pairs
+          const size_t smem = ((size_t(pb) * (c + 1) + 1) & ~size_t(1)) * sizeof(float) + size_t(pb) * 8;
           const int sx = int(x.stride), sy = int(d.stride);
           if (c == 32) chan_ln_tile_kernel<32><<<grid, 128, smem, s>>>(np, x.ptr, sx, P(ws), P(wb), d.ptr, sy, kLnEps);
           else if (c == 64) chan_ln_tile_kernel<64><<<grid, 128, smem, s>>>(np, x.ptr, sx, P(ws), P(wb), d.ptr, sy, kLnEps);

@@ -131,8 +131,9 @@ struct Cin3Weights {
 __global__ void __launch_bounds__(128) conv3x3_cin3c_kernel(int h, int wd, int n, const float* __restrict__ x, int sx,
                                                             float* __restrict__ y, int sy,
                                                             const __grid_constant__ Cin3Weights cw) {
-  const int p = blockIdx.x * blockDim.x + threadIdx.x;
-  if (p >= h * wd) return;
+  // A pixel past the end computes on zeros (its row of the staging buffer
+  // is never stored) so that every thread reaches the barrier below.
+  const int p = min(blockIdx.x * blockDim.x + threadIdx.x, h * wd - 1);
   const int py = p / wd, px = p - py * wd;
   float in[27];
 #pragma unroll
@@ -152,14 +153,31 @@ __global__ void __launch_bounds__(128) conv3x3_cin3c_kernel(int h, int wd, int n
   for (int k = 0; k < 27; ++k)
 #pragma unroll
     for (int o = 0; o < 32; ++o) acc[o] = fmaf(in[k], cw.w[o * 27 + k], acc[o]);
-  float* d = y + size_t(p) * sy;
-  if (n == 32 && (reinterpret_cast<uintptr_t>(d) % 16) == 0) {
+  // The block's 128 x 32 outputs go through shared memory (rows padded to
+  // 36 floats: conflict-free float4 access both ways), so each warp-wide
+  // store writes four whole 128-byte pixel chunks instead of 32 scattered
+  // 16-byte pieces.
+  __shared__ float4 stage[128 * 9];
+  const int t = threadIdx.x;
 #pragma unroll
-    for (int o = 0; o < 32; o += 4) *reinterpret_cast<float4*>(d + o) = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
-  } else {
+  for (int o = 0; o < 32; o += 4) stage[t * 9 + o / 4] = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
+  __syncthreads();
+  const int p0 = blockIdx.x * blockDim.x, npix = min(128, h * wd - p0);
+  const bool vec = n == 32 && sy % 4 == 0 && (reinterpret_cast<uintptr_t>(y) % 16) == 0;
 #pragma unroll
-    for (int o = 0; o < 32; ++o)
-      if (o < n) d[o] = acc[o];
+  for (int i = 0; i < 8; ++i) {
+    const int f = t + 128 * i, pp = f >> 3, q = f & 7;
+    if (pp >= npix) break;
+    float* d = y + size_t(p0 + pp) * sy + 4 * q;
+    const float4 v = stage[pp * 9 + q];
+    if (vec) {
+      *reinterpret_cast<float4*>(d) = v;
+    } else {
+      if (4 * q < n) d[0] = v.x;
+      if (4 * q + 1 < n) d[1] = v.y;
+      if (4 * q + 2 < n) d[2] = v.z;
+      if (4 * q + 3 < n) d[3] = v.w;
+    }
   }
 }
 

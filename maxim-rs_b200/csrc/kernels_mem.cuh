@@ -53,7 +53,8 @@ __global__ void __launch_bounds__(128) chan_ln_tile_kernel(int npix, const float
                                                            float* __restrict__ y, int sy, float eps) {
   constexpr int P = C <= 64 ? 128 : (C == 128 ? 64 : 32);
   constexpr int C4 = C / 4, R = C + 1;
-  extern __shared__ float tile[];  // P * R
+  extern __shared__ float tile[];  // P * R, then P (mean, rstd) pairs
+  float2* st = reinterpret_cast<float2*>(tile + ((P * R + 1) & ~1));
   const int p0 = blockIdx.x * P;
   const int np = min(P, npix - p0);
   for (int idx = threadIdx.x; idx < np * C4; idx += 128) {
@@ -66,8 +67,9 @@ __global__ void __launch_bounds__(128) chan_ln_tile_kernel(int npix, const float
     t[3] = v.w;
   }
   __syncthreads();
+  // The statistics, one pixel per thread, serially in channel order.
   if (threadIdx.x < np) {
-    float* t = tile + threadIdx.x * R;
+    const float* t = tile + threadIdx.x * R;
     float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll 8
     for (int i = 0; i < C; ++i) {
@@ -79,14 +81,26 @@ __global__ void __launch_bounds__(128) chan_ln_tile_kernel(int npix, const float
     float m = __fdiv_rn(s1, nf);
     float var = __fsub_rn(__fdiv_rn(s2, nf), __fmul_rn(m, m));
     float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(fmaxf(var, 0.0f), eps)));
-#pragma unroll 8
-    for (int i = 0; i < C; ++i) t[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(t[i], m), rstd), __ldg(w + i)), __ldg(b + i));
+    st[threadIdx.x] = make_float2(m, rstd);
   }
   __syncthreads();
+  // The normalisation, spread over all threads four channels at a time:
+  // ((x - m) * rstd) * w + b, each operation rounded on its own (paired).
   for (int idx = threadIdx.x; idx < np * C4; idx += 128) {
-    int r = idx / C4, c = (idx - r * C4) * 4;
+    const int r = idx / C4, c = (idx - r * C4) * 4;
     const float* t = tile + r * R + c;
-    *reinterpret_cast<float4*>(y + size_t(p0 + r) * sy + c) = make_float4(t[0], t[1], t[2], t[3]);
+    const float2 ms = st[r];
+    const float4 wv = __ldg(reinterpret_cast<const float4*>(w + c));
+    const float4 bv = __ldg(reinterpret_cast<const float4*>(b + c));
+    const uint64_t mm = f2_pack(ms.x, ms.x), rr = f2_pack(ms.y, ms.y);
+    float4 o;
+    f2_unpack(f2_add_after_mul(f2_mul(f2_mul(f2_sub(f2_pack(t[0], t[1]), mm), rr), f2_pack(wv.x, wv.y)),
+                               f2_pack(bv.x, bv.y)),
+              o.x, o.y);
+    f2_unpack(f2_add_after_mul(f2_mul(f2_mul(f2_sub(f2_pack(t[2], t[3]), mm), rr), f2_pack(wv.z, wv.w)),
+                               f2_pack(bv.z, bv.w)),
+              o.z, o.w);
+    *reinterpret_cast<float4*>(y + size_t(p0 + r) * sy + c) = o;
   }
 }
 
