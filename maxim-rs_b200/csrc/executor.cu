@@ -317,9 +317,16 @@ bool tma_view(const mx_gpu& g, const Layout& L, int32_t id, int n) {
 // Whether a conv runs on the tensor-core kernel: TMA needs 16-byte aligned
 // rows and strides; the kernel takes K in blocks of 32 channels and
 // N = c_out in {32, 64, 128, 256}.
+// A 1x1 conv over fewer pixels than one tensor-core tile (the channel
+// attention's convs on the 1x1 squeeze) runs on the small-conv kernel: the
+// persistent tensor-core kernel would launch 148 CTAs for one tile.
+constexpr int64_t kSmallConvPixels = 128;
+bool small_conv(const mx_op& o) { return o.kind == MX_OP_CONV1X1 && int64_t(o.h) * o.wd < kSmallConvPixels; }
+
 bool umma_eligible(const mx_gpu& g, const Layout& L, const mx_op& o) {
   if (!g.use_umma) return false;
   if (o.kind != MX_OP_CONV1X1 && o.kind != MX_OP_CONV3X3 && o.kind != MX_OP_CONV4X4S2) return false;
+  if (small_conv(o)) return false;
   if (o.c_in % 32 != 0) return false;
   if (o.c_out != 32 && o.c_out != 64 && o.c_out != 128 && o.c_out != 256) return false;
   ViewMeta x = meta_of(g, L, o.src), d = meta_of(g, L, o.dst);
@@ -421,6 +428,7 @@ enum WeightTag : int {
   WT_CONVT_HI = 7,
   WT_CONVT_LO = 8,
   WT_BIAS4 = 9,  // a bias repeated once per transposed-conv tap
+  WT_T = 10,     // a 1x1 kernel transposed to [c_in][c_out] (the small-conv kernel)
 };
 int64_t cached(mx_gpu& g, int32_t id, int tag, const std::function<std::vector<float>()>& make) {
   if (id < 0) return -1;
@@ -912,6 +920,29 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
         on_umma = true;
         break;
       }
+      if (small_conv(o)) {
+        // [c_out][c_in] -> [c_in][c_out]
+        const int ci = o.c_in, co = o.c_out;
+        const int64_t wt = cached(g, o.w, WT_T, [&] {
+          auto w = W(o.w);
+          std::vector<float> t(w.size());
+          for (int n = 0; n < co; ++n)
+            for (int k = 0; k < ci; ++k) t[size_t(k) * co + n] = w[size_t(n) * ci + k];
+          return t;
+        });
+        const int64_t bo = raw(o.bias);
+        const int tail = E.epi == EPI_GELU ? EW_GELU : E.epi == EPI_LRELU ? EW_LRELU : E.epi == EPI_SIGMOID ? EW_SIGMOID : -1;
+        if (E.epi != EPI_NONE && tail < 0) throw Error(fmt("op %d: a small 1x1 conv takes only a unary tail", oi));
+        const float slope = E.slope;
+        needs_umma = false;
+        st.run = [G, L, P, dst, src, wt, bo, ci, co, tail, slope](cudaStream_t s) {
+          View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
+          const dim3 grid(unsigned(x.npix), unsigned((co + 127) / 128));
+          conv1x1_small_kernel<<<grid, 128, size_t(ci) * sizeof(float), s>>>(ci, co, x.ptr, x.stride, P(wt), P(bo),
+                                                                               d.ptr, d.stride, tail, slope);
+        };
+        break;
+      }
       int64_t wo = raw(o.w), bo = raw(o.bias);  // [c_out][c_in]
       int ci = o.c_in, co = o.c_out;
       st.run = [G, L, P, dst, src, wo, bo, ci, co](cudaStream_t s) {
@@ -1229,12 +1260,13 @@ ScheduleHooks schedule_hooks(const mx_gpu& g) {
     return umma_gate_spatial_ok(*G, G->roffs, gate, perm) && tma_view(*G, G->roffs, gate.dst, gate.c);
   };
   h.tma_view = [G](int32_t b, int n) { return tma_view(*G, G->roffs, b, n); };
+  h.small_conv = [](const mx_op& o) { return small_conv(o); };
   // The split stage normalises A for 1x1 convs whose input has a channel
   // count the statistics kernel takes (32..256, aligned rows). A 3x3 conv
   // could too, but it would normalise every input pixel once per tap (nine
   // times), which measured slower than the separate LayerNorm.
   h.ln_on_load = [G](const mx_op& o) {
-    if (o.kind != MX_OP_CONV1X1) return false;
+    if (o.kind != MX_OP_CONV1X1 || small_conv(o)) return false;
     const int c = o.c_in;
     return (c == 32 || c == 64 || c == 128 || c == 256) && tma_view(*G, G->roffs, o.src, c);
   };

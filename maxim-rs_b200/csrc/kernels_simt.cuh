@@ -314,6 +314,29 @@ struct ProbConv1x1 {
   __device__ void store(int, int64_t m, int n, float v) const { y[m * sy + n] = v; }
 };
 
+// A 1x1 conv over a handful of pixels (the channel-attention convs run on
+// the 1x1 squeeze): one block per pixel and 128 outputs, the pixel's inputs
+// staged in shared memory, each thread one output's sum - the bias, then
+// c_in ascending (fused multiply-adds) - and the unary tail (EW_LRELU /
+// EW_SIGMOID / EW_GELU, or none). W is [c_in][c_out], so a warp's weight
+// reads are consecutive.
+__global__ void __launch_bounds__(128) conv1x1_small_kernel(int K, int N, const float* __restrict__ x, int64_t sx,
+                                                            const float* __restrict__ wt,
+                                                            const float* __restrict__ bias, float* __restrict__ y,
+                                                            int64_t sy, int tail, float slope) {
+  extern __shared__ float xs[];
+  const int m = blockIdx.x, n = blockIdx.y * 128 + threadIdx.x;
+  for (int k = threadIdx.x; k < K; k += 128) xs[k] = x[int64_t(m) * sx + k];
+  __syncthreads();
+  if (n >= N) return;
+  float a = bias ? bias[n] : 0.0f;
+  for (int k = 0; k < K; ++k) a = fmaf(xs[k], wt[int64_t(k) * N + n], a);
+  if (tail == EW_LRELU) a = a >= 0.0f ? a : slope * a;
+  else if (tail == EW_SIGMOID) a = sigmoid_f(a);
+  else if (tail == EW_GELU) a = gelu_f(a);
+  y[int64_t(m) * sy + n] = a;
+}
+
 // k x k conv, stride s, padding (pt, pl): k = tap * c_in + ci, tap = ky*ks + kx,
 // the reference's (ky, kx, ic) order. W is [c_out][tap][c_in].
 struct ProbConvKxK {

@@ -330,6 +330,8 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
         // the residual (all views 4-channel aligned for the vector kernel).
         if (epi != EPI_ADD || A.epi != EPI_NONE) break;
         if (!H.tma_view(D, A.o.c) || !H.tma_view(operand, A.o.c) || !H.tma_view(A.o.src, A.o.c)) break;
+      } else if (H.small_conv && H.small_conv(A.o)) {
+        if (A.epi != EPI_NONE || operand >= 0 || (epi != EPI_GELU && epi != EPI_LRELU && epi != EPI_SIGMOID)) break;
       } else {
         // (A transposed conv's epilogue only forwards copies.)
         if (!umma || A.epi != EPI_NONE || A.o.kind == MX_OP_CONVT2X2) break;

@@ -109,6 +109,10 @@ struct ScheduleHooks {
   std::function<bool(int32_t b, int n)> tma_view;
   // Whether the op's kernel can LayerNorm its A operand on load.
   std::function<bool(const mx_op&)> ln_on_load;
+  // Whether the op is a 1x1 conv over so few pixels that it runs on the
+  // small-conv kernel, whose epilogue takes the unary tails (GELU / LeakyReLU
+  // / sigmoid) but no second operand.
+  std::function<bool(const mx_op&)> small_conv;
   // The output-column slice width of a tensor-core op whose epilogue can
   // write LayerNorm statistics (whole pixel rows per thread), 0 if it cannot.
   std::function<int(const mx_op&)> stats_slice;

@@ -87,12 +87,15 @@ class HostPlan:
         self.shape = (v.shape.c, v.shape.h, v.shape.w)
 
     def __del__(self):
-        if getattr(self, "_h", None):
-            lib().mxo_plan_free(self._h)
-            self._h = None
-        if getattr(self, "_w", None):
-            lib().mxo_weights_free(self._w)
-            self._w = None
+        try:
+            if getattr(self, "_h", None):
+                lib().mxo_plan_free(self._h)
+                self._h = None
+            if getattr(self, "_w", None):
+                lib().mxo_weights_free(self._w)
+                self._w = None
+        except Exception:  # interpreter shutdown: the module's globals may already be gone
+            pass
 
     def buf(self, i):
         b = self.view.contents.bufs[i]

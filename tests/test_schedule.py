@@ -74,9 +74,12 @@ def test_schedule_off_keeps_every_op(mx):
 
 
 def test_schedule_without_tensor_cores_fuses_only_copies(mx):
-    """With the tensor-core kernel off no GEMM has an epilogue: only Copies are
-    forwarded and the channel-attention residual add joins its channel scale;
-    block permutations stay (the SIMT gating reads blocks)."""
+    """With the tensor-core kernel off only the small-conv kernel (1x1 convs
+    over fewer than 128 pixels: the channel attention's on the squeezed 1x1
+    plane, and at 64x64 the bottleneck's) takes an epilogue, a unary tail;
+    otherwise only Copies are forwarded and the
+    channel-attention residual add joins its channel scale; block
+    permutations stay (the SIMT gating reads blocks)."""
     plan = mx.Plan(None, 64, 64, variant="S-2")
     os.environ["MAXIM_NO_UMMA"] = "1"
     try:
@@ -86,5 +89,9 @@ def test_schedule_without_tensor_cores_fuses_only_copies(mx):
     kinds = np.array([o.kind for o in plan.ops()])
     assert st["perms_dropped"] == 0
     moved = (primary >= 0) & (primary != np.arange(plan.n_ops))
-    assert moved.any() and np.isin(kinds[moved], [COPY, ADD]).all()
+    assert moved.any() and np.isin(kinds[moved], [COPY, ADD, GELU, 5, 6]).all()
     assert (kinds[primary[moved & (kinds == ADD)]] == 9).all()  # an add only ever joins a channel scale
+    ops = plan.ops()
+    for i in np.nonzero(moved & np.isin(kinds, [GELU, 5, 6]))[0]:  # GELU / LeakyReLU / sigmoid: a small conv's tail
+        p = ops[primary[i]]
+        assert p.kind == CONV1X1 and p.h * p.wd < 128
