@@ -938,8 +938,11 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
         st.run = [G, L, P, dst, src, wt, bo, ci, co, tail, slope](cudaStream_t s) {
           View d = view_of(*G, *L, dst), x = view_of(*G, *L, src);
           const dim3 grid(unsigned(x.npix), unsigned((co + 127) / 128));
-          conv1x1_small_kernel<<<grid, 128, size_t(ci) * sizeof(float), s>>>(ci, co, x.ptr, x.stride, P(wt), P(bo),
-                                                                               d.ptr, d.stride, tail, slope);
+          const size_t ws = size_t(ci) * size_t(std::min(co, 128)) * sizeof(float);
+          const int stage_w = ws + size_t(ci) * sizeof(float) <= 48 * 1024;
+          const size_t smem = size_t(ci) * sizeof(float) + (stage_w ? ws : 0);
+          conv1x1_small_kernel<<<grid, 128, smem, s>>>(ci, co, x.ptr, x.stride, P(wt), P(bo), d.ptr, d.stride, tail,
+                                                       slope, stage_w);
         };
         break;
       }

@@ -320,17 +320,30 @@ struct ProbConv1x1 {
 // c_in ascending (fused multiply-adds) - and the unary tail (EW_LRELU /
 // EW_SIGMOID / EW_GELU, or none). W is [c_in][c_out], so a warp's weight
 // reads are consecutive.
+// With `stage_w`, the block first copies its [K][<=128] slice of W into
+// shared memory in one coalesced sweep, so the sums wait on one round trip
+// rather than one per k.
 __global__ void __launch_bounds__(128) conv1x1_small_kernel(int K, int N, const float* __restrict__ x, int64_t sx,
                                                             const float* __restrict__ wt,
                                                             const float* __restrict__ bias, float* __restrict__ y,
-                                                            int64_t sy, int tail, float slope) {
-  extern __shared__ float xs[];
-  const int m = blockIdx.x, n = blockIdx.y * 128 + threadIdx.x;
+                                                            int64_t sy, int tail, float slope, int stage_w) {
+  extern __shared__ float xs[];  // K inputs, then (stage_w) K x nb weights
+  const int m = blockIdx.x, n0 = blockIdx.y * 128, n = n0 + threadIdx.x, nb = min(128, N - n0);
+  float* ws = xs + K;
   for (int k = threadIdx.x; k < K; k += 128) xs[k] = x[int64_t(m) * sx + k];
+  if (stage_w)
+    for (int i = threadIdx.x; i < K * nb; i += 128) {
+      const int k = i / nb, j = i - k * nb;
+      ws[i] = wt[int64_t(k) * N + n0 + j];
+    }
   __syncthreads();
   if (n >= N) return;
   float a = bias ? bias[n] : 0.0f;
-  for (int k = 0; k < K; ++k) a = fmaf(xs[k], wt[int64_t(k) * N + n], a);
+  if (stage_w) {
+    for (int k = 0; k < K; ++k) a = fmaf(xs[k], ws[k * nb + threadIdx.x], a);
+  } else {
+    for (int k = 0; k < K; ++k) a = fmaf(xs[k], wt[int64_t(k) * N + n], a);
+  }
   if (tail == EW_LRELU) a = a >= 0.0f ? a : slope * a;
   else if (tail == EW_SIGMOID) a = sigmoid_f(a);
   else if (tail == EW_GELU) a = gelu_f(a);
