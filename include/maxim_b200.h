@@ -234,9 +234,11 @@ int mx_gpu_get_stats(mx_gpu* g, mx_gpu_stats* s);
  * MX_SCHED_LN_ON_LOAD when op i, a conv, normalises its input with such
  * statistics as it loads it; MX_SCHED_LN_IN_EPILOGUE when op i, a channel
  * LayerNorm, is written whole by the epilogue of the conv that produces its
- * input (primary[i]). n_ops must be the plan's op count. No counterpart in
- * the reference (its executor runs every op as its own launch). */
-enum { MX_SCHED_STATS_ONLY = 1, MX_SCHED_LN_ON_LOAD = 2, MX_SCHED_LN_IN_EPILOGUE = 4 };
+ * input (primary[i]), plus MX_SCHED_LN_INPUT_UNSTORED when no other op reads
+ * that input, so the epilogue stores the LayerNorm alone. n_ops must be the
+ * plan's op count. No counterpart in the reference (its executor runs every
+ * op as its own launch). */
+enum { MX_SCHED_STATS_ONLY = 1, MX_SCHED_LN_ON_LOAD = 2, MX_SCHED_LN_IN_EPILOGUE = 4, MX_SCHED_LN_INPUT_UNSTORED = 8 };
 int mx_gpu_schedule(mx_gpu* g, int32_t* primary, int32_t* flags, int32_t n_ops);
 
 /* The same schedule worked out on the host alone, without a device: for

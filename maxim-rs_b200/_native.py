@@ -505,7 +505,7 @@ def _stats_dict(s):
             "ops_fused": s.ops_fused, "perms_dropped": s.perms_dropped, "pass_arena_bytes": s.pass_arena_bytes}
 
 
-SCHED_STATS_ONLY, SCHED_LN_ON_LOAD, SCHED_LN_IN_EPILOGUE = 1, 2, 4
+SCHED_STATS_ONLY, SCHED_LN_ON_LOAD, SCHED_LN_IN_EPILOGUE, SCHED_LN_INPUT_UNSTORED = 1, 2, 4, 8
 
 
 def plan_schedule(plan, flags=False):

@@ -1546,7 +1546,8 @@ int mx_gpu_new_budget(int device, const mx_plan* plan, int64_t budget_bytes, mx_
       for (int32_t c : ss.covers) g->primary_of[size_t(c)] = ss.op;
       g->sched_flags[size_t(ss.op)] = (ss.stats_only ? MX_SCHED_STATS_ONLY : 0) |
                                       (ss.ln_stats >= 0 ? MX_SCHED_LN_ON_LOAD : 0);
-      if (ss.ln_out_op >= 0) g->sched_flags[size_t(ss.ln_out_op)] |= MX_SCHED_LN_IN_EPILOGUE;
+      if (ss.ln_out_op >= 0)
+        g->sched_flags[size_t(ss.ln_out_op)] |= MX_SCHED_LN_IN_EPILOGUE | (ss.ln_out_only ? MX_SCHED_LN_INPUT_UNSTORED : 0);
     }
     add_boundary_steps(*g, g->fsteps, &g->foffs);
     for (auto& st : g->fsteps) g->kernels += st.kernels;
@@ -1882,7 +1883,8 @@ int mx_plan_schedule(const mx_plan* plan, mx_gpu_stats* stats, int32_t* primary,
       for (int32_t i = 0; i < n_ops; ++i) flags[i] = 0;
       for (const SchedStep& ss : S.steps) {
         flags[ss.op] = (ss.stats_only ? MX_SCHED_STATS_ONLY : 0) | (ss.ln_stats >= 0 ? MX_SCHED_LN_ON_LOAD : 0);
-        if (ss.ln_out_op >= 0) flags[ss.ln_out_op] |= MX_SCHED_LN_IN_EPILOGUE;
+        if (ss.ln_out_op >= 0)
+          flags[ss.ln_out_op] |= MX_SCHED_LN_IN_EPILOGUE | (ss.ln_out_only ? MX_SCHED_LN_INPUT_UNSTORED : 0);
       }
     }
   });

@@ -66,15 +66,18 @@ def schedule_steps(primary):
     return out
 
 
-SCHED_STATS_ONLY, SCHED_LN_ON_LOAD = 1, 2
+SCHED_STATS_ONLY, SCHED_LN_ON_LOAD, SCHED_LN_IN_EPILOGUE, SCHED_LN_INPUT_UNSTORED = 1, 2, 4, 8
 
 
 def step_work(plan, ops, members, flags=None):
     """(family, flops, bytes) of one scheduled step. The members' own work,
     less what fusion removes: each absorbed op (an epilogue or a forwarded
     Copy) consumed a tensor its producer no longer writes and it no longer
-    reads, the size of its own output. A LayerNorm reduced to its statistics
-    reads its input and writes 8 bytes per pixel."""
+    reads, the size of its own output. A LayerNorm that the epilogue writes
+    whole (SCHED_LN_IN_EPILOGUE) normalises a tensor that other ops read too,
+    so its producer still writes it and only the LayerNorm's read goes -
+    unless no other op reads it (SCHED_LN_INPUT_UNSTORED). A LayerNorm
+    reduced to its statistics reads its input and writes 8 bytes per pixel."""
     p = members[0]
     f, b = op_work(plan, ops[p])
     fam = [KINDS[ops[p].kind]]
@@ -89,7 +92,9 @@ def step_work(plan, ops, members, flags=None):
         fj, bj = op_work(plan, ops[j])
         c, h, w = plan.buf(ops[j].dst)
         f += fj
-        b += bj - 8 * c * h * w
+        fj_flags = 0 if flags is None else int(flags[j])
+        whole_ln = fj_flags & SCHED_LN_IN_EPILOGUE and not fj_flags & SCHED_LN_INPUT_UNSTORED
+        b += bj - (4 if whole_ln else 8) * c * h * w
         if KINDS[ops[j].kind] in TAILS:
             fam.append(KINDS[ops[j].kind])
     return "+".join(fam), f, b

@@ -95,3 +95,36 @@ def test_schedule_without_tensor_cores_fuses_only_copies(mx):
     for i in np.nonzero(moved & np.isin(kinds, [GELU, 5, 6]))[0]:  # GELU / LeakyReLU / sigmoid: a small conv's tail
         p = ops[primary[i]]
         assert p.kind == CONV1X1 and p.h * p.wd < 128
+
+
+def test_step_work_counts_what_a_fused_step_must_move(mx):
+    """The roofline numerators: a fused step moves its members' bytes less
+    the intermediates fusion removes. A GELU tail removes its input both
+    ways (the conv no longer writes it, the GELU no longer reads it); a
+    LayerNorm written whole by the epilogue normalises a tensor that other
+    ops still read, so only its read goes and its own output is counted;
+    where nothing else reads that tensor, it goes both ways like the GELU's."""
+    import importlib
+    work = importlib.import_module("maxim-rs_b200.work")
+    plan = mx.Plan(None, 256, 320, variant="S-3")
+    ops = plan.ops()
+    _, prim, flags = mx.plan_schedule(plan, flags=True)
+    seen_gelu = seen_ln = False
+    for p, members in work.schedule_steps(prim).items():
+        fam, f, b = work.step_work(plan, ops, members, flags)
+        if flags[p] & mx._native.SCHED_STATS_ONLY:  # a LayerNorm reduced to its statistics
+            o = ops[p]
+            assert fam == "ln_stats" and b == 4 * o.c * o.hw + 8 * o.hw
+            continue
+        own = sum(work.op_work(plan, ops[j])[1] for j in members)
+        removed = 0
+        for j in members[1:]:
+            c, h, w = plan.buf(ops[j].dst)
+            if flags[j] & mx._native.SCHED_LN_IN_EPILOGUE and not flags[j] & mx._native.SCHED_LN_INPUT_UNSTORED:
+                removed += 4 * c * h * w
+                seen_ln = True
+            else:
+                removed += 8 * c * h * w
+                seen_gelu |= ops[j].kind == GELU
+        assert b == own - removed
+    assert seen_gelu and seen_ln
