@@ -504,8 +504,8 @@ Step umma_gate_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
         const uint64_t px = uint64_t(v.stride) * 4;
         sv[0] = px, sv[1] = fw * px, sv[2] = fw * gw * px, sv[3] = fh * fw * gw * px;
       };
-      uint64_t sa[4], sd[4];
-      strides(x, sa), strides(d, sd);
+      uint64_t sa[4], sd[4], se[4];
+      strides(x, sa), strides(d, sd), strides(e, se);
       uint32_t box[5];
       if (op.mode == 0) {  // grid gating: t = cell, a group = a position in the cell
         box[0] = 32, box[1] = 1, box[2] = uint32_t(gw), box[3] = 1, box[4] = uint32_t(32 / gw);
@@ -516,7 +516,8 @@ Step umma_gate_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
       }
       u->a = make_tensor_map(x.ptr, 5, dims, sa, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
       u->d = make_tensor_map(d.ptr, 5, dims, sd, box);
-      u->l = u->d;
+      // The gate operand, read by the epilogue in the output's boxes.
+      u->l = E.epi >= EPI_ADD ? make_tensor_map(e.ptr, 5, dims, se, box) : u->d;
       u->mode = MODE_GATE_SP;
       u->p.sp_mode = op.mode == 0 ? 0 : 1;
       u->p.fw = P.fw;
@@ -547,7 +548,8 @@ Step umma_gate_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
       uint32_t bd[3] = {box[0], box[1], 1};
       if (op.mode == 0) bd[1] = 1, bd[2] = 32;
       u->d = make_tensor_map(d.ptr, 3, dims, sd, bd);
-      u->l = u->d;
+      const uint64_t se[2] = {uint64_t(e.stride) * 4, pp * uint64_t(e.stride) * 4};
+      u->l = E.epi >= EPI_ADD ? make_tensor_map(e.ptr, 3, dims, se, bd) : u->d;
     }
     u->p.n_slices = n / tn;
     u->p.tiles_x = (u->p.groups + 3) / 4;
@@ -992,7 +994,7 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
             memset(&c, 0, sizeof(c));
             for (int oo = 0; oo < 32 && int(k) * 32 + oo < co; ++oo) {
               const int oc = int(k) * 32 + oo;
-              for (int t = 0; t < 27; ++t) c.w[oo * 27 + t] = wk[size_t(oc) * 27 + t];
+              for (int t = 0; t < 27; ++t) c.w[t * 32 + oo] = wk[size_t(oc) * 27 + t];
               c.b[oo] = bk.empty() ? 0.0f : bk[size_t(oc)];
             }
           }

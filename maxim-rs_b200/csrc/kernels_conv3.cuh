@@ -122,10 +122,13 @@ __global__ void __launch_bounds__(256) conv3x3_cout3_kernel(int h, int wd, int c
 // and every output's sum runs in the same order as in the kernels above, so
 // the results are theirs bit for bit.
 //
-// c_in == 3, one 32-output-channel chunk per launch (weights [o][tap][c],
-// 27 per output): one output pixel per thread, all 32 outputs.
-struct Cin3Weights {
-  float w[32 * 27];
+// c_in == 3, one 32-output-channel chunk per launch: one output pixel per
+// thread, all 32 outputs. The weights are [k = (ky, kx, c)][output], so the
+// two weights of an output pair are one 8-byte constant: the multiply-adds
+// run paired (f32x2), half the instructions and half the constant-bank
+// reads (which set this kernel's pace when each multiply-add read its own).
+struct alignas(16) Cin3Weights {
+  float w[27 * 32];
   float b[32];
 };
 __global__ void __launch_bounds__(128) conv3x3_cin3c_kernel(int h, int wd, int n, const float* __restrict__ x, int sx,
@@ -146,13 +149,20 @@ __global__ void __launch_bounds__(128) conv3x3_cin3c_kernel(int h, int wd, int n
 #pragma unroll
       for (int c = 0; c < 3; ++c) in[(ky * 3 + kx) * 3 + c] = ok ? __ldg(s + c) : 0.0f;
     }
+  uint64_t acc2[16];
+  const uint64_t* b2 = reinterpret_cast<const uint64_t*>(cw.b);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) acc2[j] = b2[j];
+#pragma unroll
+  for (int k = 0; k < 27; ++k) {
+    const uint64_t v = f2_pack(in[k], in[k]);
+    const uint64_t* w2 = reinterpret_cast<const uint64_t*>(cw.w + k * 32);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc2[j] = f2_fma(v, w2[j], acc2[j]);
+  }
   float acc[32];
 #pragma unroll
-  for (int o = 0; o < 32; ++o) acc[o] = cw.b[o];
-#pragma unroll
-  for (int k = 0; k < 27; ++k)
-#pragma unroll
-    for (int o = 0; o < 32; ++o) acc[o] = fmaf(in[k], cw.w[o * 27 + k], acc[o]);
+  for (int j = 0; j < 16; ++j) f2_unpack(acc2[j], acc[2 * j], acc[2 * j + 1]);
   // The block's 128 x 32 outputs go through shared memory (rows padded to
   // 36 floats: conflict-free float4 access both ways), so each warp-wide
   // store writes four whole 128-byte pixel chunks instead of 32 scattered

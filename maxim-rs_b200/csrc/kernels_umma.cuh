@@ -240,7 +240,7 @@ struct UmmaCfg {
   static constexpr int A_COL0 = ACC_SETS * 2 * N;  // first TMEM column of the A_lo slots
   static constexpr int TMEM_COLS = TMEM_A ? 512 : ACC_SETS * 2 * N;
   static constexpr int SMEM_BYTES =
-      1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 8 * (3 * STAGES + 2 * ACC_SETS) + 16;
+      1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 8 * (3 * STAGES + 2 * ACC_SETS + EPI_WARPS) + 16;
   static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
   static_assert(!TMEM_A || A_COL0 + STAGES * 32 <= 512, "TMEM holds the accumulators and the A_lo slots");
   static_assert(2 * N <= 256, "one instruction covers B_hi and B_lo");
@@ -313,7 +313,8 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
   uint64_t* empty = lo_ready + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;
   uint64_t* acc_empty = acc_full + C::ACC_SETS;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + C::ACC_SETS);
+  uint64_t* ebar = acc_empty + C::ACC_SETS;  // per epilogue warp: its gate operand tile has landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + C::EPI_WARPS);
   __shared__ int abort_flag;
   const volatile int* vabort = &abort_flag;
 
@@ -351,12 +352,13 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 128);
     }
+    for (int w = 0; w < C::EPI_WARPS; ++w) mbar_init(&ebar[w], 1);
     fence_mbar_init();
     tma_prefetch(&tmA);
     tma_prefetch(&tmB);
     tma_prefetch(&tmBlo);
     tma_prefetch(&tmD);
-    if (MODE == MODE_CONV1 && p.lo_scale) tma_prefetch(&tmL);
+    if ((MODE == MODE_CONV1 && p.lo_scale) || (GATE && E)) tma_prefetch(&tmL);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -739,18 +741,22 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
     const int set = ew >> 2;
     const int q = warp & 3;         // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;  // accumulator row this thread owns
-    constexpr int NE = E ? 32 : 1;  // operand values held per thread
+    // The gating instances take their second operand (the gate) by TMA into
+    // the warp's staging buffer, in the layout the output is staged in, so
+    // each thread reads its values where it then writes its results; the
+    // others hold it in registers, loaded one chunk ahead.
+    constexpr bool TMA_E = GATE && E;
+    constexpr int NE = E && !GATE ? 32 : 1;  // operand values held per thread
     uint8_t* sb = staging + ew * 4096;
+    uint32_t euse = 0;  // gate tiles this warp has taken from ebar
 
-    // The second operand's values for this thread in chunk j of tile t: for
-    // row layouts its output pixel's 32 channels, for gating layouts its
-    // channel at the chunk's 32 output positions of its group.
+    // The second operand's values for this thread in chunk j of tile t: its
+    // output pixel's 32 channels.
     auto load_e = [&](int t, int j, float(&e)[NE]) {
-      if constexpr (E) {
-      int a0, a1, n0;
-      decode(t, a0, a1, n0);
-      const int col = n0 + j * 32;
-      if (!GATE) {
+      if constexpr (E && !GATE) {
+        int a0, a1, n0;
+        decode(t, a0, a1, n0);
+        const int col = n0 + j * 32;
         int pix;
         bool ok;
         if (MODE == MODE_CONV1) {
@@ -767,56 +773,33 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
           const float4 v = ok ? src[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
           e[4 * i] = v.x, e[4 * i + 1] = v.y, e[4 * i + 2] = v.z, e[4 * i + 3] = v.w;
         }
-      } else if (MODE == MODE_GATE_SP) {
-        // Positions col .. col + 31 of group G, in rows of 1 << sp_shift
-        // positions: consecutive positions lie sc pixels apart, rows sr
-        // pixels apart (grid gating: position = cell, group = the pixel's
-        // place in its cell; block gating: position = place in the block,
-        // group = the block). With the row length a compile-time constant
-        // every load's offset is one add from the last.
-        const int G = a0 + q;
-        const bool ok = G < p.groups;
-        int pix0, sc, sr;
-        if (p.sp_mode == 0) {
-          const int fx = G % p.fw, fy = G / p.fw;
-          pix0 = ((col >> p.sp_shift) * p.fh + fy) * p.e_w + fx;
-          sc = p.fw, sr = p.fh * p.e_w;
-        } else {
-          const int gx = G % p.gw, gy = G / p.gw;
-          pix0 = (gy * p.fh + (col >> p.sp_shift)) * p.e_w + gx * p.fw;
-          sc = 1, sr = p.e_w;
-        }
-        const float* src = p.eptr + a1 + lane + size_t(ok ? pix0 : 0) * p.estride;
-        const int dc = sc * p.estride, dr = sr * p.estride;
-        auto rows = [&](auto lg) {
-          constexpr int RL = 1 << decltype(lg)::value;
-#pragma unroll
-          for (int r = 0; r < 32 / RL; ++r)
-#pragma unroll
-            for (int c = 0; c < RL; ++c) e[r * RL + c] = ok ? src[r * dr + c * dc] : 0.0f;
-        };
-        switch (p.sp_shift) {
-          case 0: rows(std::integral_constant<int, 0>()); break;
-          case 1: rows(std::integral_constant<int, 1>()); break;
-          case 2: rows(std::integral_constant<int, 2>()); break;
-          case 3: rows(std::integral_constant<int, 3>()); break;
-          case 4: rows(std::integral_constant<int, 4>()); break;
-          default: rows(std::integral_constant<int, 5>()); break;
-        }
-      } else {
-        const int G = a0 + q;
-        const bool ok = G < p.groups;
-        const float* src = p.eptr + a1 + lane;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int a = col + i;
-          const int pix = MODE == MODE_GATE ? G * p.e_pp + a : a * p.e_pp + G;
-          e[i] = ok ? src[size_t(pix) * p.estride] : 0.0f;
-        }
-      }
       }
     };
 
+    // The gate tile of chunk jj of tile tt: once the warp's previous store
+    // has read the staging buffer, TMA loads the group's (32 channel x 32
+    // position) box of the gate operand into it. It is issued as soon as the
+    // previous chunk's store has gone out, so the load overlaps the wait for
+    // the next accumulator and the TMEM loads (lane 0 only).
+    auto gate_load = [&](int tt, int jj) {
+      if constexpr (TMA_E) {
+        bulk_wait_read<0>();
+        int b0, b1, m0;
+        decode(tt, b0, b1, m0);
+        if (b0 + q >= p.groups) return;
+        const int col = m0 + jj * 32;
+        mbar_arrive_expect_tx(&ebar[ew], 4096);
+        if (MODE == MODE_GATE) {
+          tma_load_3d(sb, &tmL, &ebar[ew], b1, col, b0 + q);
+        } else if (MODE == MODE_GATE_GRID) {
+          tma_load_3d(sb, &tmL, &ebar[ew], b1, b0 + q, col);
+        } else {
+          int fx, gx, fy, gy;
+          gate_sp_coords(p, b0 + q, col, fx, gx, fy, gy);
+          tma_load_5d(sb, &tmL, &ebar[ew], b1, fx, gx, fy, gy);
+        }
+      }
+    };
     const int tstep = C::ACC_SETS * gridDim.x;
     int t = blockIdx.x + set * gridDim.x, j = 0, a0 = 0, a1 = 0, n0 = 0;
     // LayerNorm statistics of this thread's output pixel, one serial pair of
@@ -839,6 +822,8 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
         tc_fence_after();
         decode(t, a0, a1, n0);
       }
+      // A group past the last is neither loaded nor stored.
+      const bool gvalid = GATE && a0 + q < p.groups;
       const uint32_t tcol = tmem + (uint32_t(q * 32) << 16) + set * 2 * N + j * 32;
       // The chunk whose LayerNorm this step also writes (below).
       const bool lnc = MODE == MODE_CONV1 && p.lo_scale != nullptr && n0 + j * 32 == p.lo_col;
@@ -873,10 +858,30 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
             }
           }
         }
+        if constexpr (TMA_E) {
+          if (h == 0 && gvalid) {
+            bool ok = mbar_wait(&ebar[ew], euse & 1, vabort);
+            ++euse;
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+              if (lane == 0) fail(kErrEpilogue);
+              return false;
+            }
+          }
+          // This thread's channel at positions h * 16 + i: where it stages
+          // its results below.
+          const float* g = reinterpret_cast<const float*>(sb);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          if constexpr (E) e[i] = ecur[h * 16 + i];
-          else e[i] = 0.0f;
+          for (int i = 0; i < 16; ++i) {
+            const int r = h * 16 + i;
+            e[i] = gvalid ? g[r * 32 + (((lane >> 2) ^ (r & 7)) << 2) + (lane & 3)] : 0.0f;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if constexpr (E) e[i] = ecur[h * 16 + i];
+            else e[i] = 0.0f;
+          }
         }
         epi_apply(p.epi, v, e, p.slope);
         if (!GATE && MODE != MODE_CONVT && p.st_out[0]) {
@@ -909,10 +914,11 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
             }
           }
         }
-        if (h == 0) {
+        if (!TMA_E && h == 0) {
           // This warp's previous store must have read the staging buffer;
           // waiting only now lets that read overlap the TMEM loads and the
-          // arithmetic above.
+          // arithmetic above. (The gating instances waited before their
+          // gate tile's load.)
           if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
         }
@@ -1006,14 +1012,16 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
         }
       }
       if (++j == N / 32) j = 0, t += tstep;
-      if (E && t < p.tiles) load_e(t, j, ecur);
+      if (E && !GATE && t < p.tiles) load_e(t, j, ecur);
+      if (TMA_E && lane == 0 && t < p.tiles) gate_load(t, j);
       return true;
     };
 
     float e[NE];
 #pragma unroll
     for (int i = 0; i < NE; ++i) e[i] = 0.0f;
-    if (E && t < p.tiles) load_e(t, 0, e);
+    if (E && !GATE && t < p.tiles) load_e(t, 0, e);
+    if (TMA_E && lane == 0 && t < p.tiles) gate_load(t, 0);
     while (t < p.tiles && step(e)) {
     }
     if (lane == 0) bulk_wait<0>();
