@@ -450,6 +450,7 @@ int64_t cached(mx_gpu& g, int32_t id, int tag, const std::function<std::vector<f
 struct UmmaEpi {
   int epi = EPI_NONE;
   int32_t src = -1;
+  int32_t src2 = -1;  // a channel scale's second residual
   float slope = 0.0f;
   bool spatial = false;
   mx_op perm{};
@@ -762,6 +763,7 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
   if (fs) {
     E.epi = fs->epi;
     E.src = fs->epi_src;
+    E.src2 = fs->epi_src2;
     E.slope = fs->epi_slope;
     if (fs->gate_perm >= 0) {
       E.spatial = true;
@@ -888,6 +890,21 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
       break;
     }
     case MX_OP_CHAN_SCALE: {
+      if (E.epi == EPI_ADD && E.src2 >= 0) {
+        // ((x * s) + residual) + residual 2 in one pass (views 4-channel
+        // aligned, checked by the schedule).
+        const int32_t res = E.src, res2 = E.src2;
+        st.run = [G, L, dst, src, src2, res, res2](cudaStream_t s) {
+          View d = view_of(*G, *L, dst), x = view_of(*G, *L, src), sc = view_of(*G, *L, src2),
+               r = view_of(*G, *L, res), r2 = view_of(*G, *L, res2);
+          const int c4 = int(x.c / 4), total4 = int(x.npix) * c4;
+          chan_scale_add2_4_kernel<<<blocks_for(total4, TPB), TPB, 0, s>>>(
+              total4, c4, x.ptr, int(x.stride), sc.ptr, r.ptr, int(r.stride), r2.ptr, int(r2.stride), d.ptr,
+              int(d.stride));
+        };
+        on_umma = needs_umma = false;
+        break;
+      }
       if (E.epi == EPI_ADD) {
         // x * s + residual in one pass (the schedule checked the views are
         // 4-channel aligned).

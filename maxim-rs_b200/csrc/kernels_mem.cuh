@@ -233,6 +233,25 @@ __global__ void chan_scale_add4_kernel(int total4, int c4, const float* __restri
                   __fadd_rn(__fmul_rn(v.z, g.z), e.z), __fadd_rn(__fmul_rn(v.w, g.w), e.w));
 }
 
+// ((x * s) + r) + r2: the channel scale and two residual adds in one pass,
+// each operation rounded on its own as the three separate ops round it.
+__global__ void chan_scale_add2_4_kernel(int total4, int c4, const float* __restrict__ x, int sx,
+                                         const float* __restrict__ s, const float* __restrict__ r, int sr,
+                                         const float* __restrict__ r2, int sr2, float* __restrict__ d, int sd) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total4) return;
+  int p = i / c4, c = (i - p * c4) * 4;
+  float4 v = *reinterpret_cast<const float4*>(x + size_t(p) * sx + c);
+  float4 g = *reinterpret_cast<const float4*>(s + c);
+  float4 e = *reinterpret_cast<const float4*>(r + size_t(p) * sr + c);
+  float4 f = *reinterpret_cast<const float4*>(r2 + size_t(p) * sr2 + c);
+  *reinterpret_cast<float4*>(d + size_t(p) * sd + c) =
+      make_float4(__fadd_rn(__fadd_rn(__fmul_rn(v.x, g.x), e.x), f.x),
+                  __fadd_rn(__fadd_rn(__fmul_rn(v.y, g.y), e.y), f.y),
+                  __fadd_rn(__fadd_rn(__fmul_rn(v.z, g.z), e.z), f.z),
+                  __fadd_rn(__fadd_rn(__fmul_rn(v.w, g.w), e.w), f.w));
+}
+
 // Resize passes, 4 channels per thread, same tap tables and the same
 // per-channel arithmetic as the scalar kernels (acc over taps ascending with
 // non-contracting ops, then acc / wsum if wsum > 0). One block row of threads

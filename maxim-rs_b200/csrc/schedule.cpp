@@ -78,10 +78,11 @@ int reads_of(const mx_op& o, int32_t extra, int32_t* r) {
   if (extra >= 0) r[n++] = extra;
   return n;
 }
-// Everything a scheduled step reads: its op's inputs, the epilogue operand
-// and the LayerNorm statistics it normalises with. r holds 4.
+// Everything a scheduled step reads: its op's inputs, the epilogue
+// operands and the LayerNorm statistics it normalises with. r holds 5.
 int step_reads(const SchedStep& st, int32_t* r) {
   int n = reads_of(st.o, st.epi_src, r);
+  if (st.epi_src2 >= 0) r[n++] = st.epi_src2;
   if (st.ln_stats >= 0) r[n++] = st.ln_stats;
   return n;
 }
@@ -271,7 +272,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
       bool ok = true;
       for (size_t s = i + 1; s < W.size() && ok; ++s) {
         if (dead[s]) continue;
-        int32_t r[4], w[2];
+        int32_t r[5], w[2];
         const int nr = step_reads(W[s], r), nw = writes_of(W[s].o, w);
         for (int a = 0; a < nr; ++a)
           if (G.overlap(r[a], T)) {
@@ -327,8 +328,9 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
         if (umma && !H.tma_view(D, out_channels(A.o))) break;
       } else if (A.o.kind == MX_OP_CHAN_SCALE) {
         // The channel-attention tail x * s + residual: one pass over x and
-        // the residual (all views 4-channel aligned for the vector kernel).
-        if (epi != EPI_ADD || A.epi != EPI_NONE) break;
+        // the residual (all views 4-channel aligned for the vector kernel);
+        // a second residual add that follows joins it too.
+        if (epi != EPI_ADD || A.epi_src2 >= 0 || (A.epi != EPI_NONE && A.epi != EPI_ADD)) break;
         if (!H.tma_view(D, A.o.c) || !H.tma_view(operand, A.o.c) || !H.tma_view(A.o.src, A.o.c)) break;
       } else if (H.small_conv && H.small_conv(A.o)) {
         if (A.epi != EPI_NONE || operand >= 0 || (epi != EPI_GELU && epi != EPI_LRELU && epi != EPI_SIGMOID)) break;
@@ -343,7 +345,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
       const int nbr = reads_of(B.o, -1, br);
       for (size_t s = i + 1; s < j && ok; ++s) {
         if (dead[s]) continue;
-        int32_t r[4], w[2];
+        int32_t r[5], w[2];
         const int nr = step_reads(W[s], r), nw = writes_of(W[s].o, w);
         for (int a = 0; a < nw; ++a) {
           for (int b = 0; b < nbr; ++b)
@@ -353,20 +355,61 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
         for (int a = 0; a < nr; ++a)
           if (G.overlap(r[a], D)) ok = false;
       }
+      // Where the consumer's position is what stands in the way (its other
+      // operand is produced in between, most often), a tensor-core producer
+      // with no epilogue yet can run there instead: nothing in between may
+      // then write what it reads (its output has no other reader).
+      bool sink = false;
+      if (!ok && umma && A.epi == EPI_NONE && A.stats_out[0] < 0 && A.ln_out < 0 &&
+          A.o.kind != MX_OP_CHAN_SCALE && !(H.small_conv && H.small_conv(A.o))) {
+        int32_t ar2[5];
+        const int na2 = step_reads(A, ar2);
+        sink = true;
+        for (size_t s = i + 1; s < j && sink; ++s) {
+          if (dead[s]) continue;
+          int32_t w[5];
+          const int nw = step_writes(W[s], w);
+          for (int a = 0; a < nw; ++a)
+            for (int b = 0; b < na2; ++b)
+              if (G.overlap(w[a], ar2[b])) sink = false;
+        }
+        ok = sink;
+      }
       if (!ok) break;
       // The destination against what the producer itself reads: an exact
       // match is an in-place elementwise update (each value is read before
       // the same thread writes it), anything else is refused.
-      int32_t ar[4];
+      int32_t ar[5];
       const int nar = step_reads(A, ar);
       for (int a = 0; a < nar; ++a)
-        if (G.overlap(ar[a], D) && !(ar[a] == D && (elementwise(A.o.kind) || ar[a] == A.epi_src))) ok = false;
+        if (G.overlap(ar[a], D) &&
+            !(ar[a] == D && (elementwise(A.o.kind) || ar[a] == A.epi_src || ar[a] == A.epi_src2)))
+          ok = false;
       if (operand >= 0 && G.overlap(operand, D) && operand != D) ok = false;
       if (operand >= 0 && operand == D && !umma && A.o.kind != MX_OP_CHAN_SCALE) ok = false;
       if (G.overlap(D, T) && D != T) ok = false;
       if (!ok) break;
+      if (sink) {
+        // The fused step takes the consumer's place in the order.
+        SchedStep moved = std::move(W[i]);
+        const std::vector<int32_t> bc = W[j].covers;
+        moved.o.dst = D;
+        if (!identity) {
+          moved.epi = epi;
+          moved.epi_src = operand;
+          moved.epi_slope = W[j].o.slope;
+        }
+        moved.covers.insert(moved.covers.end(), bc.begin(), bc.end());
+        W[j] = std::move(moved);
+        dead[i] = 1;
+        S.ops_fused += int(bc.size());
+        ++S.steps_moved;
+        break;
+      }
       A.o.dst = D;
-      if (!identity) {
+      if (!identity && A.o.kind == MX_OP_CHAN_SCALE && A.epi == EPI_ADD) {
+        A.epi_src2 = operand;
+      } else if (!identity) {
         A.epi = epi;
         A.epi_src = operand;
         A.epi_slope = B.o.slope;
@@ -394,7 +437,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     bool ok = true, src_written = false;
     for (size_t s = c + 1; s < W.size() && ok; ++s) {
       if (dead[s]) continue;
-      int32_t r[4], w[5];
+      int32_t r[5], w[5];
       const int nr = step_reads(W[s], r), nw = step_writes(W[s], w);
       bool reads_d = false;
       for (int a = 0; a < nr; ++a)
@@ -419,6 +462,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
       if (R.o.src == D) R.o.src = Sr;
       if (R.o.src2 == D) R.o.src2 = Sr;
       if (R.epi_src == D) R.epi_src = Sr;
+      if (R.epi_src2 == D) R.epi_src2 = Sr;
     }
     dead[c] = 1;
     ++S.copies_elided;
@@ -436,7 +480,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     bool ok = true;
     for (size_t s = j + 1; s < W.size() && ok; ++s) {
       if (dead[s]) continue;
-      int32_t r[4], w[2];
+      int32_t r[5], w[2];
       const int nr = step_reads(W[s], r), nw = writes_of(W[s].o, w);
       for (int a = 0; a < nr; ++a)
         if (G.overlap(r[a], y)) {
@@ -453,7 +497,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     }
     if (!ok || k == SIZE_MAX) continue;
     SchedStep& C = W[k];
-    if (C.o.src != y || C.o.src2 == y || C.epi_src == y || C.ln_stats >= 0) continue;
+    if (C.o.src != y || C.o.src2 == y || C.epi_src == y || C.epi_src2 == y || C.ln_stats >= 0) continue;
     mx_op as_read = C.o;
     as_read.src = x;
     if (!H.umma(as_read) || !H.ln_on_load(as_read)) continue;
@@ -546,12 +590,12 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     const int64_t c0 = G.lo[size_t(x)] - G.lo[size_t(P.o.dst)], c = G.hi[size_t(x)] - G.lo[size_t(x)];
     if (c != 32 || c0 % 32 != 0) continue;
     if (G.overlap(y, p.output) || G.overlap(y, P.o.dst)) continue;
-    int32_t pr[4];
+    int32_t pr[5];
     const int npr = step_reads(P, pr);
     for (int a = 0; a < npr; ++a) ok = ok && !G.overlap(pr[a], y);
     for (size_t s = i + 1; s < j && ok; ++s) {
       if (dead[s]) continue;
-      int32_t r[4], w[5];
+      int32_t r[5], w[5];
       const int nr = step_reads(W[s], r), nw = step_writes(W[s], w);
       for (int a = 0; a < nr; ++a) ok = ok && !G.overlap(r[a], y);
       for (int a = 0; a < nw; ++a) ok = ok && !G.overlap(w[a], y);
@@ -567,7 +611,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     bool read = G.overlap(x, p.output);
     for (size_t s = i + 1; s < W.size() && !read; ++s) {
       if (dead[s] || s == j) continue;
-      int32_t r[4], w[5];
+      int32_t r[5], w[5];
       const int nr = step_reads(W[s], r), nw = step_writes(W[s], w);
       for (int a = 0; a < nr; ++a) read = read || G.overlap(r[a], x);
       bool gone = false;
@@ -597,7 +641,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
   touch(p.input, -1);
   touch(p.output, m);
   for (int t = 0; t < m; ++t) {
-    int32_t r[4], w[5];
+    int32_t r[5], w[5];
     const int nr = step_reads(S.steps[size_t(t)], r);
     const int nw = step_writes(S.steps[size_t(t)], w);
     for (int a = 0; a < nr; ++a) touch(r[a], t);

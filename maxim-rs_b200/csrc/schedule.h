@@ -61,6 +61,9 @@ struct SchedStep {
   std::vector<int32_t> covers;  // every plan op this step carries out, primary first
   int epi = EPI_NONE;
   int32_t epi_src = -1;         // the epilogue's second operand
+  // A channel scale whose epilogue adds two residuals, ((x * s) + epi_src) +
+  // epi_src2 (two consecutive residual adds); -1 otherwise.
+  int32_t epi_src2 = -1;
   float epi_slope = 0.0f;
   // A gating matmul over spatial-order data: the plan op (a forward block
   // permutation, since dropped) whose blocking it reads through; -1 if it
@@ -98,6 +101,7 @@ struct Schedule {
   int stats_in_epilogue = 0;  // of those, statistics written by the producer's epilogue
   int ln_in_epilogue = 0;     // LayerNorms written whole by their producer's epilogue
   int copies_elided = 0;      // Copies whose readers read the source instead
+  int steps_moved = 0;        // producers run at their consumer's position to take it as an epilogue
 };
 
 struct ScheduleHooks {

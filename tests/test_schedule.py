@@ -128,3 +128,44 @@ def test_step_work_counts_what_a_fused_step_must_move(mx):
                 seen_gelu |= ops[j].kind == GELU
         assert b == own - removed
     assert seen_gelu and seen_ln
+
+
+def _steps_and_writers(mx, plan):
+    import importlib
+    work = importlib.import_module("maxim-rs_b200.work")
+    ops = plan.ops()
+    _, prim = mx.plan_schedule(plan)
+    writers = {}
+    for i, o in enumerate(ops):
+        writers.setdefault(o.dst, []).append(i)
+    return ops, work.schedule_steps(prim), writers
+
+
+def test_schedule_moves_a_producer_to_its_consumer(mx):
+    """A tensor-core conv whose only reader is a multiply by a tensor made
+    after the conv (the gMLP block's gelu(conv_a(x)) * conv_b(x), conv_b
+    first in the plan) runs at the multiply's position with the multiply as
+    its epilogue; nothing between the two rewrites the conv's input."""
+    plan = mx.Plan(None, 256, 320, variant="S-3")
+    ops, steps, writers = _steps_and_writers(mx, plan)
+    moved = 0
+    for p, members in steps.items():
+        if ops[p].kind not in (CONV1X1, CONV3X3):
+            continue
+        for m in members[1:]:
+            if ops[m].kind != 2:  # MUL
+                continue
+            other = ops[m].src2 if ops[m].src == ops[p].dst else ops[m].src
+            if any(p < w < m for w in writers.get(other, [])):
+                moved += 1
+                assert not any(p < w < m for w in writers.get(ops[p].src, []))
+    assert moved >= 21
+
+
+def test_schedule_channel_scale_takes_two_residual_adds(mx):
+    """x * s + r followed by + r2 is one channel-scale step over both adds."""
+    plan = mx.Plan(None, 256, 320, variant="S-3")
+    ops, steps, _ = _steps_and_writers(mx, plan)
+    two = [p for p, members in steps.items()
+           if ops[p].kind == 9 and sum(ops[m].kind == ADD for m in members) == 2]
+    assert len(two) >= 24
