@@ -41,6 +41,7 @@
 #include "kernels_conv3.cuh"
 #include "kernels_mem.cuh"
 #include "kernels_umma.cuh"
+#include "kernels_conv3f.cuh"
 #include "maxim_b200.h"
 #include "schedule.h"
 
@@ -387,6 +388,8 @@ void umma_attrs_once() {
                                UmmaCfg<NN, MM>::SMEM_BYTES));
   MX_UMMA_INSTANCES(MX_UMMA_ATTR)
 #undef MX_UMMA_ATTR
+  MX_CUDA(cudaFuncSetAttribute(umma_conv3f_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Conv3fCfg::SMEM_BYTES));
   done = true;
 }
 int umma_smem(int n, int mode) {
@@ -429,6 +432,7 @@ enum WeightTag : int {
   WT_CONVT_LO = 8,
   WT_BIAS4 = 9,  // a bias repeated once per transposed-conv tap
   WT_T = 10,     // a 1x1 kernel transposed to [c_in][c_out] (the small-conv kernel)
+  WT_CONV3F = 11,  // a 32-to-32 3x3 kernel for umma_conv3f_kernel: [ky][hi, lo][kx][c_out][c_in]
 };
 int64_t cached(mx_gpu& g, int32_t id, int tag, const std::function<std::vector<float>()>& make) {
   if (id < 0) return -1;
@@ -678,6 +682,77 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
     u->smem = umma_smem(tn, u->mode);
   };
   st.run = [u](cudaStream_t s) { launch_umma(s, *u); };
+  return st;
+}
+
+// The 32-to-32 3x3 conv on umma_conv3f_kernel (MAXIM_NO_CONV3F=1 keeps it
+// on umma_conv_kernel): 4 x 30 output-pixel tiles, the A box 32 x 6 input
+// pixels around each, the weights (WT_CONV3F layout) resident in shared
+// memory. Its epilogue takes every tail a schedule gives a 3x3 conv (unary,
+// add, multiply) but no LayerNorm statistics, which the schedule therefore
+// never assigns it, so the scheduled pass and the op-by-op walk run every
+// such conv on this kernel alike.
+bool conv3f_shape(const mx_gpu& g, const Layout& L, const mx_op& o) {
+  if (o.kind != MX_OP_CONV3X3 || o.c_in != 32 || o.c_out != 32 || !umma_eligible(g, L, o)) return false;
+  const char* off = std::getenv("MAXIM_NO_CONV3F");
+  return !(off && *off && std::strcmp(off, "0") != 0);
+}
+bool conv3f_eligible(const mx_gpu& g, const Layout& L, const mx_op& o, const UmmaEpi& E) {
+  if (!conv3f_shape(g, L, o) || E.epi == EPI_GATE) return false;
+  return E.ln_stats < 0 && E.st_out[0] < 0 && E.st_out[1] < 0 && E.lo_dst < 0 && !E.spatial;
+}
+struct Conv3fOp {
+  CUtensorMap a, w, d, e;
+  UmmaConvParams p{};
+  int grid = 0;
+};
+Step umma_conv3f_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int64_t wf, int64_t bo,
+                      const UmmaEpi& E) {
+  auto u = std::make_shared<Conv3fOp>();
+  mx_gpu* G = &g;
+  const mx_op op = o;
+  ++g.umma_ops;
+  Step st{oi, 1, nullptr, nullptr};
+  st.prepare = [G, L, u, op, wf, bo, E]() {
+    View x = view_of(*G, *L, op.src), d = view_of(*G, *L, op.dst);
+    const int H = op.h, W = op.wd;
+    {
+      uint64_t dims[2] = {32, 3 * 2 * 96}, str[1] = {32 * 4};
+      uint32_t box[2] = {32, 2 * 96};
+      u->w = make_tensor_map(reinterpret_cast<const float*>(G->pool.dev + wf), 2, dims, str, box);
+    }
+    uint64_t da[3] = {32, uint64_t(W), uint64_t(H)};
+    uint64_t sa[2] = {uint64_t(x.stride) * 4, uint64_t(W) * uint64_t(x.stride) * 4};
+    uint32_t ba[3] = {32, Conv3fCfg::BOX_W, Conv3fCfg::BOX_H};
+    u->a = make_tensor_map(x.ptr, 3, da, sa, ba);
+    uint64_t dd[3] = {32, uint64_t(W), uint64_t(H)};
+    uint64_t sd[2] = {uint64_t(d.stride) * 4, uint64_t(W) * uint64_t(d.stride) * 4};
+    uint32_t bd[3] = {32, Conv3fCfg::OUT_W, 1};  // per epilogue warp: one output row of the tile
+    u->d = make_tensor_map(d.ptr, 3, dd, sd, bd);
+    u->e = u->d;
+    if (E.epi >= EPI_ADD) {
+      // The binary tail's operand, read in the output's boxes.
+      View e = view_of(*G, *L, E.src);
+      uint64_t se[2] = {uint64_t(e.stride) * 4, uint64_t(W) * uint64_t(e.stride) * 4};
+      u->e = make_tensor_map(e.ptr, 3, dd, se, bd);
+    }
+    u->p.e_w = W;
+    u->p.e_h = H;
+    u->p.tiles_x = (W + Conv3fCfg::OUT_W - 1) / Conv3fCfg::OUT_W;
+    u->p.tiles = u->p.tiles_x * ((H + Conv3fCfg::OUT_H - 1) / Conv3fCfg::OUT_H);
+    u->p.n_slices = 1;
+    u->p.kb_per_tap = 1;
+    u->p.c_in = 32;
+    u->p.epi = E.epi;
+    u->p.slope = E.slope;
+    u->p.bias = bo < 0 ? nullptr : reinterpret_cast<const float*>(G->pool.dev + bo);
+    u->p.status = G->status;
+    u->grid = std::min(u->p.tiles, G->sms);
+  };
+  st.run = [u](cudaStream_t s) {
+    umma_conv3f_kernel<<<unsigned(u->grid), Conv3fCfg::THREADS, Conv3fCfg::SMEM_BYTES, s>>>(u->a, u->w, u->d,
+                                                                                           u->e, u->p);
+  };
   return st;
 }
 
@@ -989,6 +1064,25 @@ Step make_step(mx_gpu& g, const mx_plan& plan, const mx_op& o, int32_t oi, const
               wt[(size_t(oc) * ks * ks + t) * ci + ic] = w[(size_t(oc) * ci + ic) * ks * ks + t];
         return wt;
       };
+      if (ks == 3 && conv3f_eligible(g, *L, o, E)) {
+        // [co][tap][ci] split into TF32 halves, then [ky][hi, lo][kx][co][ci].
+        const int64_t wf = cached(g, o.w, WT_CONV3F, [&] {
+          std::vector<float> hi, lo;
+          split_tf32(ktap(), hi, lo);
+          std::vector<float> f(size_t(3 * 2 * 3 * 32 * 32));
+          for (int ky = 0; ky < 3; ++ky)
+            for (int part = 0; part < 2; ++part)
+              for (int kx = 0; kx < 3; ++kx)
+                for (int oc = 0; oc < 32; ++oc)
+                  for (int ic = 0; ic < 32; ++ic)
+                    f[((((size_t(ky) * 2 + part) * 3 + kx) * 32 + oc) * 32) + ic] =
+                        (part ? lo : hi)[(size_t(oc) * 9 + ky * 3 + kx) * 32 + ic];
+          return f;
+        });
+        st = umma_conv3f_step(g, oi, o, L, wf, raw(o.bias), E);
+        on_umma = true;
+        break;
+      }
       if (umma_eligible(g, *L, o)) {
         const auto hl = cached_split(g, o.w, WT_KTAP_HI, WT_KTAP_LO, ktap);
         st = umma_conv_step(g, oi, o, L, hl.first, hl.second, raw(o.bias), E);
@@ -1296,6 +1390,7 @@ ScheduleHooks schedule_hooks(const mx_gpu& g) {
   // per epilogue thread, one output slice at a time.
   h.stats_slice = [G](const mx_op& o) {
     if (o.kind != MX_OP_CONV1X1 && o.kind != MX_OP_CONV3X3 && o.kind != MX_OP_CONV4X4S2) return 0;
+    if (conv3f_shape(*G, G->roffs, o)) return 0;
     return umma_eligible(*G, G->roffs, o) ? umma_tile_n(o.c_out) : 0;
   };
   return h;
