@@ -209,6 +209,7 @@ struct mx_gpu {
   std::vector<int> step_of_op;  // op index -> step index
   std::vector<int64_t> roffs;   // each buffer's offset relative to its root (alignment checks)
   std::vector<int64_t> foffs;   // the scheduled pass's offsets
+  std::vector<int32_t> merged_into;  // per plan root: the root it is placed inside in the pass (-1: none)
   std::vector<mx::Step> fsteps; // the scheduled pass: [in-transpose, steps..., out-transpose]
   std::vector<int32_t> primary_of;  // plan op -> the op whose step carries it out (-1: dropped)
   std::vector<int32_t> sched_flags; // plan op -> MX_SCHED_* flags
@@ -253,8 +254,17 @@ int32_t root_of(const mx_gpu& g, int32_t id) {
 // plan's, or the scheduled pass's).
 using Layout = std::vector<int64_t>;
 
-View view_of(const mx_gpu& g, const Layout& L, int32_t id) {
+// The root whose pixel stride a buffer's view has in layout L: its plan
+// root, or in the scheduled pass the root that root is placed inside.
+int32_t base_of(const mx_gpu& g, const Layout& L, int32_t id) {
   int32_t base = root_of(g, id);
+  if (&L == &g.foffs && size_t(base) < g.merged_into.size() && g.merged_into[size_t(base)] >= 0)
+    base = g.merged_into[size_t(base)];
+  return base;
+}
+
+View view_of(const mx_gpu& g, const Layout& L, int32_t id) {
+  int32_t base = base_of(g, L, id);
   const mx_buf& b = g.bufs[size_t(id)];
   int64_t hw = b.h * b.w;
   int64_t ch0 = hw ? (L[size_t(id)] - L[size_t(base)]) / hw : 0;
@@ -300,7 +310,7 @@ struct ViewMeta {
   int64_t off, stride, c, npix;
 };
 ViewMeta meta_of(const mx_gpu& g, const Layout& L, int32_t id) {
-  int32_t base = root_of(g, id);
+  int32_t base = base_of(g, L, id);
   const mx_buf& b = g.bufs[size_t(id)];
   int64_t hw = b.h * b.w;
   int64_t ch0 = hw ? (L[size_t(id)] - L[size_t(base)]) / hw : 0;
@@ -1650,6 +1660,7 @@ int mx_gpu_new_budget(int device, const mx_plan* plan, int64_t budget_bytes, mx_
       g->roffs.push_back(0);
     }
     g->foffs = S.offs;
+    g->merged_into = S.merged_into;
     g->farena_len = S.arena_len;
     g->perms_dropped = S.perms_dropped;
     g->ops_fused = S.ops_fused;

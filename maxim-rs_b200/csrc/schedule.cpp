@@ -625,6 +625,56 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     ++S.ops_fused;
   }
 
+  // 3b. Merged placement. A Copy of a whole root Sr into a view D of
+  // another root (a concatenation copied into a wider one: the UpSampleRatio
+  // inputs stacked ahead of their 1x1 conv) moves nothing if Sr is placed
+  // where D is: the steps that write Sr's channel slices then write D's. That
+  // takes: Sr read by the Copy alone, written only before it, and nothing
+  // else touching D from Sr's first write to the Copy.
+  std::vector<int32_t> merge_root(size_t(p.n_bufs), -1);
+  std::vector<int64_t> merge_delta(size_t(p.n_bufs), 0);
+  std::vector<char> merge_target(size_t(p.n_bufs), 0);
+  for (size_t c = 0; fuse && c < W.size(); ++c) {
+    if (dead[c] || W[c].o.kind != MX_OP_COPY || p.ops[W[c].op].kind != MX_OP_COPY || W[c].epi != EPI_NONE ||
+        W[c].covers.size() != 1)
+      continue;
+    const int32_t Sr = W[c].o.src, D = W[c].o.dst;
+    if (Sr < 0 || D < 0 || Sr >= p.n_bufs || D >= p.n_bufs || G.root[size_t(Sr)] != Sr) continue;
+    const int32_t Dr = G.root[size_t(D)];
+    if (Dr == Sr || merge_root[size_t(Sr)] >= 0 || merge_target[size_t(Sr)] || merge_root[size_t(Dr)] >= 0) continue;
+    if (G.overlap(Sr, p.output) || G.overlap(Sr, p.input) || G.overlap(D, p.output) || G.overlap(D, p.input)) continue;
+    const mx_buf& bs = p.bufs[Sr];
+    const mx_buf& bd = p.bufs[D];
+    if (bs.c != bd.c || bs.h != bd.h || bs.w != bd.w || W[c].o.n != bs.c * bs.h * bs.w) continue;
+    bool ok = true;
+    size_t first = SIZE_MAX;
+    for (size_t s = 0; s < W.size() && ok; ++s) {
+      if (dead[s] || s == c) continue;
+      int32_t r[5], w[5];
+      const int nr = step_reads(W[s], r), nw = step_writes(W[s], w);
+      for (int a = 0; a < nr; ++a)
+        if (r[a] >= 0 && G.root[size_t(r[a])] == Sr) ok = false;  // Sr has another reader
+      for (int a = 0; a < nw; ++a)
+        if (w[a] >= 0 && G.root[size_t(w[a])] == Sr) {
+          if (s > c) ok = false;  // written after the Copy
+          first = std::min(first, s);
+        }
+    }
+    for (size_t s = first; ok && first != SIZE_MAX && s < c; ++s) {
+      if (dead[s]) continue;
+      int32_t r[5], w[5];
+      const int nr = step_reads(W[s], r), nw = step_writes(W[s], w);
+      for (int a = 0; a < nr; ++a) ok = ok && !G.overlap(r[a], D);
+      for (int a = 0; a < nw; ++a) ok = ok && !G.overlap(w[a], D);
+    }
+    if (!ok) continue;
+    merge_root[size_t(Sr)] = Dr;
+    merge_delta[size_t(Sr)] = p.offs[D] - p.offs[Dr];
+    merge_target[size_t(Dr)] = 1;
+    dead[c] = 1;
+    ++S.copies_merged;
+  }
+
   for (size_t i = 0; i < W.size(); ++i)
     if (!dead[i]) S.steps.push_back(std::move(W[i]));
 
@@ -632,9 +682,11 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
   const int m = int(S.steps.size());
   const int32_t nb = p.n_bufs + int32_t(S.extra.size());
   std::vector<int> first(size_t(nb), INT_MAX), last(size_t(nb), INT_MIN);
+  // A merged root lives and is placed with the root it is merged into.
+  auto placed = [&](int32_t r) { return r < p.n_bufs && merge_root[size_t(r)] >= 0 ? merge_root[size_t(r)] : r; };
   auto touch = [&](int32_t b, int t) {
     if (b < 0) return;
-    const size_t r = size_t(G.root[size_t(b)]);
+    const size_t r = size_t(placed(G.root[size_t(b)]));
     first[r] = std::min(first[r], t);
     last[r] = std::max(last[r], t);
   };
@@ -653,7 +705,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
   };
   std::vector<Slot> order;
   for (int32_t b = 0; b < nb; ++b)
-    if (G.root[size_t(b)] == b && first[size_t(b)] <= last[size_t(b)]) {
+    if (G.root[size_t(b)] == b && placed(b) == b && first[size_t(b)] <= last[size_t(b)]) {
       const mx_buf& bb = b < p.n_bufs ? p.bufs[b] : S.extra[size_t(b - p.n_bufs)];
       const int64_t len = bb.c * bb.h * bb.w;
       order.push_back({b, (len + 63) / 64 * 64, 0});
@@ -685,9 +737,11 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
   S.offs.resize(size_t(nb));
   for (int32_t b = 0; b < nb; ++b) {
     const int32_t r = G.root[size_t(b)];
-    S.offs[size_t(b)] = root_off[size_t(r)] + (b < p.n_bufs ? p.offs[b] - p.offs[r] : 0);
+    const int64_t at = placed(r) == r ? root_off[size_t(r)] : root_off[size_t(placed(r))] + merge_delta[size_t(r)];
+    S.offs[size_t(b)] = at + (b < p.n_bufs ? p.offs[b] - p.offs[r] : 0);
   }
   S.arena_len = std::max<int64_t>(S.arena_len, 64);
+  S.merged_into = std::move(merge_root);
   return S;
 }
 

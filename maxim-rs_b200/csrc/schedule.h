@@ -94,6 +94,9 @@ struct Schedule {
   std::vector<SchedStep> steps;
   std::vector<mx_buf> extra;  // buffers the schedule adds (ids n_bufs, n_bufs + 1, ...), each its own root
   std::vector<int64_t> offs;  // per buffer (plan's, then extra), in floats: the root's offset + the plan's view delta
+  // Per plan buffer: for a root placed inside another root (3b, merged
+  // placement), that root, whose pixel stride its views then have; -1 else.
+  std::vector<int32_t> merged_into;
   int64_t arena_len = 0;      // floats
   int perms_dropped = 0;
   int ops_fused = 0;          // plan ops carried out inside another op's step
@@ -102,6 +105,7 @@ struct Schedule {
   int ln_in_epilogue = 0;     // LayerNorms written whole by their producer's epilogue
   int copies_elided = 0;      // Copies whose readers read the source instead
   int steps_moved = 0;        // producers run at their consumer's position to take it as an epilogue
+  int copies_merged = 0;      // Copies of a whole root into a view of another, the two placed as one
 };
 
 struct ScheduleHooks {

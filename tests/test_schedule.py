@@ -169,3 +169,34 @@ def test_schedule_channel_scale_takes_two_residual_adds(mx):
     two = [p for p, members in steps.items()
            if ops[p].kind == 9 and sum(ops[m].kind == ADD for m in members) == 2]
     assert len(two) >= 24
+
+
+def test_schedule_places_a_copied_concatenation_inside_its_copy(mx):
+    """A Copy of a whole root (a concatenation) into a view of a wider root
+    goes: the root is placed where the Copy would have written it, so the
+    steps that write its slices write the wider root's (MAXIM-3S: the three
+    UpSampleRatio stacks per stage, nine Copies)."""
+    plan = mx.Plan(None, 256, 320, variant="S-3")
+    ops = plan.ops()
+    _, prim = mx.plan_schedule(plan)
+
+    def root(b):
+        while plan.alias(b) is not None:
+            b = plan.alias(b)[0]
+        return b
+    readers = {}
+    for o in ops:
+        for s in (o.src, o.src2):
+            if s >= 0:
+                readers[root(s)] = readers.get(root(s), 0) + 1
+    merged = 0
+    for i, o in enumerate(ops):
+        if o.kind != COPY or plan.alias(o.src) is not None or plan.alias(o.dst) is None or readers[o.src] != 1:
+            continue
+        parent = plan.alias(o.dst)[0]
+        if plan.buf(parent)[0] > plan.buf(o.dst)[0] and plan.buf(o.src) == plan.buf(o.dst):
+            # Forwarded into the source's producer, or placed away: never a
+            # step of its own.
+            assert prim[i] != i
+            merged += prim[i] < 0
+    assert merged == 9
