@@ -645,6 +645,15 @@ Step umma_conv_step(mx_gpu& g, int32_t oi, const mx_op& o, const Layout* L, int6
         u->p.lo_scale = reinterpret_cast<const float*>(G->pool.dev + E.lo_scale);
         u->p.lo_bias = reinterpret_cast<const float*>(G->pool.dev + E.lo_bias);
       }
+      if (E.src2 >= 0) {
+        // The second addend of a binary tail, in the output's boxes (the
+        // schedule gives no LayerNorm output to such a step).
+        if (E.lo_dst >= 0 || E.epi != EPI_ADD) throw Error("schedule: a second addend beside a LayerNorm output");
+        View e2 = view_of(*G, *L, E.src2);
+        uint64_t de[2] = {uint64_t(n), uint64_t(d.npix)}, se[1] = {uint64_t(e2.stride) * 4};
+        u->l = make_tensor_map(e2.ptr, 2, de, se, bd);
+        u->p.e2 = 1;
+      }
       u->p.tiles = int((x.npix + 127) / 128);
       u->p.tiles_x = 0;
       u->p.e_npix = int(d.npix);

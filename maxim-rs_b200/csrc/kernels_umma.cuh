@@ -130,6 +130,9 @@ struct UmmaConvParams {
   // the fifth tensor map (tmL) beside the plain output; lo_scale null if off.
   int lo_col;
   int lo_only;  // the chunk itself has no reader: only its LayerNorm is stored
+  // CONV1 with a binary tail: a second addend, v = (v + e) + e2, read through
+  // tmL (then not a LayerNorm output) into the epilogue warp's staging buffer.
+  int e2;
   const float* lo_scale;
   const float* lo_bias;
   const float* bias;  // per output column, or null
@@ -358,7 +361,7 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
     tma_prefetch(&tmB);
     tma_prefetch(&tmBlo);
     tma_prefetch(&tmD);
-    if ((MODE == MODE_CONV1 && p.lo_scale) || (GATE && E)) tma_prefetch(&tmL);
+    if ((MODE == MODE_CONV1 && (p.lo_scale || p.e2)) || (GATE && E)) tma_prefetch(&tmL);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -747,8 +750,10 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
     // others hold it in registers, loaded one chunk ahead.
     constexpr bool TMA_E = GATE && E;
     constexpr int NE = E && !GATE ? 32 : 1;  // operand values held per thread
+    // A 1x1 conv's second addend comes the same way as the gate.
+    const bool E2 = MODE == MODE_CONV1 && E && p.e2 != 0;
     uint8_t* sb = staging + ew * 4096;
-    uint32_t euse = 0;  // gate tiles this warp has taken from ebar
+    uint32_t euse = 0;  // operand tiles this warp has taken from ebar
 
     // The second operand's values for this thread in chunk j of tile t: its
     // output pixel's 32 channels.
@@ -782,6 +787,14 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
     // previous chunk's store has gone out, so the load overlaps the wait for
     // the next accumulator and the TMEM loads (lane 0 only).
     auto gate_load = [&](int tt, int jj) {
+      if (MODE == MODE_CONV1 && E2) {
+        bulk_wait_read<0>();
+        int b0, b1, m0;
+        decode(tt, b0, b1, m0);
+        mbar_arrive_expect_tx(&ebar[ew], 4096);
+        tma_load_2d(sb, &tmL, &ebar[ew], m0 + jj * 32, b0 + 32 * q);
+        return;
+      }
       if constexpr (TMA_E) {
         bulk_wait_read<0>();
         int b0, b1, m0;
@@ -884,6 +897,27 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
           }
         }
         epi_apply(p.epi, v, e, p.slope);
+        if (E2) {
+          // The second addend, where this thread stages its pixel's row.
+          if (h == 0) {
+            bool ok = mbar_wait(&ebar[ew], euse & 1, vabort);
+            ++euse;
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+              if (lane == 0) fail(kErrEpilogue);
+              return false;
+            }
+          }
+          const float4* r4 = reinterpret_cast<const float4*>(sb + lane * 128);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 f = r4[(h * 4 + i) ^ (lane & 7)];
+            v[4 * i] = v[4 * i] + f.x;
+            v[4 * i + 1] = v[4 * i + 1] + f.y;
+            v[4 * i + 2] = v[4 * i + 2] + f.z;
+            v[4 * i + 3] = v[4 * i + 3] + f.w;
+          }
+        }
         if (!GATE && MODE != MODE_CONVT && p.st_out[0]) {
           const int colh = n0 + j * 32 + h * 16;
 #pragma unroll
@@ -914,7 +948,7 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
             }
           }
         }
-        if (!TMA_E && h == 0) {
+        if (!TMA_E && !E2 && h == 0) {
           // This warp's previous store must have read the staging buffer;
           // waiting only now lets that read overlap the TMEM loads and the
           // arithmetic above. (The gating instances waited before their
@@ -1013,7 +1047,7 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
       }
       if (++j == N / 32) j = 0, t += tstep;
       if (E && !GATE && t < p.tiles) load_e(t, j, ecur);
-      if (TMA_E && lane == 0 && t < p.tiles) gate_load(t, j);
+      if ((TMA_E || E2) && lane == 0 && t < p.tiles) gate_load(t, j);
       return true;
     };
 
@@ -1021,7 +1055,7 @@ __global__ void __launch_bounds__(UmmaCfg<N, MODE>::THREADS, 1)
 #pragma unroll
     for (int i = 0; i < NE; ++i) e[i] = 0.0f;
     if (E && !GATE && t < p.tiles) load_e(t, 0, e);
-    if (TMA_E && lane == 0 && t < p.tiles) gate_load(t, 0);
+    if ((TMA_E || E2) && lane == 0 && t < p.tiles) gate_load(t, 0);
     while (t < p.tiles && step(e)) {
     }
     if (lane == 0) bulk_wait<0>();

@@ -335,8 +335,10 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
       } else if (H.small_conv && H.small_conv(A.o)) {
         if (A.epi != EPI_NONE || operand >= 0 || (epi != EPI_GELU && epi != EPI_LRELU && epi != EPI_SIGMOID)) break;
       } else {
-        // (A transposed conv's epilogue only forwards copies.)
-        if (!umma || A.epi != EPI_NONE || A.o.kind == MX_OP_CONVT2X2) break;
+        // (A transposed conv's epilogue only forwards copies.) A 1x1 conv's
+        // residual add takes a second add that follows it.
+        const bool add2 = A.o.kind == MX_OP_CONV1X1 && A.epi == EPI_ADD && A.epi_src2 < 0 && epi == EPI_ADD;
+        if (!umma || (A.epi != EPI_NONE && !add2) || A.o.kind == MX_OP_CONVT2X2) break;
         if (!H.tma_view(D, out_channels(A.o))) break;
         if (operand >= 0 && !H.tma_view(operand, out_channels(A.o))) break;
       }
@@ -407,7 +409,7 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
         break;
       }
       A.o.dst = D;
-      if (!identity && A.o.kind == MX_OP_CHAN_SCALE && A.epi == EPI_ADD) {
+      if (!identity && (A.o.kind == MX_OP_CHAN_SCALE || A.o.kind == MX_OP_CONV1X1) && A.epi == EPI_ADD) {
         A.epi_src2 = operand;
       } else if (!identity) {
         A.epi = epi;
@@ -586,7 +588,11 @@ Schedule build_schedule(const mx_plan& p, const ScheduleHooks& H, bool fuse) {
     }
     if (!ok || i == SIZE_MAX) continue;
     SchedStep& P = W[i];
-    if (P.o.kind != MX_OP_CONV1X1 || P.ln_out >= 0 || H.stats_slice(P.o) <= 0 || !H.tma_view(y, 32)) continue;
+    // (A step with a second addend reads it through the map a LayerNorm
+    // output would use.)
+    if (P.o.kind != MX_OP_CONV1X1 || P.ln_out >= 0 || P.epi_src2 >= 0 || H.stats_slice(P.o) <= 0 ||
+        !H.tma_view(y, 32))
+      continue;
     const int64_t c0 = G.lo[size_t(x)] - G.lo[size_t(P.o.dst)], c = G.hi[size_t(x)] - G.lo[size_t(x)];
     if (c != 32 || c0 % 32 != 0) continue;
     if (G.overlap(y, p.output) || G.overlap(y, P.o.dst)) continue;
