@@ -166,6 +166,26 @@ int mx_gpu_poll(mx_gpu* g);
  * batch of images already resident in HBM): device-to-device, async. */
 int mx_gpu_upload_input_device(mx_gpu* g, const float* dev_input);
 int mx_gpu_download_output_device(mx_gpu* g, float* dev_output);
+/* The reference CLI's whole image path (`run_gpu` between `read_png` and
+ * `write_png`: src/main.rs:467-504 with src/image.rs:40-104 and 171-246) with
+ * its per-pixel steps on the device. The caller passes the PNG's 8-bit
+ * samples (interleaved RGB, h x w x 3 bytes, e.g. from mx_png_read_rgb8_mem)
+ * and gets the restored image's 8-bit samples back (h x w x 3 bytes, the
+ * original size). On the device: divide by 255, reflect to the even shape,
+ * reflect-pad centred to a multiple of `factor` (the plan must be built for
+ * that padded shape, mx_pad_geometry), the pass, then the centred crop,
+ * clamp to 0..1 and round half up to 8 bits. Only the 8-bit images cross
+ * PCIe (a quarter of the float copies each way). Results are bit for bit
+ * those of mx_preprocess + mx_gpu_run + mx_crop_out + the PNG writer's
+ * rounding. The first call allocates the handle's 8-bit staging (two
+ * buffers of the padded size). Images the host pipeline refuses (too small
+ * to reflect) are refused with the same message.
+ * upload_rgb8 / download_rgb8 are the two halves (asynchronous on the
+ * handle's stream, around mx_gpu_enqueue; download crops with the geometry
+ * of the image last uploaded); run_rgb8 does all of it and waits. */
+int mx_gpu_upload_rgb8(mx_gpu* g, const uint8_t* rgb, int32_t h, int32_t w, int32_t factor);
+int mx_gpu_download_rgb8(mx_gpu* g, uint8_t* out_rgb);
+int mx_gpu_run_rgb8(mx_gpu* g, const uint8_t* rgb, int32_t h, int32_t w, int32_t factor, uint8_t* out_rgb);
 /* The handle's CUDA stream (a cudaStream_t, as an opaque pointer) so a caller
  * can order its own work or record timing events against the pass. */
 int mx_gpu_stream(mx_gpu* g, void** stream);
@@ -382,6 +402,29 @@ int mx_preprocess(const mx_image* img, int32_t factor, mx_image* padded, int32_t
 /* `image::crop_out` (src/image.rs:233-246). */
 int mx_crop_out(const mx_image* pred, int32_t orig_h, int32_t orig_w, int32_t even_h, int32_t even_w,
                 mx_image* out);
+
+/* The shapes `image::preprocess` (src/image.rs:171-207) gives an h x w image,
+ * without its pixels: the padded shape (what to build the plan for) and the
+ * even shape (what to crop with). Refuses exactly the images preprocess
+ * refuses, with the same message. */
+int mx_pad_geometry(int32_t h, int32_t w, int32_t factor, int32_t* padded_h, int32_t* padded_w, int32_t* even_h,
+                    int32_t* even_w);
+
+/* The 8-bit side of `read_png_stream` / `write_png_stream`
+ * (src/image.rs:40-104): the PNG's samples as decoded, interleaved RGB
+ * (c = 3, h x w x 3 bytes; gray and gray+alpha expanded, alpha dropped), as
+ * the device-side pipeline (mx_gpu_run_rgb8) takes them. Memory is owned by
+ * the library; free with mx_image8_free. mx_png_size_mem reads the width and
+ * height from the IHDR chunk alone, so a caller can size and build its plan
+ * while the pixels are still being decoded. */
+typedef struct mx_image8 {
+  int32_t c, h, w;
+  uint8_t* data;
+} mx_image8;
+void mx_image8_free(mx_image8* img);
+int mx_png_size_mem(const uint8_t* bytes, size_t n, int32_t* h, int32_t* w);
+int mx_png_read_rgb8_mem(const uint8_t* bytes, size_t n, mx_image8* out);
+int mx_png_write_rgb8(const char* path, const mx_image8* img);
 
 #ifdef __cplusplus
 }

@@ -5,7 +5,9 @@ GPU executor and the C++ host contract; this package is its Python binding plus
 the synthetic-checkpoint and synthetic-input generators (`synth`).
 """
 from ._native import (Batch, Gpu, MaximError, Plan, Weights, crop_out, device_count, driver_ready, exported_symbols, lib,
-                      param_spec, plan_schedule, png_read, png_read_bytes, png_write, preprocess)
+                      pad_geometry, param_spec, plan_schedule, png_read, png_read_bytes, png_read_rgb8_bytes,
+                      png_size, png_write, png_write_rgb8, preprocess)
 
 __all__ = ["Batch", "Gpu", "MaximError", "Plan", "Weights", "crop_out", "device_count", "driver_ready", "exported_symbols",
-           "lib", "param_spec", "plan_schedule", "png_read", "png_read_bytes", "png_write", "preprocess"]
+           "lib", "pad_geometry", "param_spec", "plan_schedule", "png_read", "png_read_bytes", "png_read_rgb8_bytes",
+           "png_size", "png_write", "png_write_rgb8", "preprocess"]

@@ -77,6 +77,11 @@ class mx_image(ctypes.Structure):
                 ("data", ctypes.POINTER(ctypes.c_float))]
 
 
+class mx_image8(ctypes.Structure):
+    _fields_ = [("c", ctypes.c_int32), ("h", ctypes.c_int32), ("w", ctypes.c_int32),
+                ("data", ctypes.POINTER(ctypes.c_uint8))]
+
+
 class MaximError(RuntimeError):
     def __init__(self, code, msg):
         super().__init__(msg)
@@ -98,6 +103,11 @@ _SIGS = {
     "mx_gpu_sync": (ctypes.c_int, [ctypes.c_void_p]),
     "mx_gpu_poll": (ctypes.c_int, [ctypes.c_void_p]),
     "mx_gpu_stream": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "mx_gpu_upload_rgb8": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int32]),
+    "mx_gpu_download_rgb8": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "mx_gpu_run_rgb8": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                       ctypes.c_int32, ctypes.c_void_p]),
     "mx_gpu_upload_input_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "mx_gpu_download_output_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "mx_gpu_begin": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
@@ -147,6 +157,13 @@ _SIGS = {
                                      ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]),
     "mx_crop_out": (ctypes.c_int, [ctypes.POINTER(mx_image), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                    ctypes.c_int32, ctypes.POINTER(mx_image)]),
+    "mx_pad_geometry": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32] +
+                        [ctypes.POINTER(ctypes.c_int32)] * 4),
+    "mx_image8_free": (None, [ctypes.POINTER(mx_image8)]),
+    "mx_png_size_mem": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int32),
+                                       ctypes.POINTER(ctypes.c_int32)]),
+    "mx_png_read_rgb8_mem": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(mx_image8)]),
+    "mx_png_write_rgb8": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(mx_image8)]),
 }
 
 
@@ -322,6 +339,25 @@ class Gpu:
             out = np.empty(self.out_shape, np.float32)
         check(lib().mx_gpu_run(self._h, _ptr(x), _ptr(out)), "run")
         return out
+
+    def run_rgb8(self, rgb, factor=64, out=None):
+        """The image path with its per-pixel steps on the device: h x w x 3 uint8
+        in, the restored h x w x 3 uint8 out (`mx_gpu_run_rgb8`)."""
+        x = np.ascontiguousarray(rgb, dtype=np.uint8)
+        if x.ndim != 3 or x.shape[2] != 3:
+            raise ValueError("expected h x w x 3 uint8 samples, got shape %s" % (x.shape,))
+        if out is None:
+            out = np.empty(x.shape, np.uint8)
+        check(lib().mx_gpu_run_rgb8(self._h, _ptr(x), x.shape[0], x.shape[1], factor, _ptr(out)), "run_rgb8")
+        return out
+
+    def upload_rgb8(self, rgb, factor=64):
+        x = np.ascontiguousarray(rgb, dtype=np.uint8)
+        check(lib().mx_gpu_upload_rgb8(self._h, _ptr(x), x.shape[0], x.shape[1], factor), "upload_rgb8")
+        self._rgb_keep = x  # the copy from pageable memory may still be reading it
+
+    def download_rgb8(self, out):
+        check(lib().mx_gpu_download_rgb8(self._h, _ptr(out)), "download_rgb8")
 
     def upload_input(self, image):
         x = np.ascontiguousarray(image, dtype=np.float32).reshape(-1)
@@ -570,3 +606,32 @@ def crop_out(a, orig_h, orig_w, even_h, even_w):
     out = mx_image()
     check(lib().mx_crop_out(ctypes.byref(img), orig_h, orig_w, even_h, even_w, ctypes.byref(out)), "crop")
     return _image_to_np(out)
+
+
+def pad_geometry(h, w, factor=64):
+    """`mx_pad_geometry` -> ((padded_h, padded_w), (even_h, even_w))."""
+    v = [ctypes.c_int32() for _ in range(4)]
+    check(lib().mx_pad_geometry(h, w, factor, *[ctypes.byref(x) for x in v]), "pad_geometry")
+    return (v[0].value, v[1].value), (v[2].value, v[3].value)
+
+
+def png_size(data):
+    """Height and width from a PNG's IHDR chunk."""
+    h, w = ctypes.c_int32(), ctypes.c_int32()
+    check(lib().mx_png_size_mem(data, len(data), ctypes.byref(h), ctypes.byref(w)), "png")
+    return h.value, w.value
+
+
+def png_read_rgb8_bytes(data):
+    """A PNG's 8-bit samples as h x w x 3 uint8 (gray expanded to RGB)."""
+    img = mx_image8()
+    check(lib().mx_png_read_rgb8_mem(data, len(data), ctypes.byref(img)), "png")
+    a = np.ctypeslib.as_array(img.data, shape=(img.h, img.w, img.c)).copy()
+    lib().mx_image8_free(ctypes.byref(img))
+    return a
+
+
+def png_write_rgb8(path, a):
+    a = np.ascontiguousarray(a, dtype=np.uint8)
+    img = mx_image8(3, a.shape[0], a.shape[1], a.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)))
+    check(lib().mx_png_write_rgb8(os.fsencode(path), ctypes.byref(img)), str(path))

@@ -1,5 +1,9 @@
 // extern "C" entry points of the host contract (weights, plan, image).
+#include <cerrno>
+#include <climits>
 #include <cstdarg>
+#include <cstdint>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <memory>
@@ -192,6 +196,60 @@ int mx_preprocess(const mx_image* img, int32_t factor, mx_image* padded, int32_t
     if (even_h) *even_h = int32_t(p.even_h);
     if (even_w) *even_w = int32_t(p.even_w);
     *padded = to_c(std::move(p.img));
+  });
+}
+
+int mx_pad_geometry(int32_t h, int32_t w, int32_t factor, int32_t* padded_h, int32_t* padded_w, int32_t* even_h,
+                    int32_t* even_w) {
+  return guard([&] {
+    if (h <= 0 || w <= 0 || factor <= 0) throw Error("mx_pad_geometry: bad argument");
+    const PadGeometry g = pad_geometry(h, w, factor);
+    if (padded_h) *padded_h = int32_t(g.h);
+    if (padded_w) *padded_w = int32_t(g.w);
+    if (even_h) *even_h = int32_t(g.even_h);
+    if (even_w) *even_w = int32_t(g.even_w);
+  });
+}
+
+void mx_image8_free(mx_image8* img) {
+  if (img) {
+    free(img->data);
+    img->data = nullptr;
+  }
+}
+
+int mx_png_size_mem(const uint8_t* bytes, size_t n, int32_t* h, int32_t* w) {
+  return guard([&] {
+    if (!bytes || !h || !w) throw Error("mx_png_size_mem: null argument");
+    const auto hw = png_size(bytes, n, "<memory>");
+    if (hw.first > INT32_MAX || hw.second > INT32_MAX) throw Error("PNG dimensions out of range", MX_E_IO);
+    *h = int32_t(hw.first), *w = int32_t(hw.second);
+  });
+}
+
+int mx_png_read_rgb8_mem(const uint8_t* bytes, size_t n, mx_image8* out) {
+  return guard([&] {
+    if (!bytes || !out) throw Error("mx_png_read_rgb8_mem: null argument");
+    Rgb8 px = decode_png_rgb8(bytes, n, "<memory>");
+    mx_image8 o{};
+    o.c = 3, o.h = int32_t(px.h), o.w = int32_t(px.w);
+    o.data = static_cast<uint8_t*>(malloc(px.data.size() + 1));
+    if (!o.data) throw Error("host allocation failed", MX_E_OOM);
+    memcpy(o.data, px.data.data(), px.data.size());
+    *out = o;
+  });
+}
+
+int mx_png_write_rgb8(const char* path, const mx_image8* img) {
+  return guard([&] {
+    if (!path || !img || !img->data || img->c != 3 || img->h <= 0 || img->w <= 0)
+      throw Error("mx_png_write_rgb8: needs a 3-channel image and a path");
+    const std::vector<uint8_t> bytes = encode_png_rgb8(img->data, img->h, img->w);
+    FILE* f = fopen(path, "wb");
+    if (!f) throw Error(std::string(path) + ": " + strerror(errno), MX_E_IO);
+    size_t wr = fwrite(bytes.data(), 1, bytes.size(), f);
+    int rc = fclose(f);
+    if (wr != bytes.size() || rc != 0) throw Error(std::string(path) + ": write failed", MX_E_IO);
   });
 }
 

@@ -10,6 +10,8 @@
 // backend here: a missing driver is an error, never a silent fallback.
 #include <dirent.h>
 
+#include <cerrno>
+
 #include <algorithm>
 #include <chrono>
 #include <cstdio>
@@ -18,6 +20,7 @@
 #include <unistd.h>
 #include <map>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "maxim_b200.h"
@@ -248,23 +251,47 @@ int main(int argc, char** argv) {
     return rc;
   }
 
-  mx_image img{};
+  // The PNG's size comes from its header, so the plan can be built and the
+  // executor brought up (weights converted and uploaded) while a second
+  // thread decodes the pixels. The per-pixel steps either side of the pass
+  // (divide by 255, reflect pad, crop, 8-bit rounding) run on the device, and
+  // only 8-bit images cross PCIe.
+  std::vector<uint8_t> bytes;
+  const std::string src_name = input == "-" ? "stdin" : input;
   if (input == "-") {
-    auto bytes = read_all(stdin);
-    if (mx_png_read_mem(bytes.data(), bytes.size(), &img) != MX_OK) return fail("stdin");
-  } else if (mx_png_read(input.c_str(), &img) != MX_OK) {
-    return fail("");
+    bytes = read_all(stdin);
+  } else {
+    FILE* f = fopen(input.c_str(), "rb");
+    if (!f) {
+      fprintf(stderr, "maxim: %s: %s\n", input.c_str(), strerror(errno));
+      return 1;
+    }
+    bytes = read_all(f);
+    fclose(f);
   }
-  mx_image padded{};
-  int32_t even_h = 0, even_w = 0;
-  if (mx_preprocess(&img, factor, &padded, &even_h, &even_w) != MX_OK) return fail("");
+  int32_t img_h = 0, img_w = 0, pad_h = 0, pad_w = 0, even_h = 0, even_w = 0;
+  if (mx_png_size_mem(bytes.data(), bytes.size(), &img_h, &img_w) != MX_OK) return fail(src_name);
+  if (mx_pad_geometry(img_h, img_w, factor, &pad_h, &pad_w, &even_h, &even_w) != MX_OK) return fail("");
   if (!quiet)
-    fprintf(stderr, "maxim %s: %dx%d -> padded %dx%d (even %dx%d), variant %s\n", kVersion, img.w, img.h, padded.w,
-            padded.h, even_w, even_h, variant);
+    fprintf(stderr, "maxim %s: %dx%d -> padded %dx%d (even %dx%d), variant %s\n", kVersion, img_w, img_h, pad_w,
+            pad_h, even_w, even_h, variant);
+  mx_image8 img{};
+  int dec_rc = MX_OK;
+  std::string dec_err;
+  std::thread decoder([&] {
+    dec_rc = mx_png_read_rgb8_mem(bytes.data(), bytes.size(), &img);
+    if (dec_rc != MX_OK) dec_err = last_error();  // the message slot is per thread
+  });
+  struct Joiner {
+    std::thread& t;
+    ~Joiner() {
+      if (t.joinable()) t.join();
+    }
+  } joiner{decoder};
 
   auto t0 = std::chrono::steady_clock::now();
   mx_plan_handle* plan = nullptr;
-  if (mx_plan_build(w, padded.h, padded.w, 0, &plan) != MX_OK) return fail("");
+  if (mx_plan_build(w, pad_h, pad_w, 0, &plan) != MX_OK) return fail("");
   const mx_plan* pv = mx_plan_view(plan);
   if (!quiet)
     fprintf(stderr, "maxim: plan %d ops, %d buffers, arena %.1f MiB\n", pv->n_ops, pv->n_bufs,
@@ -279,10 +306,14 @@ int main(int argc, char** argv) {
     fprintf(stderr, "maxim: device %s, %lld kernel launches per pass, weights %.1f MiB\n", st.device_name,
             (long long)st.kernels, st.weight_bytes / 1048576.0);
   if (profile) mx_gpu_set_timeline(gpu, 1);
-  const size_t n_out = size_t(pv->bufs[pv->output].c * pv->bufs[pv->output].h * pv->bufs[pv->output].w);
-  std::vector<float> out(n_out);
+  decoder.join();
+  if (dec_rc != MX_OK) {
+    fprintf(stderr, "maxim: %s: %s\n", src_name.c_str(), dec_err.c_str());
+    return 1;
+  }
+  std::vector<uint8_t> out(size_t(img_h) * size_t(img_w) * 3);
   auto t1 = std::chrono::steady_clock::now();
-  if (mx_gpu_run(gpu, padded.data, out.data()) != MX_OK) return fail("");
+  if (mx_gpu_run_rgb8(gpu, img.data, img_h, img_w, factor, out.data()) != MX_OK) return fail("");
   auto t2 = std::chrono::steady_clock::now();
   if (!quiet)
     fprintf(stderr, "maxim: setup %.2fs, pass %.1f ms\n", std::chrono::duration<double>(t1 - t0).count(),
@@ -304,9 +335,7 @@ int main(int argc, char** argv) {
                100.0 * kv.second.first / (total > 0 ? total : 1));
     }
   }
-  mx_image pred{3, int32_t(padded.h), int32_t(padded.w), out.data()};
-  mx_image cropped{};
-  if (mx_crop_out(&pred, img.h, img.w, even_h, even_w, &cropped) != MX_OK) return fail("");
+  mx_image8 restored{3, img_h, img_w, out.data()};
   if (output == "-") {
     // The library writes files; stream through a temporary for stdout.
     char tmpl[] = "/tmp/maxim_out_XXXXXX";
@@ -316,19 +345,17 @@ int main(int argc, char** argv) {
       return 1;
     }
     close(fd);
-    if (mx_png_write(tmpl, &cropped) != MX_OK) return fail("stdout");
+    if (mx_png_write_rgb8(tmpl, &restored) != MX_OK) return fail("stdout");
     FILE* f = fopen(tmpl, "rb");
-    auto bytes = read_all(f);
+    auto obytes = read_all(f);
     fclose(f);
     unlink(tmpl);
-    fwrite(bytes.data(), 1, bytes.size(), stdout);
+    fwrite(obytes.data(), 1, obytes.size(), stdout);
   } else {
-    if (mx_png_write(output.c_str(), &cropped) != MX_OK) return fail("");
+    if (mx_png_write_rgb8(output.c_str(), &restored) != MX_OK) return fail("");
     if (!quiet) fprintf(stderr, "maxim: wrote %s\n", output.c_str());
   }
-  mx_image_free(&cropped);
-  mx_image_free(&padded);
-  mx_image_free(&img);
+  mx_image8_free(&img);
   mx_gpu_free(gpu);
   mx_plan_free(plan);
   mx_weights_free(w);

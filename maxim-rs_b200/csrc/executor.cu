@@ -42,6 +42,8 @@
 #include "kernels_mem.cuh"
 #include "kernels_umma.cuh"
 #include "kernels_conv3f.cuh"
+#include "kernels_image.cuh"
+#include "image.h"
 #include "maxim_b200.h"
 #include "schedule.h"
 
@@ -236,6 +238,12 @@ struct mx_gpu {
   bool use_umma = true;
   float* scratch = nullptr;  // per-op scratch (the channel-mean partial sums)
   int64_t scratch_len = 0;   // floats
+  // The device-side image pipeline (mx_gpu_upload_rgb8 / download_rgb8):
+  // 8-bit staging, allocated at its first use, and the geometry of the image
+  // last uploaded through it.
+  uint8_t* rgb_in = nullptr;
+  uint8_t* rgb_out = nullptr;
+  int32_t rgb_h = 0, rgb_w = 0, rgb_even_h = 0, rgb_even_w = 0;
 };
 
 namespace mx {
@@ -1759,6 +1767,8 @@ void mx_gpu_free(mx_gpu* g) {
   cudaFree(g->status);
   cudaFree(g->scratch);
   cudaFree(g->readback);
+  cudaFree(g->rgb_in);
+  cudaFree(g->rgb_out);
   if (g->stream) cudaStreamDestroy(g->stream);
   delete g;
 }
@@ -1868,6 +1878,59 @@ int mx_gpu_run(mx_gpu* g, const float* input, float* output) {
   int rc = mx_gpu_upload_input(g, input);
   if (rc == MX_OK) rc = mx_gpu_enqueue(g);
   if (rc == MX_OK) rc = mx_gpu_download_output(g, output);
+  if (rc == MX_OK) rc = mx_gpu_sync(g);
+  return rc;
+}
+
+int mx_gpu_upload_rgb8(mx_gpu* g, const uint8_t* rgb, int32_t h, int32_t w, int32_t factor) {
+  return guard([&] {
+    if (!g || !rgb) throw Error("mx_gpu_upload_rgb8: null argument");
+    if (h < 2 || w < 2 || factor <= 0)
+      throw Error(fmt("mx_gpu_upload_rgb8: a %dx%d image (factor %d); reflection needs at least 2 pixels a side", w,
+                      h, factor));
+    const PadGeometry pg = pad_geometry(h, w, factor);
+    const mx_buf& in = g->bufs[size_t(g->input)];
+    if (in.c != 3 || pg.h != in.h || pg.w != in.w)
+      throw Error(fmt("mx_gpu_upload_rgb8: a %dx%d image pads to %lldx%lld, but this executor's plan takes a "
+                      "%lldx%lld input",
+                      w, h, (long long)pg.w, (long long)pg.h, (long long)in.w, (long long)in.h));
+    DevicePin pin(g->device);
+    // The original image is never larger than the padded one.
+    const size_t cap = size_t(in.h * in.w * 3);
+    if (!g->rgb_in) MX_CUDA(cudaMalloc(&g->rgb_in, cap));
+    if (!g->rgb_out) MX_CUDA(cudaMalloc(&g->rgb_out, cap));
+    MX_CUDA(cudaMemcpyAsync(g->rgb_in, rgb, size_t(h) * size_t(w) * 3, cudaMemcpyHostToDevice, g->stream));
+    const int64_t n = in.h * in.w;
+    const unsigned grid = std::min<unsigned>(blocks_for(n, 256), unsigned(g->sms) * 8);
+    rgb8_to_padded_kernel<<<grid, 256, 0, g->stream>>>(g->rgb_in, h, w, int(pg.even_h), int(pg.even_w),
+                                                        int(pg.top), int(pg.left), int(in.h), int(in.w), g->io_in);
+    check_launch();
+    g->rgb_h = h, g->rgb_w = w, g->rgb_even_h = int32_t(pg.even_h), g->rgb_even_w = int32_t(pg.even_w);
+  });
+}
+
+int mx_gpu_download_rgb8(mx_gpu* g, uint8_t* out_rgb) {
+  return guard([&] {
+    if (!g || !out_rgb) throw Error("mx_gpu_download_rgb8: null argument");
+    if (!g->rgb_in) throw Error("mx_gpu_download_rgb8: no image was uploaded with mx_gpu_upload_rgb8");
+    const mx_buf& ob = g->bufs[size_t(g->output)];
+    const int64_t hs = ob.h / 2 - g->rgb_even_h / 2, ws = ob.w / 2 - g->rgb_even_w / 2;
+    if (ob.c != 3 || hs < 0 || ws < 0 || hs + g->rgb_h > ob.h || ws + g->rgb_w > ob.w)
+      throw Error("mx_gpu_download_rgb8: the crop does not fit inside the prediction");
+    DevicePin pin(g->device);
+    const int64_t n = int64_t(g->rgb_h) * g->rgb_w;
+    const unsigned grid = std::min<unsigned>(blocks_for(n, 256), unsigned(g->sms) * 8);
+    crop_to_rgb8_kernel<<<grid, 256, 0, g->stream>>>(g->io_out, int(ob.h), int(ob.w), int(hs), int(ws), g->rgb_h,
+                                                      g->rgb_w, g->rgb_out);
+    check_launch();
+    MX_CUDA(cudaMemcpyAsync(out_rgb, g->rgb_out, size_t(n) * 3, cudaMemcpyDeviceToHost, g->stream));
+  });
+}
+
+int mx_gpu_run_rgb8(mx_gpu* g, const uint8_t* rgb, int32_t h, int32_t w, int32_t factor, uint8_t* out_rgb) {
+  int rc = mx_gpu_upload_rgb8(g, rgb, h, w, factor);
+  if (rc == MX_OK) rc = mx_gpu_enqueue(g);
+  if (rc == MX_OK) rc = mx_gpu_download_rgb8(g, out_rgb);
   if (rc == MX_OK) rc = mx_gpu_sync(g);
   return rc;
 }

@@ -61,6 +61,18 @@ int64_t min_dimension(int64_t factor) {
   return factor;
 }
 
+// The refusal of an image too small to reflect out to a multiple of
+// `factor` (src/image.rs:185-199).
+[[noreturn]] void refuse_small(int64_t factor, const char* axis, int64_t dim, int64_t pad) {
+  throw Error(fmt("this image is too small for MAXIM's %lld-multiple padding: the %s is %lld pixels and the "
+                  "pipeline reflects it out to the next multiple of %lld, which is %lld pixels of padding a side - "
+                  "a reflection needs less padding than the dimension it mirrors. The reference pipeline refuses "
+                  "this input for the same reason (torch's reflect pad: `Padding size should be less than the "
+                  "corresponding input dimension`). Give it an image at least %lld pixels on its %s.",
+                  (long long)factor, axis, (long long)dim, (long long)factor, (long long)pad,
+                  (long long)min_dimension(factor), axis));
+}
+
 }  // namespace
 
 std::pair<int64_t, int64_t> same_pad(int64_t size, int64_t stride, int64_t k) {
@@ -69,7 +81,17 @@ std::pair<int64_t, int64_t> same_pad(int64_t size, int64_t stride, int64_t k) {
   return {total / 2, total - total / 2};
 }
 
-Image read_png_bytes(const uint8_t* b, size_t n, const std::string& what) {
+std::pair<int64_t, int64_t> png_size(const uint8_t* b, size_t n, const std::string& what) {
+  static const uint8_t sig[8] = {137, 80, 78, 71, 13, 10, 26, 10};
+  if (n < 8 || memcmp(b, sig, 8) != 0) throw Error(what + ": not a PNG file", MX_E_IO);
+  // The IHDR chunk comes first: 8-byte signature, 4-byte length, "IHDR".
+  if (n < 8 + 8 + 13 || memcmp(b + 12, "IHDR", 4) != 0) throw Error(what + ": PNG has no IHDR", MX_E_IO);
+  const int64_t W = be32(b + 16), H = be32(b + 20);
+  if (W == 0 || H == 0) throw Error(what + ": empty PNG", MX_E_IO);
+  return {H, W};
+}
+
+Rgb8 decode_png_rgb8(const uint8_t* b, size_t n, const std::string& what) {
   static const uint8_t sig[8] = {137, 80, 78, 71, 13, 10, 26, 10};
   if (n < 8 || memcmp(b, sig, 8) != 0) throw Error(what + ": not a PNG file", MX_E_IO);
   size_t p = 8;
@@ -146,16 +168,32 @@ Image read_png_bytes(const uint8_t* b, size_t n, const std::string& what) {
       cur[i] = uint8_t(v);
     }
   }
-  Image img(3, H, W);
-  size_t plane = size_t(H) * W;
+  Rgb8 out;
+  out.h = H, out.w = W;
+  const size_t plane = size_t(H) * W;
+  if (ch == 3) {
+    out.data = std::move(pix);
+    return out;
+  }
+  out.data.resize(plane * 3);
   for (size_t i = 0; i < plane; ++i) {
     const uint8_t* s = &pix[i * ch];
-    uint8_t r, g, bl;
-    if (ch <= 2) r = g = bl = s[0];
-    else r = s[0], g = s[1], bl = s[2];
-    img.data[i] = r / 255.0f;
-    img.data[plane + i] = g / 255.0f;
-    img.data[2 * plane + i] = bl / 255.0f;
+    uint8_t* d = &out.data[i * 3];
+    if (ch <= 2) d[0] = d[1] = d[2] = s[0];
+    else d[0] = s[0], d[1] = s[1], d[2] = s[2];
+  }
+  return out;
+}
+
+Image read_png_bytes(const uint8_t* b, size_t n, const std::string& what) {
+  const Rgb8 px = decode_png_rgb8(b, n, what);
+  Image img(3, px.h, px.w);
+  const size_t plane = size_t(px.h) * px.w;
+  for (size_t i = 0; i < plane; ++i) {
+    const uint8_t* s = &px.data[i * 3];
+    img.data[i] = s[0] / 255.0f;
+    img.data[plane + i] = s[1] / 255.0f;
+    img.data[2 * plane + i] = s[2] / 255.0f;
   }
   return img;
 }
@@ -170,16 +208,24 @@ Image read_png(const std::string& path) {
 std::vector<uint8_t> encode_png(const Image& img) {
   if (img.c != 3) throw Error("write_png: the image must have 3 channels");
   const int64_t H = img.h, W = img.w;
-  std::vector<uint8_t> raw(size_t(H * (W * 3 + 1)));
+  std::vector<uint8_t> rgb(size_t(H * W * 3));
   size_t plane = size_t(H * W);
-  for (int64_t y = 0; y < H; ++y) {
-    uint8_t* row = &raw[size_t(y * (W * 3 + 1))];
-    row[0] = 0;
+  for (int64_t y = 0; y < H; ++y)
     for (int64_t x = 0; x < W; ++x)
       for (int c = 0; c < 3; ++c) {
         float v = std::min(std::max(img.data[c * plane + size_t(y * W + x)], 0.0f), 1.0f);
-        row[1 + x * 3 + c] = uint8_t(v * 255.0f + 0.5f);
+        rgb[size_t((y * W + x) * 3 + c)] = uint8_t(v * 255.0f + 0.5f);
       }
+  return encode_png_rgb8(rgb.data(), H, W);
+}
+
+std::vector<uint8_t> encode_png_rgb8(const uint8_t* rgb, int64_t H, int64_t W) {
+  if (H <= 0 || W <= 0) throw Error("write_png: empty image");
+  std::vector<uint8_t> raw(size_t(H * (W * 3 + 1)));
+  for (int64_t y = 0; y < H; ++y) {
+    uint8_t* row = &raw[size_t(y * (W * 3 + 1))];
+    row[0] = 0;
+    memcpy(row + 1, rgb + size_t(y * W * 3), size_t(W * 3));
   }
   uLongf zlen = compressBound(uLong(raw.size()));
   std::vector<uint8_t> z(zlen);
@@ -213,6 +259,24 @@ void write_png(const std::string& path, const Image& img) {
   if (wr != bytes.size() || rc != 0) throw Error(path + ": write failed", MX_E_IO);
 }
 
+PadGeometry pad_geometry(int64_t h, int64_t w, int64_t factor) {
+  if (h <= 0 || w <= 0 || factor <= 0) throw Error("pad_geometry: bad argument");
+  const int64_t eh = h + h % 2, ew = w + w % 2;
+  const int64_t hp = eh % factor ? ((eh + factor) / factor) * factor : eh;
+  const int64_t wp = ew % factor ? ((ew + factor) / factor) * factor : ew;
+  const int64_t padh = hp - eh, padw = wp - ew;
+  struct Ax {
+    const char* name;
+    int64_t dim, pad;
+  } axes[2] = {{"height", eh, padh / 2}, {"width", ew, padw / 2}};
+  for (auto& a : axes)
+    if (a.pad != 0 && a.pad >= a.dim) refuse_small(factor, a.name, a.dim, a.pad);
+  PadGeometry g;
+  g.even_h = eh, g.even_w = ew, g.top = padh / 2, g.left = padw / 2;
+  g.h = eh + 2 * (padh / 2), g.w = ew + 2 * (padw / 2);
+  return g;
+}
+
 Padded preprocess(const Image& img, int64_t factor) {
   int64_t h = img.h, w = img.w;
   int64_t ph = h % 2, pw = w % 2;
@@ -226,14 +290,7 @@ Padded preprocess(const Image& img, int64_t factor) {
     int64_t dim, pad;
   } axes[2] = {{"height", eh, padh / 2}, {"width", ew, padw / 2}};
   for (auto& a : axes)
-    if (a.pad != 0 && a.pad >= a.dim)
-      throw Error(fmt("this image is too small for MAXIM's %lld-multiple padding: the %s is %lld pixels and the "
-                      "pipeline reflects it out to the next multiple of %lld, which is %lld pixels of padding a side - "
-                      "a reflection needs less padding than the dimension it mirrors. The reference pipeline refuses "
-                      "this input for the same reason (torch's reflect pad: `Padding size should be less than the "
-                      "corresponding input dimension`). Give it an image at least %lld pixels on its %s.",
-                      (long long)factor, a.name, (long long)a.dim, (long long)factor, (long long)a.pad,
-                      (long long)min_dimension(factor), a.name));
+    if (a.pad != 0 && a.pad >= a.dim) refuse_small(factor, a.name, a.dim, a.pad);
   Padded p;
   p.img = (padh || padw) ? reflect_pad2(even, padh / 2, padh / 2, padw / 2, padw / 2) : even;
   p.orig_h = h, p.orig_w = w, p.even_h = eh, p.even_w = ew;

@@ -98,3 +98,58 @@ def test_png_rejects_indexed(mx):
     img.save(buf, "PNG")
     with pytest.raises(mx.MaximError, match="indexed PNG"):
         mx.png_read_bytes(buf.getvalue())
+
+
+# ---- the 8-bit side: what the device-side pipeline (mx_gpu_run_rgb8) takes and gives
+
+@pytest.mark.parametrize("h,w", [(22, 22), (33, 97), (64, 64), (65, 130), (853, 1280), (400, 600), (1362, 2048),
+                                 (41, 300)])
+@pytest.mark.parametrize("factor", [64, 32, 8])
+def test_pad_geometry_is_preprocess_without_pixels(mx, h, w, factor):
+    p, even = mx.preprocess(np.zeros((3, h, w), np.float32), factor)
+    (ph, pw), even2 = mx.pad_geometry(h, w, factor)
+    assert (ph, pw) == p.shape[1:] and even2 == tuple(even)
+
+
+@pytest.mark.parametrize("h,w", [(16, 16), (64, 16), (20, 200)])
+def test_pad_geometry_refuses_what_preprocess_refuses(mx, h, w):
+    with pytest.raises(mx.MaximError) as a:
+        mx.preprocess(np.zeros((3, h, w), np.float32), 64)
+    with pytest.raises(mx.MaximError) as b:
+        mx.pad_geometry(h, w, 64)
+    assert str(a.value).split(": ", 1)[-1] == str(b.value).split(": ", 1)[-1]
+
+
+@pytest.mark.parametrize("mode", ["RGB", "RGBA", "L", "LA"])
+def test_png_rgb8_decode_matches_pil_and_the_float_reader(mx, mode):
+    from PIL import Image
+    rng = np.random.default_rng(5)
+    chans = {"RGB": 3, "RGBA": 4, "L": 1, "LA": 2}[mode]
+    arr = rng.integers(0, 256, (19, 27, chans), dtype=np.uint8)
+    img = Image.fromarray(arr[..., 0] if chans == 1 else arr, mode)
+    buf = io.BytesIO()
+    img.save(buf, "PNG")
+    data = buf.getvalue()
+    got = mx.png_read_rgb8_bytes(data)
+    assert got.dtype == np.uint8 and np.array_equal(got, np.asarray(img.convert("RGB")))
+    assert mx.png_size(data) == (19, 27)
+    # the float reader is exactly these samples divided by 255
+    f = mx.png_read_bytes(data)
+    assert np.array_equal(f, got.transpose(2, 0, 1).astype(np.float32) / np.float32(255.0))
+
+
+def test_png_rgb8_write_round_trip(mx, tmp_path):
+    from PIL import Image
+    a = np.random.default_rng(6).integers(0, 256, (23, 31, 3), dtype=np.uint8)
+    path = str(tmp_path / "x8.png")
+    mx.png_write_rgb8(path, a)
+    assert np.array_equal(np.asarray(Image.open(path).convert("RGB")), a)
+    # the float writer quantises to the same file contents
+    path2 = str(tmp_path / "xf.png")
+    mx.png_write(path2, a.transpose(2, 0, 1).astype(np.float32) / np.float32(255.0))
+    assert open(path, "rb").read() == open(path2, "rb").read()
+
+
+def test_png_size_refuses_non_png(mx):
+    with pytest.raises(mx.MaximError, match="not a PNG"):
+        mx.png_size(b"GIF89a....................")
