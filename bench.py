@@ -489,6 +489,52 @@ def config3_gmlp(mx, local, reps=5, warmup=3):
                          "min_bytes": min_bytes, "hbm_frac_of_min_traffic": min_bytes / (ms / 1e3) / 1e9 / hbm}}
 
 
+def startup_times(mx, local):
+    """Seconds to bring an executor up for the headline workload: opening the
+    checkpoint and building the plan (host), then mx_gpu_new deriving every
+    tensor-core layout, mx_gpu_new_cached writing a fresh converted-weights
+    cache, and mx_gpu_new_cached reading it back."""
+    import tempfile
+    t0 = time.perf_counter()
+    w = mx.Weights(checkpoint_path())
+    plan = mx.Plan(w, PAD_H, PAD_W)
+    t_plan = time.perf_counter() - t0
+    out = {"weights_and_plan_s": t_plan}
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "weights.mxw")
+        for key, kw in (("gpu_new_s", {}), ("gpu_new_cache_write_s", {"weight_cache": path}),
+                        ("gpu_new_cache_read_s", {"weight_cache": path})):
+            t0 = time.perf_counter()
+            g = mx.Gpu(plan, device=local, **kw)
+            out[key] = time.perf_counter() - t0
+            out[key.replace("_s", "_phases")] = g.build_info()
+            g.close()
+        out["cache_file_bytes"] = os.path.getsize(path)
+    return out
+
+
+def e2e_rgb8(mx, gpu, steps):
+    """The single-image public path with its per-pixel steps on the device
+    (mx_gpu_run_rgb8): 8-bit 1280x853 RGB from host memory in, the restored
+    8-bit image out, one synchronous call per image."""
+    synth = importlib.import_module("maxim-rs_b200.synth")
+    rng = synth.input_rng(IN_SEED)
+    imgs = [np.ascontiguousarray((np.floor(synth.image_uniform(rng, IMG_H, IMG_W) * np.float32(255) +
+                                           np.float32(0.5))).astype(np.uint8).transpose(1, 2, 0))
+            for _ in range(2)]
+    out = np.empty_like(imgs[0])
+    for i in range(3):
+        gpu.run_rgb8(imgs[i % 2], out=out)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        gpu.run_rgb8(imgs[i % 2], out=out)
+    dt = time.perf_counter() - t0
+    nbytes = IMG_H * IMG_W * 3
+    return {"value": steps * IMG_H * IMG_W / dt / 1e6, "unit": "Mpx/s", "images": steps, "seconds": dt,
+            "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+            "api": "mx_gpu_run_rgb8 (one image per call, no overlap)"}
+
+
 def run_native(args):
     import torch
     import torch.distributed as dist
@@ -606,6 +652,7 @@ def run_native(args):
             "gpu_launches": int(stats["kernels"] * args.steps * B),
             "roofline": roof, "clocks": clk.summary()}
     if rank == 0 and world == 1:
+        line["e2e_rgb8"] = e2e_rgb8(mx, gpu, args.steps)
         with Clocks(uuid) as clk4:
             line["latency_2048"] = latency_2048(mx, local)
         line["latency_2048"]["clocks"] = clk4.summary()
@@ -616,6 +663,8 @@ def run_native(args):
             line["config3_gmlp"] = config3_gmlp(mx, local)
         line["config3_gmlp"]["clocks"] = clk3.summary()
     gpu.close()
+    if rank == 0 and world == 1:
+        line["startup"] = startup_times(mx, local)
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(len(os.sched_getaffinity(0)))
     if world > 1:

@@ -143,6 +143,42 @@ int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out);
  * free (a GPU shared with other work). 0 means the device's free memory. No
  * counterpart in the reference. */
 int mx_gpu_new_budget(int device, const mx_plan* plan, int64_t budget_bytes, mx_gpu** out);
+/* The same, with a converted-weights cache file (the weights loader's
+ * on-disk format; the reference derives its layouts at every start,
+ * src/weights.rs:57-211). Besides the plan's own layouts the executor derives
+ * tensor-core ones from every weight (tap-major orders, TF32 hi/lo halves,
+ * transposes); a cache file holds those derived layouts, each tagged with
+ * the length and a 64-bit hash of the plan weight it was made from. At
+ * construction every layout whose source weight is unchanged is read from
+ * the file instead of derived, at any image size and in either walk; the
+ * rest are derived, and when anything was derived the file is (re)written
+ * (under a temporary name, then renamed). A missing file is an empty cache;
+ * a file that is not a cache is refused (MX_E_IO); a cache of another
+ * format version is ignored. Passes are bit for bit those of mx_gpu_new.
+ * cache_path null is mx_gpu_new_budget. */
+int mx_gpu_new_cached(int device, const mx_plan* plan, int64_t budget_bytes, const char* cache_path, mx_gpu** out);
+/* Write this executor's derived layouts to a cache file now (the executor
+ * must come from mx_gpu_new_cached, which records the source weights'
+ * hashes). */
+int mx_gpu_save_weight_cache(mx_gpu* g, const char* path);
+/* How the executor was built: weight layouts `loaded` from the cache file
+ * and `derived` from the plan's weights; `cache_saved` 1 when
+ * mx_gpu_new_cached wrote the file, 0 when it had no reason to, -1 when
+ * writing it failed; and the wall time of each phase: reading and indexing
+ * the cache file, scheduling and making the steps (which derives the layouts
+ * not loaded), device allocation with the weight upload and tensor maps, and
+ * writing the cache. No counterpart in the reference. */
+typedef struct mx_build_info {
+  int64_t layouts_loaded;
+  int64_t layouts_derived;
+  int32_t cache_saved;
+  int32_t reserved;
+  double seconds_cache_read;
+  double seconds_steps;
+  double seconds_device;
+  double seconds_cache_write;
+} mx_build_info;
+int mx_gpu_build_info(mx_gpu* g, mx_build_info* out);
 void mx_gpu_free(mx_gpu* g);
 
 /* `Gpu::run` (src/exec_gpu.rs:196-229): input [3][H][W] host floats in,

@@ -53,6 +53,13 @@ class mx_gpu_stats(ctypes.Structure):
                 ("perms_dropped", ctypes.c_int64), ("pass_arena_bytes", ctypes.c_int64)]
 
 
+class mx_build_info(ctypes.Structure):
+    _fields_ = [("layouts_loaded", ctypes.c_int64), ("layouts_derived", ctypes.c_int64),
+                ("cache_saved", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("seconds_cache_read", ctypes.c_double), ("seconds_steps", ctypes.c_double),
+                ("seconds_device", ctypes.c_double), ("seconds_cache_write", ctypes.c_double)]
+
+
 class mx_batch_worker(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int32), ("state", ctypes.c_int32), ("error_code", ctypes.c_int32),
                 ("images_done", ctypes.c_int32), ("seconds", ctypes.c_double), ("error", ctypes.c_char * 256)]
@@ -96,6 +103,10 @@ _SIGS = {
     "mx_device_count": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "mx_gpu_new": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(mx_plan), ctypes.POINTER(ctypes.c_void_p)]),
     "mx_gpu_free": (None, [ctypes.c_void_p]),
+    "mx_gpu_new_cached": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(mx_plan), ctypes.c_int64, ctypes.c_char_p,
+                                         ctypes.POINTER(ctypes.c_void_p)]),
+    "mx_gpu_save_weight_cache": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p]),
+    "mx_gpu_build_info": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(mx_build_info)]),
     "mx_gpu_run": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "mx_gpu_upload_input": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "mx_gpu_enqueue": (ctypes.c_int, [ctypes.c_void_p]),
@@ -314,10 +325,18 @@ def device_count():
 class Gpu:
     """`exec_gpu::Gpu` (src/exec_gpu.rs:48-357) on one device, over the C ABI."""
 
-    def __init__(self, plan, device=0):
+    def __init__(self, plan, device=0, weight_cache=None, mem_budget=0):
+        """weight_cache: path of a converted-weights cache file
+        (`mx_gpu_new_cached`): layouts found there are loaded, the rest
+        derived and the file written."""
         self.plan = plan
         self._h = ctypes.c_void_p()
-        check(lib().mx_gpu_new(device, plan.view, ctypes.byref(self._h)), "gpu")
+        if weight_cache is None and not mem_budget:
+            check(lib().mx_gpu_new(device, plan.view, ctypes.byref(self._h)), "gpu")
+        else:
+            check(lib().mx_gpu_new_cached(device, plan.view, mem_budget,
+                                          None if weight_cache is None else os.fsencode(weight_cache),
+                                          ctypes.byref(self._h)), "gpu")
         c, h, w = plan.buf(plan.input)
         self.in_len = c * h * w
         c, h, w = plan.buf(plan.output)
@@ -339,6 +358,21 @@ class Gpu:
             out = np.empty(self.out_shape, np.float32)
         check(lib().mx_gpu_run(self._h, _ptr(x), _ptr(out)), "run")
         return out
+
+    def build_info(self):
+        """`mx_gpu_build_info` as a dict: layouts loaded / derived, whether the
+        cache was saved, and the construction phases' seconds."""
+        b = mx_build_info()
+        check(lib().mx_gpu_build_info(self._h, ctypes.byref(b)))
+        return {f: getattr(b, f) for f, _ in b._fields_ if f != "reserved"}
+
+    def weight_cache_info(self):
+        """(loaded, derived, saved): how the executor's weight layouts were obtained."""
+        b = self.build_info()
+        return b["layouts_loaded"], b["layouts_derived"], b["cache_saved"]
+
+    def save_weight_cache(self, path):
+        check(lib().mx_gpu_save_weight_cache(self._h, os.fsencode(path)), str(path))
 
     def run_rgb8(self, rgb, factor=64, out=None):
         """The image path with its per-pixel steps on the device: h x w x 3 uint8

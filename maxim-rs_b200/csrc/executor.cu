@@ -22,6 +22,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <climits>
 #include <cmath>
 #include <cstdlib>
@@ -34,6 +35,13 @@
 #include <vector>
 
 #include <cudaTypedefs.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cerrno>
+#include <cstdio>
 
 #include "common.h"
 #include "gpu_common.cuh"
@@ -98,21 +106,67 @@ HostTaps make_taps(int n_in, int n_out, int max_taps) {
   return t;
 }
 
+// One converted layout read back from a converted-weights cache file: the
+// source blob's length and hash it was made from, and the layout itself.
+struct WcEntry {
+  uint64_t src_hash = 0;
+  int64_t src_len = 0;
+  const float* data = nullptr;  // into the file's bytes, held by the handle while it is built
+  int64_t len = 0;              // floats
+};
+
+// A read-only mapping of a whole file (the converted-weights cache), pages
+// populated up front.
+struct FileMap {
+  const char* p = nullptr;
+  size_t n = 0;
+  FileMap() = default;
+  FileMap(const FileMap&) = delete;
+  FileMap& operator=(const FileMap&) = delete;
+  ~FileMap() { reset(); }
+  void reset() {
+    if (p) munmap(const_cast<char*>(p), n);
+    p = nullptr;
+    n = 0;
+  }
+};
+
 // A bump allocator over one device allocation: weights and tables, each
-// 256-byte aligned.
+// 256-byte aligned. The host image grows by realloc (which moves large
+// blocks by remapping pages, not copying) and is never zero-filled beyond
+// the alignment gaps: a std::vector's resize cleared and re-copied the whole
+// image at every doubling, most of an executor's construction time.
 struct DevicePool {
-  std::vector<char> host;
+  char* host = nullptr;
+  size_t len = 0, cap = 0;
   char* dev = nullptr;
-  size_t size() const { return host.size(); }
+  DevicePool() = default;
+  DevicePool(const DevicePool&) = delete;
+  DevicePool& operator=(const DevicePool&) = delete;
+  ~DevicePool() { free(host); }
+  size_t size() const { return len; }
   size_t put(const void* data, size_t bytes) {
-    size_t off = (host.size() + 255) & ~size_t(255);
-    host.resize(off + bytes);
-    if (bytes) memcpy(&host[off], data, bytes);
+    const size_t off = (len + 255) & ~size_t(255), need = off + bytes;
+    if (need > cap) {
+      size_t nc = cap ? cap : (size_t(1) << 20);
+      while (nc < need) nc *= 2;
+      char* q = static_cast<char*>(realloc(host, nc));
+      if (!q) throw std::bad_alloc();
+      host = q, cap = nc;
+    }
+    if (off > len) memset(host + len, 0, off - len);
+    if (bytes) memcpy(host + off, data, bytes);
+    len = need;
     return off;
   }
   template <class T>
   size_t put(const std::vector<T>& v) {
     return put(v.data(), v.size() * sizeof(T));
+  }
+  void drop_host() {
+    free(host);
+    host = nullptr;
+    cap = 0;
   }
 };
 
@@ -244,6 +298,17 @@ struct mx_gpu {
   uint8_t* rgb_in = nullptr;
   uint8_t* rgb_out = nullptr;
   int32_t rgb_h = 0, rgb_w = 0, rgb_even_h = 0, rgb_even_w = 0;
+  // The converted-weights cache (mx_gpu_new_cached, mx_gpu_save_weight_cache).
+  const mx_plan* building = nullptr;  // the caller's plan, while the steps are made
+  bool wc_track = false;              // hash source weights (a cache file is in use)
+  mx::FileMap wc_file;                // the cache file, mapped while the steps are made
+  std::map<std::pair<int32_t, int>, mx::WcEntry> wc_loaded;  // layouts read from the file, not yet used
+  std::map<int32_t, uint64_t> wc_hash;                       // weight id -> hash of its plan blob
+  std::map<int32_t, int64_t> wsrc_len;                       // weight id -> its plan blob's length
+  std::map<std::pair<int32_t, int>, int64_t> wbytes;        // (weight id, layout) -> bytes in the pool
+  int64_t wc_hits = 0, wc_converted = 0;
+  int wc_saved = 0;
+  double t_cache_read = 0, t_steps = 0, t_device = 0, t_cache_write = 0;  // construction phases, seconds
 };
 
 namespace mx {
@@ -452,16 +517,90 @@ enum WeightTag : int {
   WT_T = 10,     // a 1x1 kernel transposed to [c_in][c_out] (the small-conv kernel)
   WT_CONV3F = 11,  // a 32-to-32 3x3 kernel for umma_conv3f_kernel: [ky][hi, lo][kx][c_out][c_in]
 };
+// 64-bit hash of a weight blob's bytes (multiply-rotate over 8-byte words,
+// then a final avalanche): what ties a cached layout to the weights it was
+// made from.
+uint64_t blob_hash(const float* p, int64_t n) {
+  const uint64_t k1 = 0x9E3779B97F4A7C15ull, k2 = 0xC2B2AE3D27D4EB4Full;
+  auto mix = [&](uint64_t h, uint64_t x) {
+    h ^= x * k2;
+    return ((h << 31) | (h >> 33)) * k1;
+  };
+  const unsigned char* b = reinterpret_cast<const unsigned char*>(p);
+  const size_t bytes = size_t(n) * 4;
+  // Four independent lanes over 32-byte blocks, so the multiplies overlap.
+  uint64_t h[4] = {uint64_t(n) * k1, k2, k1 ^ k2, uint64_t(n) ^ k2};
+  size_t i = 0;
+  for (; i + 32 <= bytes; i += 32) {
+    uint64_t x[4];
+    memcpy(x, b + i, 32);
+    for (int l = 0; l < 4; ++l) h[l] = mix(h[l], x[l]);
+  }
+  uint64_t r = mix(mix(mix(h[0], h[1]), h[2]), h[3]);
+  for (; i < bytes; i += 8) {
+    uint64_t x = 0;
+    memcpy(&x, b + i, std::min<size_t>(8, bytes - i));
+    r = mix(r, x);
+  }
+  r ^= r >> 33;
+  r *= k2;
+  r ^= r >> 29;
+  return r;
+}
+
+uint64_t src_hash(mx_gpu& g, int32_t id) {
+  auto it = g.wc_hash.find(id);
+  if (it != g.wc_hash.end()) return it->second;
+  if (!g.building) throw Error("weight cache: no plan to hash");
+  const uint64_t h = blob_hash(g.building->weights[id], g.building->weight_lens[id]);
+  g.wc_hash[id] = h;
+  g.wsrc_len[id] = g.building->weight_lens[id];
+  return h;
+}
+
+// Whether the cache file held this layout, made from the weight blob the plan
+// holds now (same length and hash).
+bool cache_has(mx_gpu& g, const std::pair<int32_t, int>& key) {
+  if (g.wc_loaded.empty()) return false;
+  auto it = g.wc_loaded.find(key);
+  return it != g.wc_loaded.end() && it->second.src_len == g.building->weight_lens[key.first] &&
+         it->second.src_hash == src_hash(g, key.first);
+}
+
+WcEntry cache_take(mx_gpu& g, const std::pair<int32_t, int>& key) {
+  auto it = g.wc_loaded.find(key);
+  const WcEntry e = it->second;
+  g.wc_loaded.erase(it);
+  ++g.wc_hits;
+  return e;
+}
+
 int64_t cached(mx_gpu& g, int32_t id, int tag, const std::function<std::vector<float>()>& make) {
   if (id < 0) return -1;
   const auto key = std::make_pair(id, tag);
   auto it = g.wcache.find(key);
   if (it != g.wcache.end()) return it->second;
-  const std::vector<float> v = make();
+  std::vector<float> v;
+  const float* data = nullptr;
+  int64_t len = 0;
+  if (tag == WT_RAW && g.building) {
+    data = g.building->weights[id], len = g.building->weight_lens[id];  // as the plan holds it
+  } else if (tag != WT_RAW && cache_has(g, key)) {
+    const WcEntry e = cache_take(g, key);
+    data = e.data, len = e.len;
+  } else {
+    v = make();
+    data = v.data(), len = int64_t(v.size());
+    if (tag != WT_RAW) {
+      ++g.wc_converted;
+      if (g.wc_track) src_hash(g, id);  // known for a later save
+    }
+  }
   int64_t off = -1;
-  if (!v.empty()) {
-    off = int64_t(g.pool.put(v));
-    g.weight_bytes += int64_t(v.size() * 4);
+  if (len > 0) {
+    off = int64_t(g.pool.put(data, size_t(len) * 4));
+    g.weight_bytes += len * 4;
+    if (tag != WT_RAW) g.wbytes[key] = len * 4;
   }
   g.wcache[key] = off;
   return off;
@@ -790,11 +929,24 @@ std::pair<int64_t, int64_t> cached_split(mx_gpu& g, int32_t id, int tag_hi, int 
   auto ih = g.wcache.find(kh), il = g.wcache.find(kl);
   if (ih != g.wcache.end() && il != g.wcache.end()) return {ih->second, il->second};
   std::vector<float> hi, lo;
-  split_tf32(make(), hi, lo);
-  const int64_t oh = int64_t(g.pool.put(hi)), ol = int64_t(g.pool.put(lo));
-  g.weight_bytes += int64_t(2 * hi.size() * 4);
+  WcEntry eh, el;
+  if (cache_has(g, kh) && cache_has(g, kl)) {
+    eh = cache_take(g, kh);
+    el = cache_take(g, kl);
+  } else {
+    split_tf32(make(), hi, lo);
+    eh.data = hi.data(), eh.len = int64_t(hi.size());
+    el.data = lo.data(), el.len = int64_t(lo.size());
+    g.wc_converted += 2;
+    if (g.wc_track) src_hash(g, id);
+  }
+  const int64_t oh = int64_t(g.pool.put(eh.data, size_t(eh.len) * 4));
+  const int64_t ol = int64_t(g.pool.put(el.data, size_t(el.len) * 4));
+  g.weight_bytes += (eh.len + el.len) * 4;
   g.wcache[kh] = oh;
   g.wcache[kl] = ol;
+  g.wbytes[kh] = eh.len * 4;
+  g.wbytes[kl] = el.len * 4;
   return {oh, ol};
 }
 
@@ -1456,6 +1608,120 @@ void check_status(mx_gpu& g) {
 // Every weight an op names must be present with exactly the length the op's
 // layout needs; a plan built without a checkpoint (empty blobs) is refused
 // here rather than read out of bounds.
+// The converted-weights cache file: every layout the executor derived from
+// the plan's weights (tensor-core tap-major orders, TF32 hi/lo halves,
+// transposes), so a later executor for the same checkpoint, at any image
+// size, uploads them instead of deriving them again. Little-endian:
+//   "MXWCACHE", u32 format version, u32 entry count, then per entry
+//   i32 weight id, i32 layout tag, u64 source-blob hash, i64 source length
+//   (floats), i64 layout length (floats), the layout's floats.
+// An entry is used only when the plan's blob for that weight id has the
+// recorded length and hash; anything else is derived afresh. The version
+// changes whenever a layout's definition changes, and a file of another
+// version is ignored as a whole.
+constexpr char kWcMagic[8] = {'M', 'X', 'W', 'C', 'A', 'C', 'H', 'E'};
+constexpr uint32_t kWcVersion = 1;
+
+// Maps the whole file into `map` and indexes it; the entries point into the
+// mapping.
+std::map<std::pair<int32_t, int>, WcEntry> load_weight_cache(const std::string& path, FileMap& map) {
+  std::map<std::pair<int32_t, int>, WcEntry> m;
+  const int fd = open(path.c_str(), O_RDONLY | O_CLOEXEC);
+  if (fd < 0) {
+    if (errno == ENOENT) return m;  // no cache yet: everything is derived, then saved
+    throw Error(path + ": " + strerror(errno), MX_E_IO);
+  }
+  struct stat st;
+  if (fstat(fd, &st) != 0) {
+    close(fd);
+    throw Error(path + ": " + strerror(errno), MX_E_IO);
+  }
+  const size_t size = size_t(st.st_size);
+  if (size > 0) {
+    void* p = mmap(nullptr, size, PROT_READ, MAP_PRIVATE | MAP_POPULATE, fd, 0);
+    if (p == MAP_FAILED) {
+      close(fd);
+      throw Error(path + ": " + strerror(errno), MX_E_IO);
+    }
+    map.p = static_cast<const char*>(p);
+    map.n = size;
+  }
+  close(fd);
+  size_t at = 0;
+  auto rd = [&](void* p, size_t n) {
+    if (n > size - at) throw Error(path + ": truncated converted-weights cache", MX_E_IO);
+    memcpy(p, map.p + at, n);
+    at += n;
+  };
+  char magic[8];
+  uint32_t version = 0, count = 0;
+  rd(magic, 8);
+  if (memcmp(magic, kWcMagic, 8) != 0) throw Error(path + ": not a converted-weights cache", MX_E_IO);
+  rd(&version, 4);
+  if (version != kWcVersion) return m;  // another layout definition: derive everything again
+  rd(&count, 4);
+  for (uint32_t i = 0; i < count; ++i) {
+    int32_t id = 0, tag = 0;
+    WcEntry e;
+    rd(&id, 4);
+    rd(&tag, 4);
+    rd(&e.src_hash, 8);
+    rd(&e.src_len, 8);
+    rd(&e.len, 8);
+    if (id < 0 || e.len < 0 || e.len > (int64_t(1) << 31) || e.src_len < 0 || size_t(e.len) * 4 > size - at)
+      throw Error(path + ": corrupt converted-weights cache entry", MX_E_IO);
+    e.data = reinterpret_cast<const float*>(map.p + at);  // 4-byte aligned: the header and entry heads are
+    at += size_t(e.len) * 4;
+    m[std::make_pair(id, int(tag))] = e;
+  }
+  return m;
+}
+
+// Every derived layout of this handle, read back from its weight pool, into
+// `path` (written beside it under a temporary name, then renamed over it).
+void save_weight_cache(mx_gpu& g, const std::string& path) {
+  if (g.wbytes.empty()) throw Error("weight cache: this executor derived no weight layouts");
+  if (!g.wc_track)
+    throw Error("weight cache: build the executor with mx_gpu_new_cached to save its layouts (the source weights' "
+                "hashes are taken only then)");
+  const std::string tmp = path + fmt(".tmp%d", int(getpid()));
+  FILE* f = fopen(tmp.c_str(), "wb");
+  if (!f) throw Error(tmp + ": " + strerror(errno), MX_E_IO);
+  bool ok = true;
+  auto wr = [&](const void* p, size_t n) { ok = ok && fwrite(p, 1, n, f) == n; };
+  const uint32_t n = uint32_t(g.wbytes.size());
+  wr(kWcMagic, 8);
+  wr(&kWcVersion, 4);
+  wr(&n, 4);
+  std::vector<float> buf;
+  try {
+    for (const auto& kv : g.wbytes) {
+      const int32_t id = kv.first.first, tag = kv.first.second;
+      const int64_t off = g.wcache.at(kv.first), len = kv.second / 4;
+      auto h = g.wc_hash.find(id);
+      if (h == g.wc_hash.end()) throw Error(fmt("weight cache: weight %d was never hashed", id));
+      const int64_t src_len = g.wsrc_len.at(id);
+      buf.resize(size_t(len));
+      MX_CUDA(cudaMemcpy(buf.data(), g.pool.dev + off, size_t(kv.second), cudaMemcpyDeviceToHost));
+      wr(&id, 4);
+      wr(&tag, 4);
+      wr(&h->second, 8);
+      wr(&src_len, 8);
+      wr(&len, 8);
+      wr(buf.data(), size_t(kv.second));
+    }
+  } catch (...) {
+    fclose(f);
+    unlink(tmp.c_str());
+    throw;
+  }
+  ok = (fclose(f) == 0) && ok;
+  if (!ok || rename(tmp.c_str(), path.c_str()) != 0) {
+    unlink(tmp.c_str());
+    throw Error(path + ": could not write the converted-weights cache", MX_E_IO);
+  }
+}
+
 void validate_weights(const mx_plan& plan) {
   auto need = [&](int32_t oi, int32_t id, int64_t n, const char* what) {
     if (id < 0) return;
@@ -1645,6 +1911,10 @@ int mx_device_count(int* count) {
 int mx_gpu_new(int device, const mx_plan* plan, mx_gpu** out) { return mx_gpu_new_budget(device, plan, 0, out); }
 
 int mx_gpu_new_budget(int device, const mx_plan* plan, int64_t budget_bytes, mx_gpu** out) {
+  return mx_gpu_new_cached(device, plan, budget_bytes, nullptr, out);
+}
+
+int mx_gpu_new_cached(int device, const mx_plan* plan, int64_t budget_bytes, const char* cache_path, mx_gpu** out) {
   std::unique_ptr<mx_gpu> g;
   int rc = guard([&] {
     if (budget_bytes < 0) throw Error("mx_gpu_new_budget: negative budget");
@@ -1659,6 +1929,16 @@ int mx_gpu_new_budget(int device, const mx_plan* plan, int64_t budget_bytes, mx_
     g->device = device;
     validate_weights(*plan);
     g->use_umma = std::getenv("MAXIM_NO_UMMA") == nullptr;
+    g->building = plan;
+    g->wc_track = cache_path != nullptr;
+    auto now = [] { return std::chrono::steady_clock::now(); };
+    auto secs = [](std::chrono::steady_clock::time_point a, std::chrono::steady_clock::time_point b) {
+      return std::chrono::duration<double>(b - a).count();
+    };
+    auto t0 = now();
+    if (cache_path) g->wc_loaded = load_weight_cache(cache_path, g->wc_file);
+    auto t1 = now();
+    g->t_cache_read = secs(t0, t1);
     const Schedule S = plan_schedule(*g, *plan);
 
     // The op-by-op walk, at the plan's offsets.
@@ -1693,6 +1973,11 @@ int mx_gpu_new_budget(int device, const mx_plan* plan, int64_t budget_bytes, mx_
     }
     add_boundary_steps(*g, g->fsteps, &g->foffs);
     for (auto& st : g->fsteps) g->kernels += st.kernels;
+    g->building = nullptr;
+    g->wc_loaded.clear();
+    g->wc_file.reset();
+    auto t2 = now();
+    g->t_steps = secs(t1, t2);
 
     // Size the pass before allocating it, and refuse it with the numbers
     // (src/exec_gpu.rs:96-146). One arena serves both walks.
@@ -1725,9 +2010,8 @@ int mx_gpu_new_budget(int device, const mx_plan* plan, int64_t budget_bytes, mx_
                       (long long)(free_b >> 20), cudaGetErrorString(e)),
                   MX_E_OOM);
     MX_CUDA(cudaMalloc(&g->pool.dev, std::max<size_t>(g->pool.size(), 256)));
-    MX_CUDA(cudaMemcpy(g->pool.dev, g->pool.host.data(), g->pool.size(), cudaMemcpyHostToDevice));
-    g->pool.host.clear();
-    g->pool.host.shrink_to_fit();
+    MX_CUDA(cudaMemcpy(g->pool.dev, g->pool.host, g->pool.size(), cudaMemcpyHostToDevice));
+    g->pool.drop_host();
     MX_CUDA(cudaMalloc(&g->io_in, size_t(len_of(g->bufs[size_t(g->input)]) * 4)));
     MX_CUDA(cudaMalloc(&g->io_out, size_t(len_of(g->bufs[size_t(g->output)]) * 4)));
     if (g->scratch_len > 0) MX_CUDA(cudaMalloc(&g->scratch, size_t(g->scratch_len) * 4));
@@ -1748,10 +2032,45 @@ int mx_gpu_new_budget(int device, const mx_plan* plan, int64_t budget_bytes, mx_
       if (st.prepare) st.prepare();
     for (auto& st : g->fsteps)
       if (st.prepare) st.prepare();
+    auto t3 = now();
+    g->t_device = secs(t2, t3);
+    // Save what had to be derived, so the next executor for these weights
+    // finds it. A cache that cannot be written does not stop this one.
+    if (cache_path && g->wc_converted > 0) {
+      try {
+        save_weight_cache(*g, cache_path);
+        g->wc_saved = 1;
+      } catch (const Error&) {
+        g->wc_saved = -1;
+      }
+    }
+    g->t_cache_write = secs(t3, now());
     *out = g.release();
   });
   if (rc != MX_OK && g) mx_gpu_free(g.release());
   return rc;
+}
+
+int mx_gpu_save_weight_cache(mx_gpu* g, const char* path) {
+  return guard([&] {
+    if (!g || !path) throw Error("mx_gpu_save_weight_cache: null argument");
+    DevicePin pin(g->device);
+    save_weight_cache(*g, path);
+  });
+}
+
+int mx_gpu_build_info(mx_gpu* g, mx_build_info* out) {
+  return guard([&] {
+    if (!g || !out) throw Error("mx_gpu_build_info: null argument");
+    memset(out, 0, sizeof(*out));
+    out->layouts_loaded = g->wc_hits;
+    out->layouts_derived = g->wc_converted;
+    out->cache_saved = g->wc_saved;
+    out->seconds_cache_read = g->t_cache_read;
+    out->seconds_steps = g->t_steps;
+    out->seconds_device = g->t_device;
+    out->seconds_cache_write = g->t_cache_write;
+  });
 }
 
 void mx_gpu_free(mx_gpu* g) {
