@@ -535,6 +535,34 @@ def e2e_rgb8(mx, gpu, steps):
             "api": "mx_gpu_run_rgb8 (one image per call, no overlap)"}
 
 
+def e2e_png(mx, plan, local, steps):
+    """PNG files in, PNG files out through the batch runner's PNG path
+    (mx_batch_run_png) on this GPU: decode, device-side pad / crop / round,
+    encode and file I/O all inside the timed region."""
+    import tempfile
+    synth = importlib.import_module("maxim-rs_b200.synth")
+    rng = synth.input_rng(IN_SEED)
+    with tempfile.TemporaryDirectory() as d:
+        ins = []
+        for k in range(2):
+            im = (np.floor(synth.image_uniform(rng, IMG_H, IMG_W) * np.float32(255) + np.float32(0.5))).astype(
+                np.uint8).transpose(1, 2, 0)
+            ins.append(os.path.join(d, "in%d.png" % k))
+            mx.png_write_rgb8(ins[-1], im)
+        runner = mx.Batch(plan, devices=(local,))
+        outs = [os.path.join(d, "out%d.png" % i) for i in range(steps)]
+        runner.run_png(ins, outs[:2])
+        t0 = time.perf_counter()
+        runner.run_png([ins[i % 2] for i in range(steps)], outs)
+        dt = time.perf_counter() - t0
+        in_bytes = sum(os.path.getsize(p) for p in ins) / 2
+        runner.close()
+    nbytes = IMG_H * IMG_W * 3
+    return {"value": steps * IMG_H * IMG_W / dt / 1e6, "unit": "Mpx/s", "images": steps, "seconds": dt,
+            "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes, "png_bytes_per_image": in_bytes,
+            "api": "mx_batch_run_png (decode and encode overlapping the passes)"}
+
+
 def run_native(args):
     import torch
     import torch.distributed as dist
@@ -653,6 +681,7 @@ def run_native(args):
             "roofline": roof, "clocks": clk.summary()}
     if rank == 0 and world == 1:
         line["e2e_rgb8"] = e2e_rgb8(mx, gpu, args.steps)
+        line["e2e_png"] = e2e_png(mx, plan, local, args.steps)
         with Clocks(uuid) as clk4:
             line["latency_2048"] = latency_2048(mx, local)
         line["latency_2048"]["clocks"] = clk4.summary()

@@ -377,6 +377,20 @@ int mx_batch_new(const mx_batch_config* cfg, const int32_t* devices, int32_t n_d
  * MX_OK / MX_E_*. Synchronous. */
 int mx_batch_run(mx_batch* b, int32_t n_images, const float* const* inputs, float* const* outputs,
                  int32_t* image_status);
+/* PNG files in, PNG files out, over the device-side image path
+ * (mx_gpu_run_rgb8): in_paths[i] is read, decoded, padded on the GPU,
+ * restored, cropped and rounded on the GPU, and written to out_paths[i] as
+ * an RGB PNG. Every image must pad (by `factor`) to the plan's input shape.
+ * Each worker reads and decodes its next image while the GPU runs the
+ * current one (two in flight), and encoder threads of its own (the host
+ * threads left over, shared out: one to four a worker) compress and write
+ * the finished ones at zlib level 1, so the PNG work overlaps the passes. An
+ * image that cannot be read, decoded, padded to the plan's shape or written
+ * fails alone (its image_status); a device failure retires the worker and
+ * its unfinished images go to the others, as in mx_batch_run. Needs the
+ * built-in GPU executor. Synchronous. */
+int mx_batch_run_png(mx_batch* b, int32_t n_images, const char* const* in_paths, const char* const* out_paths,
+                     int32_t factor, int32_t* image_status);
 int32_t mx_batch_worker_count(const mx_batch* b);
 int mx_batch_workers(const mx_batch* b, mx_batch_worker* out, int32_t n);
 void mx_batch_free(mx_batch* b);

@@ -142,6 +142,9 @@ _SIGS = {
                                     ctypes.POINTER(mx_batch_executor), ctypes.POINTER(ctypes.c_void_p)]),
     "mx_batch_run": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p),
                                     ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_int32)]),
+    "mx_batch_run_png": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_char_p),
+                                        ctypes.POINTER(ctypes.c_char_p), ctypes.c_int32,
+                                        ctypes.POINTER(ctypes.c_int32)]),
     "mx_batch_worker_count": (ctypes.c_int32, [ctypes.c_void_p]),
     "mx_batch_workers": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(mx_batch_worker), ctypes.c_int32]),
     "mx_batch_free": (None, [ctypes.c_void_p]),
@@ -559,6 +562,21 @@ class Batch:
         if rc != MX_OK and raise_on_error:
             raise MaximError(rc, "batch: " + last_error())
         return outs, status
+
+    def run_png(self, in_paths, out_paths, factor=64, raise_on_error=True):
+        """`mx_batch_run_png`: PNG files in, PNG files out over the device-side
+        image path; returns the per-image status codes."""
+        n = len(in_paths)
+        if len(out_paths) != n:
+            raise ValueError("in_paths and out_paths differ in length")
+        ip = (ctypes.c_char_p * n)(*[os.fsencode(p) for p in in_paths])
+        op = (ctypes.c_char_p * n)(*[os.fsencode(p) for p in out_paths])
+        st = (ctypes.c_int32 * n)()
+        rc = lib().mx_batch_run_png(self._h, n, ip, op, factor, st)
+        status = [int(v) for v in st]
+        if rc != MX_OK and raise_on_error:
+            raise MaximError(rc, "batch: " + last_error())
+        return status
 
     def workers(self):
         n = lib().mx_batch_worker_count(self._h)

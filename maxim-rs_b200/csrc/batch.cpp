@@ -23,7 +23,11 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cerrno>
 #include <chrono>
+#include <condition_variable>
+#include <cstdio>
+#include <deque>
 #include <cstring>
 #include <exception>
 #include <memory>
@@ -34,6 +38,7 @@
 
 #include "common.h"
 #include "gpu_common.cuh"
+#include "image.h"
 #include "maxim_b200.h"
 
 namespace mx {
@@ -148,6 +153,191 @@ size_t gpu_run_list(GpuWorker* w, const std::vector<int32_t>& list, const float*
   for (size_t j = list.size() >= 2 ? list.size() - 2 : 0; j < list.size(); ++j)
     if (j >= done && !collect(j)) return done;
   return done;
+}
+
+// ---- PNG files in, PNG files out, through the device-side image path
+//
+// Per worker: this thread reads and decodes image j+1 and copies it into a
+// pinned 8-bit slot while the GPU runs image j (two in flight, as above);
+// finished images go to the worker's encoder thread, which compresses and
+// writes them while the next ones run. Only 8-bit images cross PCIe. An
+// image that cannot be read, decoded or written fails alone; a device
+// failure retires the worker as above.
+struct PngItem {
+  int32_t img = -1;
+  int64_t h = 0, w = 0;
+  std::vector<uint8_t> rgb;
+};
+
+struct Encoder {
+  std::mutex mu;
+  std::condition_variable cv;
+  std::deque<PngItem> q;
+  bool closed = false;
+  std::vector<std::thread> th;
+};
+
+// zlib level of the batch's PNG writer. Deflate's cost depends on the data:
+// at level 6 a noisy image with few distinct values (the output of an
+// untrained checkpoint, say) took 340-420 ms to compress against 40 ms at
+// level 1, for 40% more bytes; level 1 keeps the writer behind the GPU. The
+// pixels are the same at every level.
+constexpr int kBatchPngLevel = 1;
+
+// Encoder threads per worker: the host threads left over after one per
+// worker, shared out, at least one and at most four.
+int encoder_threads(size_t workers) {
+  const int hw = int(std::thread::hardware_concurrency());
+  const int w = int(std::max<size_t>(workers, 1));
+  return std::max(1, std::min(4, (hw - w) / w));
+}
+
+struct PngSlots {
+  uint8_t* in[2] = {nullptr, nullptr};
+  uint8_t* out[2] = {nullptr, nullptr};
+  size_t cap = 0;
+  ~PngSlots() {
+    for (int k = 0; k < 2; ++k) {
+      cudaFreeHost(in[k]);
+      cudaFreeHost(out[k]);
+    }
+  }
+};
+
+// Returns how many images of `list` were dealt with (restored and handed to
+// the encoder, or failed on their own); the rest, from the returned index
+// on, are the caller's to hand to other workers after a device failure
+// (*rc, *msg).
+size_t png_run_list(GpuWorker* w, const std::vector<int32_t>& list, const char* const* in_paths,
+                    const char* const* out_paths, int32_t factor, int n_encoders, std::vector<int32_t>& status,
+                    std::vector<std::string>& why, int* rc, std::string* msg) {
+  *rc = MX_OK;
+  void* sp = nullptr;
+  if ((*rc = mx_gpu_stream(w->g, &sp)) != MX_OK || (*rc = guard([&] { MX_CUDA(cudaSetDevice(w->device)); })) != MX_OK) {
+    *msg = last_message();
+    return 0;
+  }
+  cudaStream_t stream = static_cast<cudaStream_t>(sp);
+  const size_t cap = w->in_len;  // floats of the padded [3][H][W] input = bytes of an H x W x 3 image
+  PngSlots slots;
+  int r0 = guard([&] {
+    for (int k = 0; k < 2; ++k) {
+      MX_CUDA(cudaMallocHost(&slots.in[k], cap));
+      MX_CUDA(cudaMallocHost(&slots.out[k], cap));
+    }
+  });
+  if (r0 != MX_OK) {
+    *rc = r0, *msg = last_message();
+    return 0;
+  }
+  Encoder enc;
+  for (int t = 0; t < n_encoders; ++t) enc.th.emplace_back([&] {
+    for (;;) {
+      PngItem it;
+      {
+        std::unique_lock<std::mutex> l(enc.mu);
+        enc.cv.wait(l, [&] { return enc.closed || !enc.q.empty(); });
+        if (enc.q.empty()) return;
+        it = std::move(enc.q.front());
+        enc.q.pop_front();
+      }
+      try {
+        const std::vector<uint8_t> png = encode_png_rgb8(it.rgb.data(), it.h, it.w, kBatchPngLevel);
+        FILE* f = fopen(out_paths[it.img], "wb");
+        if (!f) throw Error(std::string(out_paths[it.img]) + ": " + strerror(errno), MX_E_IO);
+        const bool ok = fwrite(png.data(), 1, png.size(), f) == png.size();
+        if (fclose(f) != 0 || !ok) throw Error(std::string(out_paths[it.img]) + ": write failed", MX_E_IO);
+        status[size_t(it.img)] = MX_OK;
+      } catch (const Error& e) {
+        status[size_t(it.img)] = e.code, why[size_t(it.img)] = e.what();
+      } catch (const std::exception& e) {
+        status[size_t(it.img)] = MX_E_IO, why[size_t(it.img)] = e.what();
+      }
+    }
+  });
+  struct InFlight {
+    size_t j;  // index into list
+    int k;     // slot
+    int64_t h, w;
+  };
+  std::deque<InFlight> fl;
+  int free_slots[2] = {1, 1};
+  auto collect = [&]() -> bool {  // finish the oldest image in flight
+    const InFlight f = fl.front();
+    int r = guard([&] { MX_CUDA(cudaEventSynchronize(w->done[f.k])); });
+    if (r == MX_OK) r = mx_gpu_poll(w->g);
+    if (r != MX_OK) {
+      *rc = r, *msg = last_message();
+      return false;
+    }
+    PngItem it;
+    it.img = list[f.j], it.h = f.h, it.w = f.w;
+    it.rgb.assign(slots.out[f.k], slots.out[f.k] + size_t(f.h * f.w * 3));
+    {
+      std::lock_guard<std::mutex> l(enc.mu);
+      enc.q.push_back(std::move(it));
+    }
+    enc.cv.notify_one();
+    free_slots[f.k] = 1;
+    fl.pop_front();
+    return true;
+  };
+  bool failed = false;
+  size_t j = 0;
+  for (; j < list.size() && !failed; ++j) {
+    const int32_t img = list[j];
+    if (fl.size() == 2 && !collect()) {
+      failed = true;
+      break;
+    }
+    // Read and decode on this thread, while the GPU runs what is in flight.
+    Rgb8 px;
+    try {
+      FILE* f = fopen(in_paths[img], "rb");
+      if (!f) throw Error(std::string(in_paths[img]) + ": " + strerror(errno), MX_E_IO);
+      std::vector<uint8_t> bytes;
+      uint8_t buf[1 << 16];
+      size_t got;
+      while ((got = fread(buf, 1, sizeof(buf), f)) > 0) bytes.insert(bytes.end(), buf, buf + got);
+      fclose(f);
+      px = decode_png_rgb8(bytes.data(), bytes.size(), in_paths[img]);
+      if (size_t(px.h * px.w * 3) > cap) throw Error(std::string(in_paths[img]) + ": larger than the batch's plan");
+    } catch (const Error& e) {
+      status[size_t(img)] = e.code, why[size_t(img)] = e.what();
+      continue;
+    }
+    int k = free_slots[0] ? 0 : 1;
+    memcpy(slots.in[k], px.data.data(), px.data.size());
+    int r = mx_gpu_upload_rgb8(w->g, slots.in[k], int32_t(px.h), int32_t(px.w), factor);
+    if (r != MX_OK) {
+      // The image's own problem (too small, pads to another shape): it fails
+      // alone, nothing was enqueued for it.
+      status[size_t(img)] = r, why[size_t(img)] = last_message();
+      continue;
+    }
+    r = mx_gpu_enqueue(w->g);
+    if (r == MX_OK) r = mx_gpu_download_rgb8(w->g, slots.out[k]);
+    if (r == MX_OK) r = guard([&] { MX_CUDA(cudaEventRecord(w->done[k], stream)); });
+    if (r != MX_OK) {
+      *rc = r, *msg = last_message();
+      failed = true;
+      break;
+    }
+    free_slots[k] = 0;
+    fl.push_back({j, k, px.h, px.w});
+  }
+  while (!failed && !fl.empty())
+    if (!collect()) failed = true;
+  // After a device failure the first image not dealt with is the oldest one
+  // still in flight, or else the one this thread was on.
+  const size_t dealt = !failed ? list.size() : !fl.empty() ? fl.front().j : j;
+  {
+    std::lock_guard<std::mutex> l(enc.mu);
+    enc.closed = true;
+  }
+  enc.cv.notify_all();
+  for (auto& t : enc.th) t.join();
+  return dealt;
 }
 
 }  // namespace
@@ -311,6 +501,67 @@ int mx_batch_run(mx_batch* b, int32_t n_images, const float* const* inputs, floa
             std::lock_guard<std::mutex> l(mu);
             left.insert(left.end(), share[r].begin() + long(j), share[r].end());
           }
+        });
+      }
+      for (auto& t : th) t.join();
+      std::sort(left.begin(), left.end());
+      todo.swap(left);
+    }
+    int failed = 0, first = -1;
+    for (int32_t i = 0; i < n_images; ++i) {
+      if (image_status) image_status[i] = status[size_t(i)];
+      if (status[size_t(i)] != MX_OK) {
+        ++failed;
+        if (first < 0) first = i;
+      }
+    }
+    if (failed)
+      throw Error(fmt("%d of %d images were not restored; image %d: %s", failed, n_images, first,
+                      why[size_t(first)].c_str()),
+                  status[size_t(first)]);
+  });
+}
+
+int mx_batch_run_png(mx_batch* b, int32_t n_images, const char* const* in_paths, const char* const* out_paths,
+                     int32_t factor, int32_t* image_status) {
+  return guard([&] {
+    if (!b || n_images < 0 || (n_images > 0 && (!in_paths || !out_paths)) || factor <= 0)
+      throw Error("mx_batch_run_png: bad argument");
+    if (b->ex.run != gpu_run) throw Error("mx_batch_run_png: needs the built-in GPU executor");
+    for (auto& w : b->workers) w.images_done = 0, w.seconds = 0.0;
+    std::vector<int32_t> status(size_t(n_images), MX_E_INVALID);
+    std::vector<std::string> why(size_t(n_images), "no device was left to restore it");
+    std::vector<int32_t> todo(static_cast<size_t>(n_images));
+    for (int32_t i = 0; i < n_images; ++i) todo[size_t(i)] = i;
+    while (!todo.empty()) {
+      std::vector<size_t> ready;
+      for (size_t k = 0; k < b->workers.size(); ++k)
+        if (b->workers[k].state == MX_WORKER_READY) ready.push_back(k);
+      if (ready.empty()) break;
+      std::vector<std::vector<int32_t>> share(ready.size());
+      for (size_t j = 0; j < todo.size(); ++j) share[j % ready.size()].push_back(todo[j]);
+      std::mutex mu;
+      std::vector<int32_t> left;
+      std::vector<std::thread> th;
+      for (size_t r = 0; r < ready.size(); ++r) {
+        th.emplace_back([&, r] {
+          const size_t k = ready[r];
+          mx_batch_worker& w = b->workers[k];
+          const auto t0 = std::chrono::steady_clock::now();
+          int rc = MX_OK;
+          std::string msg;
+          const size_t j = png_run_list(static_cast<GpuWorker*>(b->handles[k]), share[r], in_paths, out_paths,
+                                        factor, encoder_threads(ready.size()), status, why, &rc, &msg);
+          for (size_t q = 0; q < j; ++q) w.images_done += status[size_t(share[r][q])] == MX_OK;
+          if (j < share[r].size()) {
+            const int32_t img = share[r][j];
+            status[size_t(img)] = rc;
+            why[size_t(img)] = fmt("device %d: %s", w.device, msg.c_str());
+            set_worker_error(w, rc, fmt("device %d failed on image %d: %s", w.device, img, msg.c_str()));
+            std::lock_guard<std::mutex> l(mu);
+            left.insert(left.end(), share[r].begin() + long(j), share[r].end());
+          }
+          w.seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
         });
       }
       for (auto& t : th) t.join();

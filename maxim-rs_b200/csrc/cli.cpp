@@ -71,11 +71,13 @@ std::vector<uint8_t> read_all(FILE* f) {
   return v;
 }
 
-// `--batch`: every PNG of a directory, grouped by padded shape (one plan
-// per shape), each group through the batch runner over the chosen devices.
-// A file that cannot be read or padded is reported and skipped; an image the
-// runner could not restore is reported; the others are written. Exit status
-// 1 if anything failed.
+// `--batch`: every PNG of a directory, grouped by padded shape (one plan per
+// shape, the shape read from each PNG's header), each group through the batch
+// runner's PNG path over the chosen devices: the workers decode and encode
+// the PNGs while the GPUs run, and pad, crop and round on the device. A file
+// whose header cannot be read or that is too small to pad is reported and
+// skipped; an image the runner could not restore is reported; the others are
+// written. Exit status 1 if anything failed.
 int run_batch(mx_weights* w, const std::string& in_dir, const std::string& out_dir, std::vector<int32_t> devices,
               int factor, bool quiet) {
   std::vector<std::string> names;
@@ -95,24 +97,23 @@ int run_batch(mx_weights* w, const std::string& in_dir, const std::string& out_d
     if (mx_device_count(&n) != MX_OK || n == 0) return fail("cuda");
     for (int i = 0; i < n; ++i) devices.push_back(i);
   }
-  struct Item {
-    std::string name;
-    mx_image img{}, padded{};
-    int32_t eh = 0, ew = 0;
-  };
-  std::map<std::pair<int32_t, int32_t>, std::vector<Item>> groups;
+  std::map<std::pair<int32_t, int32_t>, std::vector<std::string>> groups;
   int failed = 0, written = 0;
   for (const auto& n : names) {
-    Item it;
-    it.name = n;
-    if (mx_png_read((in_dir + "/" + n).c_str(), &it.img) != MX_OK ||
-        mx_preprocess(&it.img, factor, &it.padded, &it.eh, &it.ew) != MX_OK) {
+    const std::string path = in_dir + "/" + n;
+    uint8_t head[64];
+    size_t got = 0;
+    if (FILE* f = fopen(path.c_str(), "rb")) {
+      got = fread(head, 1, sizeof(head), f);
+      fclose(f);
+    }
+    int32_t h = 0, wd = 0, ph = 0, pw = 0;
+    if (mx_png_size_mem(head, got, &h, &wd) != MX_OK || mx_pad_geometry(h, wd, factor, &ph, &pw, nullptr, nullptr) != MX_OK) {
       fprintf(stderr, "maxim: %s: %s (skipped)\n", n.c_str(), last_error().c_str());
-      mx_image_free(&it.img);
       ++failed;
       continue;
     }
-    groups[{it.padded.h, it.padded.w}].push_back(it);
+    groups[{ph, pw}].push_back(n);
   }
   for (auto& kv : groups) {
     auto& items = kv.second;
@@ -132,15 +133,13 @@ int run_batch(mx_weights* w, const std::string& in_dir, const std::string& out_d
       mx_plan_free(plan);
       continue;
     }
-    const mx_buf& ob = pv->bufs[pv->output];
-    const size_t n_out = size_t(ob.c * ob.h * ob.w);
-    std::vector<std::vector<float>> outs(items.size(), std::vector<float>(n_out));
-    std::vector<const float*> ins;
-    std::vector<float*> outp;
-    for (size_t i = 0; i < items.size(); ++i) ins.push_back(items[i].padded.data), outp.push_back(outs[i].data());
+    std::vector<std::string> ins, outs;
+    for (const auto& n : items) ins.push_back(in_dir + "/" + n), outs.push_back(out_dir + "/" + n);
+    std::vector<const char*> ip, op;
+    for (size_t i = 0; i < items.size(); ++i) ip.push_back(ins[i].c_str()), op.push_back(outs[i].c_str());
     std::vector<int32_t> st(items.size(), 0);
     auto t1 = std::chrono::steady_clock::now();
-    const int rc = mx_batch_run(b, int32_t(items.size()), ins.data(), outp.data(), st.data());
+    const int rc = mx_batch_run_png(b, int32_t(items.size()), ip.data(), op.data(), factor, st.data());
     auto t2 = std::chrono::steady_clock::now();
     if (rc != MX_OK) fprintf(stderr, "maxim: %s\n", last_error().c_str());
     std::vector<mx_batch_worker> ws(size_t(mx_batch_worker_count(b)));
@@ -154,24 +153,12 @@ int run_batch(mx_weights* w, const std::string& in_dir, const std::string& out_d
                 x.state == MX_WORKER_READY ? "ready" : "failed", x.images_done, x.error[0] ? " - " : "", x.error);
     }
     for (size_t i = 0; i < items.size(); ++i) {
-      Item& it = items[i];
       if (st[i] != MX_OK) {
-        fprintf(stderr, "maxim: %s: not restored (status %d)\n", it.name.c_str(), st[i]);
+        fprintf(stderr, "maxim: %s: not restored (status %d)\n", items[i].c_str(), st[i]);
         ++failed;
       } else {
-        mx_image pred{3, int32_t(it.padded.h), int32_t(it.padded.w), outs[i].data()};
-        mx_image cropped{};
-        if (mx_crop_out(&pred, it.img.h, it.img.w, it.eh, it.ew, &cropped) != MX_OK ||
-            mx_png_write((out_dir + "/" + it.name).c_str(), &cropped) != MX_OK) {
-          fprintf(stderr, "maxim: %s: %s\n", it.name.c_str(), last_error().c_str());
-          ++failed;
-        } else {
-          ++written;
-        }
-        mx_image_free(&cropped);
+        ++written;
       }
-      mx_image_free(&it.padded);
-      mx_image_free(&it.img);
     }
     mx_batch_free(b);
     mx_plan_free(plan);

@@ -219,7 +219,7 @@ std::vector<uint8_t> encode_png(const Image& img) {
   return encode_png_rgb8(rgb.data(), H, W);
 }
 
-std::vector<uint8_t> encode_png_rgb8(const uint8_t* rgb, int64_t H, int64_t W) {
+std::vector<uint8_t> encode_png_rgb8(const uint8_t* rgb, int64_t H, int64_t W, int level) {
   if (H <= 0 || W <= 0) throw Error("write_png: empty image");
   std::vector<uint8_t> raw(size_t(H * (W * 3 + 1)));
   for (int64_t y = 0; y < H; ++y) {
@@ -229,7 +229,8 @@ std::vector<uint8_t> encode_png_rgb8(const uint8_t* rgb, int64_t H, int64_t W) {
   }
   uLongf zlen = compressBound(uLong(raw.size()));
   std::vector<uint8_t> z(zlen);
-  if (compress2(z.data(), &zlen, raw.data(), uLong(raw.size()), 6) != Z_OK) throw Error("PNG compression failed");
+  if (compress2(z.data(), &zlen, raw.data(), uLong(raw.size()), level) != Z_OK)
+    throw Error("PNG compression failed");
   z.resize(zlen);
   std::vector<uint8_t> out = {137, 80, 78, 71, 13, 10, 26, 10};
   auto chunk = [&](const char* type, const std::vector<uint8_t>& data) {

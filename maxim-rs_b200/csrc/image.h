@@ -30,8 +30,9 @@ std::pair<int64_t, int64_t> png_size(const uint8_t* bytes, size_t n, const std::
 Image read_png(const std::string& path);
 // RGB 8-bit, clamp then round half up (src/image.rs:82-104).
 std::vector<uint8_t> encode_png(const Image& img);
-// An RGB 8-bit PNG from interleaved h x w x 3 samples, as they are.
-std::vector<uint8_t> encode_png_rgb8(const uint8_t* rgb, int64_t h, int64_t w);
+// An RGB 8-bit PNG from interleaved h x w x 3 samples, as they are; `level`
+// is zlib's compression level (the pixels do not depend on it).
+std::vector<uint8_t> encode_png_rgb8(const uint8_t* rgb, int64_t h, int64_t w, int level = 6);
 void write_png(const std::string& path, const Image& img);
 
 // Flax SAME padding for one axis (src/image.rs:108-112).
