@@ -171,10 +171,23 @@ struct PngItem {
 
 struct Encoder {
   std::mutex mu;
-  std::condition_variable cv;
+  std::condition_variable cv;       // an item was queued, or the queue was closed
+  std::condition_variable room;     // an item was taken off the queue
   std::deque<PngItem> q;
+  size_t limit = 4;                 // queued images a worker may run ahead of its encoders
   bool closed = false;
   std::vector<std::thread> th;
+  // Closing drains the queue: the encoders finish what is queued, then exit.
+  void close_and_join() {
+    {
+      std::lock_guard<std::mutex> l(mu);
+      closed = true;
+    }
+    cv.notify_all();
+    for (auto& t : th)
+      if (t.joinable()) t.join();
+  }
+  ~Encoder() { close_and_join(); }
 };
 
 // zlib level of the batch's PNG writer. Deflate's cost depends on the data:
@@ -231,6 +244,7 @@ size_t png_run_list(GpuWorker* w, const std::vector<int32_t>& list, const char* 
     return 0;
   }
   Encoder enc;
+  enc.limit = size_t(2 * n_encoders);
   for (int t = 0; t < n_encoders; ++t) enc.th.emplace_back([&] {
     for (;;) {
       PngItem it;
@@ -241,6 +255,7 @@ size_t png_run_list(GpuWorker* w, const std::vector<int32_t>& list, const char* 
         it = std::move(enc.q.front());
         enc.q.pop_front();
       }
+      enc.room.notify_one();
       try {
         const std::vector<uint8_t> png = encode_png_rgb8(it.rgb.data(), it.h, it.w, kBatchPngLevel);
         FILE* f = fopen(out_paths[it.img], "wb");
@@ -274,7 +289,10 @@ size_t png_run_list(GpuWorker* w, const std::vector<int32_t>& list, const char* 
     it.img = list[f.j], it.h = f.h, it.w = f.w;
     it.rgb.assign(slots.out[f.k], slots.out[f.k] + size_t(f.h * f.w * 3));
     {
-      std::lock_guard<std::mutex> l(enc.mu);
+      // Hold the GPU back rather than queue without bound when the encoders
+      // fall behind.
+      std::unique_lock<std::mutex> l(enc.mu);
+      enc.room.wait(l, [&] { return enc.q.size() < enc.limit; });
       enc.q.push_back(std::move(it));
     }
     enc.cv.notify_one();
@@ -305,6 +323,9 @@ size_t png_run_list(GpuWorker* w, const std::vector<int32_t>& list, const char* 
     } catch (const Error& e) {
       status[size_t(img)] = e.code, why[size_t(img)] = e.what();
       continue;
+    } catch (const std::exception& e) {
+      status[size_t(img)] = MX_E_IO, why[size_t(img)] = std::string(in_paths[img]) + ": " + e.what();
+      continue;
     }
     int k = free_slots[0] ? 0 : 1;
     memcpy(slots.in[k], px.data.data(), px.data.size());
@@ -331,12 +352,7 @@ size_t png_run_list(GpuWorker* w, const std::vector<int32_t>& list, const char* 
   // After a device failure the first image not dealt with is the oldest one
   // still in flight, or else the one this thread was on.
   const size_t dealt = !failed ? list.size() : !fl.empty() ? fl.front().j : j;
-  {
-    std::lock_guard<std::mutex> l(enc.mu);
-    enc.closed = true;
-  }
-  enc.cv.notify_all();
-  for (auto& t : enc.th) t.join();
+  enc.close_and_join();
   return dealt;
 }
 
@@ -550,8 +566,13 @@ int mx_batch_run_png(mx_batch* b, int32_t n_images, const char* const* in_paths,
           const auto t0 = std::chrono::steady_clock::now();
           int rc = MX_OK;
           std::string msg;
-          const size_t j = png_run_list(static_cast<GpuWorker*>(b->handles[k]), share[r], in_paths, out_paths,
-                                        factor, encoder_threads(ready.size()), status, why, &rc, &msg);
+          size_t j = 0;
+          try {
+            j = png_run_list(static_cast<GpuWorker*>(b->handles[k]), share[r], in_paths, out_paths, factor,
+                             encoder_threads(ready.size()), status, why, &rc, &msg);
+          } catch (const std::exception& e) {  // host resources (threads, memory): the worker stops here
+            j = 0, rc = MX_E_INVALID, msg = e.what();
+          }
           for (size_t q = 0; q < j; ++q) w.images_done += status[size_t(share[r][q])] == MX_OK;
           if (j < share[r].size()) {
             const int32_t img = share[r][j];
