@@ -218,7 +218,10 @@ int mx_gpu_download_output_device(mx_gpu* g, float* dev_output);
  * to reflect) are refused with the same message.
  * upload_rgb8 / download_rgb8 are the two halves (asynchronous on the
  * handle's stream, around mx_gpu_enqueue; download crops with the geometry
- * of the image last uploaded); run_rgb8 does all of it and waits. */
+ * of the image last uploaded); run_rgb8 does all of it and waits. As with
+ * cudaMemcpyAsync, a pinned (page-locked) host buffer given to either half
+ * must stay untouched until mx_gpu_sync; a pageable one may be reused when
+ * the call returns. The staging is not part of mx_gpu_new's memory budget. */
 int mx_gpu_upload_rgb8(mx_gpu* g, const uint8_t* rgb, int32_t h, int32_t w, int32_t factor);
 int mx_gpu_download_rgb8(mx_gpu* g, uint8_t* out_rgb);
 int mx_gpu_run_rgb8(mx_gpu* g, const uint8_t* rgb, int32_t h, int32_t w, int32_t factor, uint8_t* out_rgb);

@@ -121,3 +121,14 @@ def test_input_size_is_checked(mx):
     b = mx.Batch(devices=(0,), executor=Fake())
     with pytest.raises(ValueError):
         b.run([np.zeros(N_IN + 1, np.float32)])
+
+
+def test_png_mode_needs_the_gpu_executor(mx, tmp_path):
+    """mx_batch_run_png runs over the device-side image path, which a
+    caller-supplied executor does not have: refused, nothing run."""
+    ex = Fake()
+    b = mx.Batch(devices=(0,), executor=ex)
+    with pytest.raises(mx.MaximError, match="built-in GPU executor"):
+        b.run_png([str(tmp_path / "a.png")], [str(tmp_path / "b.png")])
+    assert ex.log == []
+    b.close()
