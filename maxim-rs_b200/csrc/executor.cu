@@ -30,6 +30,8 @@
 #include <functional>
 #include <map>
 #include <memory>
+#include <mutex>
+#include <set>
 #include <string>
 #include <utility>
 #include <vector>
@@ -203,8 +205,12 @@ void split_tf32(const std::vector<float>& w, std::vector<float>& hi, std::vector
   }
 }
 
+// The driver's tensor-map encoder, looked up once per process (batch
+// workers build executors on several threads at once).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::mutex mu;
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::lock_guard<std::mutex> l(mu);
   if (!fn) {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -461,9 +467,17 @@ bool umma_gate_spatial_ok(const mx_gpu& g, const Layout& L, const mx_op& gate, c
   X(32, 0) X(64, 0) X(128, 0) X(32, 1) X(64, 1) X(128, 1) X(32, 2) X(64, 2) X(128, 2) X(32, 3) X(64, 3) \
   X(128, 3) X(32, 4) X(64, 4) X(128, 4) X(32, 5) X(64, 5) X(128, 5) X(128, 6) X(32, 7) X(64, 7)
 
+// The tensor-core kernels' shared-memory opt-in. A function attribute is
+// per device, so it is set once for each device an executor is built on
+// (the current one), under a lock: batch workers build executors for
+// several devices on several threads at once.
 void umma_attrs_once() {
-  static bool done = false;
-  if (done) return;
+  static std::mutex mu;
+  static std::set<int> done;
+  int dev = -1;
+  MX_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> l(mu);
+  if (done.count(dev)) return;
 #define MX_UMMA_ATTR(NN, MM)                                                                              \
   MX_CUDA(cudaFuncSetAttribute(umma_conv_kernel<NN, MM, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                UmmaCfg<NN, MM>::SMEM_BYTES));                                                \
@@ -473,7 +487,7 @@ void umma_attrs_once() {
 #undef MX_UMMA_ATTR
   MX_CUDA(cudaFuncSetAttribute(umma_conv3f_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                Conv3fCfg::SMEM_BYTES));
-  done = true;
+  done.insert(dev);
 }
 int umma_smem(int n, int mode) {
 #define MX_UMMA_SMEM(NN, MM) \

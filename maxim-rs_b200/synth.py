@@ -65,7 +65,10 @@ def write_safetensors(path, params, variant, task="synthetic"):
         off += a.nbytes
     blob = json.dumps(header, separators=(",", ":"), sort_keys=True).encode()
     blob += b" " * ((-(8 + len(blob))) % 8)
-    tmp = str(path) + ".tmp"
+    # A temporary of this process's own, renamed into place: processes that
+    # write the same checkpoint at once (ranks on one box) each rename a
+    # complete file, and the last rename wins with identical bytes.
+    tmp = "%s.tmp%d" % (path, os.getpid())
     with open(tmp, "wb") as f:
         f.write(len(blob).to_bytes(8, "little"))
         f.write(blob)
